@@ -1,0 +1,5 @@
+// libkdb200.cu — the single translation unit of libkdb200.so.  Every kernel source is included here
+// so that the device status word (kdb::g_status) is one symbol without relocatable device code.
+#include "host_util.cu"
+#include "proj.cu"
+#include "capi.cu"

@@ -1,0 +1,162 @@
+// proj.cu — the bf16 dense projection Y[M, N] = X[M, K] · W[N, K]ᵀ (fp32 accumulate, bf16 out).
+//
+// Replaces the computation behind the `muse_bf16_proj` problem's kernel_fn(data, state)
+// (kdev: src/kdev/adapters/okc.py:534-537, config src/kdev/adapters/okc_problems/muse_bf16_proj.toml).
+// One persistent tcgen05 kernel (gemm_sm100.cuh); the tile width BN is picked per shape so that
+// small-M, weight-streaming shapes still put a tile on every SM.
+#include "gemm_sm100.cuh"
+#include "host_util.h"
+#include "proj.h"
+
+namespace kdb {
+
+struct ProjTile {
+  int a_row, b_row, nkb;
+  int m0, n0;
+};
+
+template <int BM, int BN>
+struct ProjSched {
+  struct Params {
+    int M, N, K;
+    int num_m, num_n, group_m;
+  };
+  Params p;
+  __device__ explicit ProjSched(const Params& pp) : p(pp) {}
+  __device__ int num_tiles() const { return p.num_m * p.num_n; }
+  // Grouped raster: group_m consecutive M-blocks sweep the N-blocks together, so the tiles in
+  // flight at once share both their X rows and their W rows in L2.
+  __device__ ProjTile tile(int t) const {
+    const int width = p.group_m * p.num_n;
+    const int g = t / width;
+    const int first_m = g * p.group_m;
+    const int gsz = min(p.num_m - first_m, p.group_m);
+    const int r = t - g * width;
+    const int mb = first_m + r % gsz;
+    const int nb = r / gsz;
+    ProjTile ti;
+    ti.m0 = mb * BM;
+    ti.n0 = nb * BN;
+    ti.a_row = ti.m0;
+    ti.b_row = ti.n0;
+    ti.nkb = (p.K + kBK - 1) / kBK;
+    return ti;
+  }
+};
+
+template <int BN>
+struct ProjEpi {
+  struct Params {
+    __nv_bfloat16* y;
+    long long ldy;
+    int M, N;
+    int vec_ok;   // y 16-byte aligned and ldy % 8 == 0
+  };
+  __device__ static void run(const Params& p, const ProjTile& ti, int r, uint32_t taddr) {
+    const int row = ti.m0 + r;
+    const bool row_ok = row < p.M;
+    __nv_bfloat16* yrow = p.y + static_cast<long long>(row) * p.ldy;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, v);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+      const int col0 = ti.n0 + c * 32;
+      if (col0 >= p.N) continue;
+      if (p.vec_ok && col0 + 32 <= p.N) {
+        uint4* dst = reinterpret_cast<uint4*>(yrow + col0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 o;
+          o.x = pack_bf16x2(__uint_as_float(v[q * 8 + 0]), __uint_as_float(v[q * 8 + 1]));
+          o.y = pack_bf16x2(__uint_as_float(v[q * 8 + 2]), __uint_as_float(v[q * 8 + 3]));
+          o.z = pack_bf16x2(__uint_as_float(v[q * 8 + 4]), __uint_as_float(v[q * 8 + 5]));
+          o.w = pack_bf16x2(__uint_as_float(v[q * 8 + 6]), __uint_as_float(v[q * 8 + 7]));
+          dst[q] = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < p.N) yrow[col0 + j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+      }
+    }
+  }
+};
+
+template <int BN, int STAGES>
+static int launch_proj_cfg(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
+                           cudaStream_t stream) {
+  constexpr int BM = 128;
+  using L = GemmLayout<BM, BN, STAGES>;
+  using Sched = ProjSched<BM, BN>;
+  using Epi = ProjEpi<BN>;
+  auto kern = gemm_tn_kernel<Sched, Epi, BM, BN, STAGES>;
+
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_done[dev] = true;
+  }
+
+  CUtensorMap ta, tb;
+  int rc = make_tmap_bf16_2d(&ta, x, K, M, K, kBK, BM);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tb, w, K, N, K, kBK, BN);
+  if (rc) return rc;
+
+  typename Sched::Params sp;
+  sp.M = M;
+  sp.N = N;
+  sp.K = K;
+  sp.num_m = (M + BM - 1) / BM;
+  sp.num_n = (N + BN - 1) / BN;
+  sp.group_m = 16;
+  typename Epi::Params ep;
+  ep.y = static_cast<__nv_bfloat16*>(y);
+  ep.ldy = ldy;
+  ep.M = M;
+  ep.N = N;
+  ep.vec_ok = aligned16(y) && (ldy % 8 == 0);
+
+  const int tiles = sp.num_m * sp.num_n;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kGemmThreads, L::kSmemBytes, stream>>>(ta, tb, sp, ep);
+  return cuda_status(cudaGetLastError());
+}
+
+int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
+              int force_bn, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return KDB_OK;
+  if (!x || !w || !y) return KDB_ERR_INVALID_ARG;
+  if (ldy < N) return KDB_ERR_INVALID_ARG;
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return KDB_ERR_UNSUPPORTED;
+  if (K == 0) {
+    return cuda_status(cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(N) * 2,
+                                         static_cast<size_t>(M), stream));
+  }
+  // TMA: 16-byte aligned base and row stride.
+  if (K % 8 != 0 || !aligned16(x) || !aligned16(w)) return KDB_ERR_INVALID_ARG;
+
+  int bn = force_bn;
+  if (bn == 0) {
+    // Widest tile that still gives every SM a tile; narrower tiles for weight-streaming shapes.
+    const long long sms = num_sms();
+    const long long mb = (M + 127) / 128;
+    if (mb * ((N + 255) / 256) >= sms) bn = 256;
+    else if (mb * ((N + 127) / 128) >= sms) bn = 128;
+    else bn = 64;
+  }
+  switch (bn) {
+    case 256: return launch_proj_cfg<256, 4>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+    case 128: return launch_proj_cfg<128, 6>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+    case 64: return launch_proj_cfg<64, 8>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+    default: return KDB_ERR_INVALID_ARG;
+  }
+}
+
+}  // namespace kdb

@@ -1,0 +1,9 @@
+// proj.h — internal launcher of the bf16 projection (the C-ABI wrapper lives in capi.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace kdb {
+// Y[M, N] (row stride ldy) = X[M, K] · W[N, K]ᵀ.  force_bn: 0 = pick per shape, else 64/128/256.
+int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
+              int force_bn, cudaStream_t stream);
+}  // namespace kdb

@@ -1,0 +1,54 @@
+"""bf16 dense projection Y = X · Wᵀ as a PyTorch custom op over libkdb200.
+
+Forward signature follows the reference's `muse_bf16_proj` problem: kdev calls
+`kernel_fn(data, state)` with data = {"x": bf16[M, K], "config": {...}} and state = prepare(weights)
+(src/kdev/adapters/okc.py:501-537).  `proj(x, w)` is the op behind that kernel_fn.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _check_operand(name: str, t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path), got {t.device}")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if t.stride(1) != 1 or t.stride(0) != t.shape[1]:
+        raise ValueError(f"{name} must be row-major contiguous")
+
+
+def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0) -> torch.Tensor:
+    """Writes X · Wᵀ into `y` ([M, N] bf16; a column slice of a wider row-major matrix is allowed)."""
+    _check_operand("x", x)
+    _check_operand("w", w)
+    m, k = x.shape
+    n, k2 = w.shape
+    if k != k2:
+        raise ValueError(f"x is [{m}, {k}] but w is [{n}, {k2}]: K mismatch")
+    if y.dtype != torch.bfloat16 or y.dim() != 2 or tuple(y.shape) != (m, n) or y.stride(1) != 1:
+        raise ValueError(f"y must be bf16 [{m}, {n}] with unit column stride")
+    if not (x.device == w.device == y.device):
+        raise ValueError("x, w and y must be on the same device")
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().kdb_proj_bf16_cfg(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, y.stride(0),
+                                          int(tile_n), stream)
+    _lib.check("kdb_proj_bf16", rc)
+    return y
+
+
+@torch.library.custom_op("kdb200::proj", mutates_args=())
+def proj(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Y[M, N] = X[M, K] · W[N, K]ᵀ, bf16 in/out, fp32 accumulation (tcgen05 on sm_100a)."""
+    y = torch.empty((x.shape[0], w.shape[0]), dtype=torch.bfloat16, device=x.device)
+    return proj_into(x, w, y)
+
+
+@proj.register_fake
+def _proj_fake(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return x.new_empty((x.shape[0], w.shape[0]))
