@@ -67,6 +67,68 @@ int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, i
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                       int tile_n, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- */
+/* Fused MoE layer                                                                                 */
+/* ---------------------------------------------------------------------------------------------- */
+/*
+ * Layer:  logits = x · Wrᵀ (+ bias) (fp32);  ids = top-k(logits);  w = renormalised softmax over the
+ * k picks;  y[t] = Σ_j w[t,j] · down_e( bf16( silu(x[t]·Wg_eᵀ) * (x[t]·Wu_eᵀ) ) ) (+ shared expert)
+ * with e = ids[t,j].  Replaces the body of kernel_fn(data, state) for the reference's fused MoE
+ * problem (`muse_moe_w4a16`: src/kdev/adapters/okc_problems/muse_moe_w4a16.toml; reference engines
+ * okc-challenge/engines/sc_h.cu:189, x3_h.cu:311, x7_h.cu:310), for the bf16 SwiGLU layer with an
+ * fp32 router inside the layer.
+ *
+ * Shapes: t tokens, h hidden (h % 8 == 0), e experts (k <= e <= 1024), i intermediate
+ * (i % 128 == 0), k top-k (k <= 32), shared in {0, 1} always-on experts of intermediate shared_i
+ * (shared_i % 128 == 0).  Weights: router fp32 [e, h], optional router_bias fp32 [e],
+ * w_gate_up bf16 [e, 2i, h] (gate rows then up rows per expert) packed once with
+ * kdb_moe_pack_gate_up, w_down bf16 [e, h, i], shared_* likewise with e = 1.
+ */
+
+/* Workspace bytes kdb_moe_forward needs for this shape (0 if the shape is unsupported). */
+size_t kdb_moe_workspace_bytes(int64_t t, int64_t h, int64_t e, int64_t i, int64_t k, int64_t shared,
+                               int64_t shared_i);
+
+/*
+ * One-time weight re-layout (the problem's `prepare(weights)`, okc.py:501-515): packed[e] holds, for
+ * every 128-wide block b of the intermediate dimension, the 128 gate rows of block b followed by the
+ * 128 up rows of block b, so one 256-wide GEMM tile carries matching gate and up columns.  Lossless
+ * (a row permutation).  w_gate_up and packed: bf16 [e, 2i, h], distinct buffers.
+ */
+int kdb_moe_pack_gate_up(const void* w_gate_up, void* packed, int64_t e, int64_t i, int64_t h, void* stream);
+
+/*
+ * Router stage alone: logits fp32 [t, e] (each the fixed-order fp64 dot product rounded once to
+ * fp32, plus bias), topk_ids int32 [t, k] (descending logit; ties -> lower expert), topk_w fp32
+ * [t, k] renormalised softmax weights.  Routing plan counterpart: x3_h.cu:346-385.
+ */
+int kdb_moe_route(const void* x, const float* router_w, const float* router_bias, float* logits, float* topk_w,
+                  int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t k, void* stream);
+
+/* Scratch bytes of kdb_moe_plan. */
+size_t kdb_moe_plan_workspace_bytes(int64_t t, int64_t e, int64_t k);
+
+/*
+ * Permutation plan alone: counts int32 [e], offsets int32 [e + 1] (exclusive scan), perm_slot int32
+ * [t*k] (slot t*k + j held by each permuted row; rows grouped by expert, tokens ascending within an
+ * expert), slot_pos int32 [t*k] (inverse).  Counterpart of the per-expert mask/popc/scan plan of
+ * x3_h.cu:346-385, for any t.
+ */
+int kdb_moe_plan(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_t e, int64_t k, int32_t* counts,
+                 int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/*
+ * The whole layer.  x bf16 [t, h]; y bf16 [t, h]; topk_w fp32 [t, k]; topk_ids int32 [t, k] (the
+ * routing outputs the reference's routing problems report at output index 2,
+ * src/kdev/adapters/okc_problems/muse_prefill_layer.toml:148).  workspace: >= kdb_moe_workspace_bytes,
+ * 256-byte aligned.  shared_gate_up_packed / shared_down may be NULL when shared == 0.
+ */
+int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+                    const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
+                    float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,
+                    int64_t shared, int64_t shared_i, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 #include "../../include/kdb200.h"
 #include "kdb_status.h"
 #include "host_util.h"
+#include "moe.h"
 #include "proj.h"
 #include "sm100_common.cuh"
 
@@ -56,6 +57,61 @@ int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, i
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                       int tile_n, void* stream) {
   return kdb::proj_bf16(x, w, y, m, n, k, ldy, tile_n, static_cast<cudaStream_t>(stream));
+}
+
+static kdb::MoeShape moe_shape(int64_t t, int64_t h, int64_t e, int64_t i, int64_t k, int64_t shared,
+                               int64_t shared_i) {
+  kdb::MoeShape sh;
+  sh.t = t;
+  sh.h = h;
+  sh.e = e;
+  sh.i = i;
+  sh.k = k;
+  sh.shared = shared;
+  sh.shared_i = shared_i;
+  return sh;
+}
+
+size_t kdb_moe_workspace_bytes(int64_t t, int64_t h, int64_t e, int64_t i, int64_t k, int64_t shared,
+                               int64_t shared_i) {
+  return kdb::moe_workspace_bytes(moe_shape(t, h, e, i, k, shared, shared_i));
+}
+
+int kdb_moe_pack_gate_up(const void* w_gate_up, void* packed, int64_t e, int64_t i, int64_t h, void* stream) {
+  if (e < 0 || i <= 0 || h <= 0 || i % 128 != 0 || h % 8 != 0) return KDB_ERR_INVALID_ARG;
+  if (e * 2 * i > (1ll << 31)) return KDB_ERR_UNSUPPORTED;
+  if (!w_gate_up || !packed || w_gate_up == packed) return KDB_ERR_INVALID_ARG;
+  if (!kdb::aligned16(w_gate_up) || !kdb::aligned16(packed)) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_pack_gate_up(w_gate_up, packed, (int)e, (int)i, (int)h, static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_route(const void* x, const float* router_w, const float* router_bias, float* logits, float* topk_w,
+                  int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t k, void* stream) {
+  if (t < 0 || h <= 0 || e <= 0 || e > 1024 || k <= 0 || k > e || k > 32) return KDB_ERR_INVALID_ARG;
+  if (t * e > (1ll << 31) / 4 || t * h > (1ll << 40)) return KDB_ERR_UNSUPPORTED;
+  if (t == 0) return KDB_OK;
+  if (!x || !router_w || !logits || !topk_w || !topk_ids) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_route(x, router_w, router_bias, logits, topk_w, topk_ids, (int)t, (int)h, (int)e, (int)k,
+                        static_cast<cudaStream_t>(stream));
+}
+
+size_t kdb_moe_plan_workspace_bytes(int64_t t, int64_t e, int64_t k) { return kdb::moe_plan_scratch_bytes(t, e, k); }
+
+int kdb_moe_plan(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_t e, int64_t k, int32_t* counts,
+                 int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  if (t < 0 || t * k > (1ll << 30)) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_plan_only(topk_ids, topk_w, (int)t, (int)e, (int)k, counts, offsets, perm_slot, slot_pos,
+                            workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+                    const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
+                    float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,
+                    int64_t shared, int64_t shared_i, void* workspace, size_t workspace_bytes, void* stream) {
+  return kdb::moe_forward(x, router_w, router_bias, w_gate_up_packed, w_down, shared_gate_up_packed, shared_down, y,
+                          topk_w, topk_ids, moe_shape(t, h, e, i, k, shared, shared_i), workspace, workspace_bytes,
+                          static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

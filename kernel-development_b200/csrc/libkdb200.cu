@@ -2,4 +2,7 @@
 // so that the device status word (kdb::g_status) is one symbol without relocatable device code.
 #include "host_util.cu"
 #include "proj.cu"
+#include "moe_route.cu"
+#include "moe_gemm.cu"
+#include "moe.cu"
 #include "capi.cu"

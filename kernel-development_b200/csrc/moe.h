@@ -1,0 +1,45 @@
+// moe.h — internal launchers of the MoE layer (C-ABI wrappers in capi.cu).
+#pragma once
+#include <cstddef>
+#include <cuda_runtime.h>
+
+namespace kdb {
+
+int moe_route(const void* x, const float* wr, const float* bias, float* logits, float* topk_w, int* topk_ids,
+              int T, int H, int E, int k, cudaStream_t s);
+int moe_plan(const int* ids, const float* topk_w, int T, int E, int k, int* chunk_counts, int* chunk_base,
+             int* counts, int* offsets, int* mtile_start, int* perm_slot, int* slot_pos, int* perm_token,
+             float* perm_w, cudaStream_t s);
+int moe_gather_rows(const void* x, const int* perm_token, void* x_perm, int R, int H, int T, cudaStream_t s);
+int moe_combine(const void* yperm, const int* slot_pos, const void* yshared, void* y, int T, int H, int k,
+                cudaStream_t s);
+int moe_pack_gate_up(const void* w, void* packed, int E, int I, int H, cudaStream_t s);
+int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
+                     const int* mtile_start, void* out, cudaStream_t s);
+int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
+                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s);
+
+struct MoeShape {
+  long long t, h, e, i, k, shared, shared_i;
+};
+
+// Validates a layer shape; KDB_OK or an error code.
+int moe_check_shape(const MoeShape& sh);
+
+// Workspace bytes of moe_forward for a shape (0 on an invalid shape).
+size_t moe_workspace_bytes(const MoeShape& sh);
+
+// Scratch bytes of moe_plan_only (chunk counts/bases, m-tile prefix, row tokens, row weights).
+size_t moe_plan_scratch_bytes(long long t, long long e, long long k);
+
+// The routing plan alone (for composition and tests): counts[E], offsets[E + 1], perm_slot[T*k],
+// slot_pos[T*k] from topk ids/weights; scratch from `workspace`.
+int moe_plan_only(const int* ids, const float* topk_w, int T, int E, int k, int* counts, int* offsets,
+                  int* perm_slot, int* slot_pos, void* workspace, size_t workspace_bytes, cudaStream_t s);
+
+int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+                const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
+                float* topk_w, int* topk_ids, const MoeShape& sh, void* workspace, size_t workspace_bytes,
+                cudaStream_t s);
+
+}  // namespace kdb

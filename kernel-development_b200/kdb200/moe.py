@@ -1,0 +1,157 @@
+"""Fused MoE layer as PyTorch custom ops over libkdb200.
+
+Forward signature follows kdev's problem-adapter contract (src/kdev/adapters/okc.py:501-537):
+`prepare(weights) -> state` once (untimed; packs gate/up rows), then `kernel_fn(data, state)` with
+data = {"x": bf16[T, H], "config": {...}} returning (y bf16[T, H], topk_w fp32[T, k],
+topk_ids int32[T, k]) — routing ids at output index 2 as in the reference's routing problems
+(src/kdev/adapters/okc_problems/muse_prefill_layer.toml:148).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_vp = ctypes.c_void_p
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(name: str, t: torch.Tensor, dtype: torch.dtype, dim: int) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path), got {t.device}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.dim() != dim:
+        raise ValueError(f"{name} must be {dim}-D, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def pack_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
+    """[E, 2I, H] (gate rows then up rows) -> the packed layout the gate_up GEMM reads."""
+    _need("w_gate_up", w_gate_up, torch.bfloat16, 3)
+    e, two_i, h = w_gate_up.shape
+    out = torch.empty_like(w_gate_up)
+    with torch.cuda.device(w_gate_up.device):
+        rc = _lib.lib().kdb_moe_pack_gate_up(w_gate_up.data_ptr(), out.data_ptr(), e, two_i // 2, h,
+                                              _vp(_stream(w_gate_up.device)))
+    _lib.check("kdb_moe_pack_gate_up", rc)
+    return out
+
+
+def route(x: torch.Tensor, router: torch.Tensor, bias: Optional[torch.Tensor], k: int):
+    """(logits fp32 [T, E], topk_w fp32 [T, k], topk_ids int32 [T, k]) of the router stage."""
+    _need("x", x, torch.bfloat16, 2)
+    _need("router", router, torch.float32, 2)
+    t, h = x.shape
+    e = router.shape[0]
+    logits = torch.empty((t, e), dtype=torch.float32, device=x.device)
+    w = torch.empty((t, k), dtype=torch.float32, device=x.device)
+    ids = torch.empty((t, k), dtype=torch.int32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().kdb_moe_route(x.data_ptr(), router.data_ptr(), _ptr(bias), logits.data_ptr(), w.data_ptr(),
+                                      ids.data_ptr(), t, h, e, k, _vp(_stream(x.device)))
+    _lib.check("kdb_moe_route", rc)
+    return logits, w, ids
+
+
+def plan(ids: torch.Tensor, topk_w: torch.Tensor, e: int) -> dict:
+    """Permutation plan: counts [E], offsets [E+1], perm_slot [T*k], slot_pos [T*k] (int32)."""
+    _need("topk_ids", ids, torch.int32, 2)
+    t, k = ids.shape
+    dev = ids.device
+    counts = torch.empty(e, dtype=torch.int32, device=dev)
+    offsets = torch.empty(e + 1, dtype=torch.int32, device=dev)
+    perm_slot = torch.empty(t * k, dtype=torch.int32, device=dev)
+    slot_pos = torch.empty(t * k, dtype=torch.int32, device=dev)
+    nbytes = _lib.lib().kdb_moe_plan_workspace_bytes(t, e, k)
+    ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().kdb_moe_plan(ids.data_ptr(), topk_w.data_ptr(), t, e, k, counts.data_ptr(), offsets.data_ptr(),
+                                     perm_slot.data_ptr(), slot_pos.data_ptr(), ws.data_ptr(), ws.numel(),
+                                     _vp(_stream(dev)))
+    _lib.check("kdb_moe_plan", rc)
+    return {"counts": counts, "offsets": offsets, "perm_slot": perm_slot, "slot_pos": slot_pos}
+
+
+def workspace_bytes(t: int, h: int, e: int, i: int, k: int, shared: int = 0, shared_i: int = 0) -> int:
+    n = int(_lib.lib().kdb_moe_workspace_bytes(t, h, e, i, k, shared, shared_i))
+    if n == 0 and t > 0:
+        raise ValueError(f"unsupported MoE shape t={t} h={h} e={e} i={i} k={k} shared={shared}/{shared_i}")
+    return n
+
+
+@torch.library.custom_op("kdb200::moe", mutates_args=())
+def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tensor], w_gate_up_packed: torch.Tensor,
+        w_down: torch.Tensor, shared_gate_up_packed: Optional[torch.Tensor], shared_down: Optional[torch.Tensor],
+        k: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The fused MoE layer; returns (y bf16[T, H], topk_w fp32[T, k], topk_ids int32[T, k])."""
+    _need("x", x, torch.bfloat16, 2)
+    _need("router", router, torch.float32, 2)
+    _need("w_gate_up_packed", w_gate_up_packed, torch.bfloat16, 3)
+    _need("w_down", w_down, torch.bfloat16, 3)
+    t, h = x.shape
+    e, two_i, h2 = w_gate_up_packed.shape
+    i = two_i // 2
+    if h2 != h or tuple(w_down.shape) != (e, h, i) or tuple(router.shape) != (e, h):
+        raise ValueError("inconsistent MoE weight shapes")
+    shared, shared_i = 0, 0
+    if shared_gate_up_packed is not None:
+        _need("shared_gate_up_packed", shared_gate_up_packed, torch.bfloat16, 3)
+        _need("shared_down", shared_down, torch.bfloat16, 3)
+        shared, shared_i = shared_gate_up_packed.shape[0], shared_gate_up_packed.shape[1] // 2
+    if router_bias is not None:
+        _need("router_bias", router_bias, torch.float32, 1)
+    dev = x.device
+    y = torch.empty((t, h), dtype=torch.bfloat16, device=dev)
+    w = torch.empty((t, k), dtype=torch.float32, device=dev)
+    ids = torch.empty((t, k), dtype=torch.int32, device=dev)
+    nbytes = workspace_bytes(t, h, e, i, k, shared, shared_i)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().kdb_moe_forward(
+            x.data_ptr(), router.data_ptr(), _ptr(router_bias), w_gate_up_packed.data_ptr(), w_down.data_ptr(),
+            _ptr(shared_gate_up_packed), _ptr(shared_down), y.data_ptr(), w.data_ptr(), ids.data_ptr(),
+            t, h, e, i, k, shared, shared_i, ws.data_ptr(), ws.numel(), _vp(_stream(dev)))
+    _lib.check("kdb_moe_forward", rc)
+    return y, w, ids
+
+
+@moe.register_fake
+def _moe_fake(x, router, router_bias, w_gate_up_packed, w_down, shared_gate_up_packed, shared_down, k):
+    t, h = x.shape
+    return (x.new_empty((t, h)), x.new_empty((t, k), dtype=torch.float32), x.new_empty((t, k), dtype=torch.int32))
+
+
+def prepare(weights: dict, k: int) -> dict:
+    """Untimed state for kernel_fn: packed gate/up weights; other weights referenced as given
+    (the caller's tensors are not modified, and every value is kept bit-exact)."""
+    dev = weights["w_gate_up"].device
+    if dev.type != "cuda":
+        raise ValueError("MoE weights must be on a CUDA device")
+    sgu = weights.get("shared_gate_up")
+    bias = weights.get("router_bias")
+    return {
+        "k": int(k),
+        "router": weights["router"].contiguous(),
+        "router_bias": None if bias is None else bias.to(dev).contiguous(),
+        "w_gate_up_packed": pack_gate_up(weights["w_gate_up"].contiguous()),
+        "w_down": weights["w_down"].contiguous(),
+        "shared_gate_up_packed": None if sgu is None else pack_gate_up(sgu.contiguous()),
+        "shared_down": None if sgu is None else weights["shared_down"].contiguous(),
+    }
+
+
+def forward(x: torch.Tensor, state: dict):
+    return moe(x, state["router"], state["router_bias"], state["w_gate_up_packed"], state["w_down"],
+               state["shared_gate_up_packed"], state["shared_down"], state["k"])
