@@ -1,0 +1,528 @@
+#!/usr/bin/env python
+"""bench.py — throughput of the B200 bf16 projection / fused MoE layer, one JSON line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
+
+Default workload: proj_7168_m4096, Y[4096, 7168] = X[4096, 7168] · W[7168, 7168]ᵀ (the projection
+the ≥70 %-of-bf16-peak target is quoted on).  Other workloads: proj_2048, proj_7168_m{16,128,1024,16384},
+moe_decode, moe_prefill, moe_skewed (see kernel-development_b200/kdb200/workloads.py).
+
+A step is one pass of the op over one batch already resident in HBM, replayed from a CUDA graph.
+The L2 is flushed (a 512 MiB device write, untimed) before every timed step; each step is timed
+with CUDA events on its own stream; the time is the max over ranks.  At N > 1 the projection is
+column-parallel with N·7168 global output columns (each rank its own 7168-column shard, no
+collective: weak scaling); the MoE layer runs as N replicas until the expert-parallel path lands.
+
+--impl reference times the oracle (the CPU restatement of the same math) on this host's cores on a
+bounded sample of the workload, and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "kernel-development_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+DEFAULT_WORKLOAD = "proj_7168_m4096"
+FLUSH_BYTES = 512 << 20
+PROFILES = ROOT / "profiles"
+
+
+# ------------------------------------------------------------------------------------------------ utils
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def _profile_traffic(kernel_key: str, workload: str) -> float | None:
+    """dram bytes per launch recorded in profiles/<kernel_key>_<workload>.txt ("traffic_bytes_per_launch: N")."""
+    f = PROFILES / f"{kernel_key}_{workload}.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU through NVML every `period` s while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.ok = False
+        self._stop = threading.Event()
+        self._period = period
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        try:
+            mhz = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM)
+            rs = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            self.samples.append((int(mhz), int(rs)))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self.ok:
+            self._sample()
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        reasons = set()
+        for _, r in self.samples:
+            for name, bit in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def _flusher(dev):
+    buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def flush():
+        buf.fill_(1.0)
+    return flush
+
+
+def _capture(fn):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def timed_steps(step, steps: int, warmup: int, flush, dist: Dist, sampler: ClockSampler | None):
+    """Per-step device times (ms) of `step`, each after an untimed L2 flush; bracketed by a barrier and
+    a synchronize on both sides.  Returns (per-step ms list, elapsed ms of the whole timed region)."""
+    for _ in range(warmup):
+        flush()
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    region0, region1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        region0.record()
+        for a, b in ev:
+            flush()
+            a.record()
+            step()
+            b.record()
+        region1.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev], region0.elapsed_time(region1)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+# ------------------------------------------------------------------------------------------------ projection
+def _proj_cfg(name):
+    from kdb200 import workloads as W
+    return W.PROJ_CONFIGS[name]
+
+
+def bench_proj(args, dist: Dist) -> dict | None:
+    from kdb200 import proj_into
+    from kdb200 import workloads as W
+    import importlib.util
+
+    cfg = _proj_cfg(args.workload)
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    x = W.proj_input(cfg.m, cfg.k, seed=1, device=dev)
+    w = W.proj_weight(cfg.k, cfg.n, seed=100 + dist.rank, device=dev)   # this rank's column shard
+    y = torch.empty((cfg.m, cfg.n), dtype=torch.bfloat16, device=dev)
+    flush = _flusher(dev)
+    g = _capture(lambda: proj_into(x, w, y))
+    sampler = ClockSampler(_physical_index(dist.local)) if dist.rank == 0 else None
+    per_step, region_ms = timed_steps(g.replay, args.steps, args.warmup, flush, dist, sampler)
+    ms = dist.max(sum(per_step) / len(per_step))
+    flops_rank = cfg.flops()
+    value = flops_rank * dist.world / (ms * 1e-3) / 1e12
+
+    # e2e: the public kdev-facing call (submission kernel_fn) with host buffers; H2D of x and D2H of y
+    # inside the timed region, every step.
+    spec = importlib.util.spec_from_file_location(
+        "b200_bf16_proj_sub", ROOT / "kernel-development_b200" / "submissions" / "b200_bf16_proj.py")
+    sub = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sub)
+    state = sub.prepare({_layer_key(cfg): w})
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((cfg.m, cfg.n), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        out = sub.kernel_fn({"x": x_dev, "config": {"m": cfg.m, "layer": _layer_key(cfg)}}, state)
+        y_host.copy_(out, non_blocking=True)
+
+    e2e_steps, _ = timed_steps(e2e_step, max(3, args.steps // 4), 2, flush, dist, None)
+    e2e_ms = dist.max(statistics.mean(e2e_steps))
+    e2e_value = flops_rank * dist.world / (e2e_ms * 1e-3) / 1e12
+    if not torch.equal(y_host.to(dev), y):
+        raise RuntimeError("e2e output differs from the device-resident run")
+
+    if dist.rank != 0:
+        return None
+    peaks = _peaks()
+    achieved = flops_rank / (statistics.mean(per_step) * 1e-3) / 1e12
+    traffic = _profile_traffic("proj_gemm", args.workload)
+    bound = "tensor" if cfg.m >= 1024 else "hbm"
+    if bound == "tensor":
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4)}
+    else:
+        gbs = cfg.bytes() / (statistics.mean(per_step) * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(gbs / peaks["hbm_gbs"], 4)}
+    roof["traffic"] = traffic
+    roof["peak_source"] = f"{peaks['source']} (burst)"
+    roof["kernel"] = "gemm_tn_kernel<ProjSched, ProjEpi> (one launch per step)"
+    line = {
+        "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in roofline.frac)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded X~N(0,1), W~N(0,1/K), bf16)",
+        "config": {"workload": args.workload, "m": cfg.m, "k": cfg.k, "n_per_gpu": cfg.n,
+                   "n_total": cfg.n * dist.world,
+                   "parallelism": f"column-parallel over N, {dist.world} shard(s), no collective",
+                   "l2": "flushed before every timed step (512 MiB device write, untimed)",
+                   "graph": "CUDA graph replay per step"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
+                "path": "submissions/b200_bf16_proj.py kernel_fn (kdev adapter API) -> kdb_proj_bf16",
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps,
+        "roofline": roof,
+        "clocks": sampler.summary() if sampler else None,
+        "timed_region_ms": round(region_ms, 2),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_proj(cfg, args.cpu_seconds)
+    return line
+
+
+def _layer_key(cfg) -> str:
+    return f"k{cfg.k}_n{cfg.n}"
+
+
+def _physical_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local < len(parts) and parts[local].strip().isdigit():
+            return int(parts[local])
+    return local
+
+
+# ------------------------------------------------------------------------------------------------ CPU baseline
+def _cpu_threads() -> int:
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_baseline_proj(cfg, seconds: float, steps: int | None = None) -> dict:
+    """Oracle fp32 projection on the host cores over a bounded row sample of the workload."""
+    from kdb200 import workloads as W
+    from oracle import proj as op
+
+    cores = _cpu_threads()
+    w = W.proj_weight(cfg.k, cfg.n, seed=100)
+    rows = min(cfg.m, 256)
+    x = W.proj_input(rows, cfg.k, seed=1)
+    op.proj_ref(x, w)            # warm-up
+    rates, t_end = [], time.perf_counter() + seconds
+    n = 0
+    while (steps is None and (time.perf_counter() < t_end or n < 3)) or (steps is not None and n < steps):
+        t0 = time.perf_counter()
+        op.proj_ref(x, w)
+        dt = time.perf_counter() - t0
+        rates.append(2.0 * rows * cfg.k * cfg.n / dt / 1e12)
+        n += 1
+    return {"value": round(statistics.median(rates), 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {cfg.m} rows of X against the full W[{cfg.n}, {cfg.k}], fp32 torch matmul "
+                      f"(oracle/proj.py), median of {n} runs"}
+
+
+# ------------------------------------------------------------------------------------------------ MoE
+def bench_moe(args, dist: Dist) -> dict | None:
+    from kdb200 import moe as M
+    from kdb200 import workloads as W
+
+    cfg = W.MOE_CONFIGS[args.workload]
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    x = W.moe_input(cfg.t, cfg.h, seed=1 + dist.rank, device=dev)
+    wts = W.moe_weights(cfg, seed=1, device=dev)
+    state = M.prepare(wts, cfg.k)
+    del wts
+    torch.cuda.empty_cache()
+    flush = _flusher(dev)
+    holder = {}
+
+    def step():
+        holder["out"] = M.forward(x, state)
+
+    g = _capture(step)
+    sampler = ClockSampler(_physical_index(dist.local)) if dist.rank == 0 else None
+    per_step, region_ms = timed_steps(g.replay, args.steps, args.warmup, flush, dist, sampler)
+    ms = dist.max(statistics.mean(per_step))
+    value = cfg.t * dist.world / (ms * 1e-3)
+    ids = holder["out"][2]
+    distinct = int(torch.unique(ids).numel())
+
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((cfg.t, cfg.h), dtype=torch.bfloat16).pin_memory()
+    w_host = torch.empty((cfg.t, cfg.k), dtype=torch.float32).pin_memory()
+    i_host = torch.empty((cfg.t, cfg.k), dtype=torch.int32).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y, w, i = M.forward(x_dev, state)
+        y_host.copy_(y, non_blocking=True)
+        w_host.copy_(w, non_blocking=True)
+        i_host.copy_(i, non_blocking=True)
+
+    e2e_steps, _ = timed_steps(e2e_step, max(3, args.steps // 4), 2, flush, dist, None)
+    e2e_ms = dist.max(statistics.mean(e2e_steps))
+    if dist.rank != 0:
+        return None
+    peaks = _peaks()
+    flops = W.moe_flops(cfg)
+    nbytes = W.moe_bytes(cfg, distinct)
+    t_c = flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    t_m = nbytes / (peaks["hbm_gbs"] * 1e9)
+    layer_s = statistics.mean(per_step) * 1e-3
+    bound = "tensor" if t_c >= t_m else "hbm"
+    if bound == "tensor":
+        ach = flops / layer_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops_sustained"],
+                "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops_sustained"], 4)}
+    else:
+        ach = nbytes / layer_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(ach / peaks["hbm_gbs"], 4)}
+    roof.update({"traffic": None, "peak_source": f"{peaks['source']} (sustained for tensor)",
+                 "kernel": "whole layer (route, plan, gather, grouped gate_up, grouped down, combine)",
+                 "layer_roofline_ms": round(max(t_c, t_m) * 1e3, 4)})
+    launches = 9 + (2 if cfg.shared else 0)
+    return {
+        "metric": "MoE layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; x~N(0,1) bf16, router N(0,1/H) fp32, experts N(0,1/fan_in) bf16)",
+        "config": {"workload": args.workload, **cfg.as_case(), "distinct_experts_hit": distinct,
+                   "parallelism": f"{dist.world} independent replica(s)",
+                   "l2": "flushed before every timed step (512 MiB device write, untimed)",
+                   "graph": "CUDA graph replay per step"},
+        "e2e": {"value": round(cfg.t * dist.world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": cfg.t * cfg.h * 2,
+                "d2h_bytes_per_step": cfg.t * cfg.h * 2 + cfg.t * cfg.k * 8,
+                "path": "kdb200.moe.forward (kdev kernel_fn path) -> kdb_moe_forward",
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": launches * args.steps,
+        "roofline": roof,
+        "clocks": sampler.summary() if sampler else None,
+        "timed_region_ms": round(region_ms, 2),
+    }
+
+
+# ------------------------------------------------------------------------------------------------ reference arm
+def run_reference(args, dist: Dist) -> dict | None:
+    if dist.rank != 0:
+        return None
+    if args.workload.startswith("proj"):
+        cfg = _proj_cfg(args.workload)
+        b = cpu_baseline_proj(cfg, 0.0, steps=args.steps + args.warmup)
+        return {
+            "impl": "reference", "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in "
+            "roofline.frac)", "value": b["value"], "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "m": cfg.m, "k": cfg.k,
+                                                             "n_per_gpu": cfg.n},
+            "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                                       "d2h_bytes_per_step": 0}}
+    b = cpu_baseline_moe(args.workload, steps=args.steps + args.warmup)
+    return {"impl": "reference", "metric": "MoE layer tokens/s", "value": b["value"], "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload},
+            "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                       "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline_moe(workload: str, steps: int = 3) -> dict:
+    """Oracle MoE layer on the host cores over a bounded token sample with CPU-generated weights of the
+    workload's shape restricted to the experts the sample routes to."""
+    from kdb200 import workloads as W
+    from oracle import moe as om
+
+    cores = _cpu_threads()
+    cfg = W.MOE_CONFIGS[workload]
+    t_s = min(cfg.t, 16)
+    x = W.moe_input(t_s, cfg.h, seed=1)
+    router = W._randn((cfg.e, cfg.h), 3, "cpu", 1.0 / cfg.h ** 0.5, torch.float32)
+    bias = W.zipf_router_bias(cfg.e, cfg.zipf_s, 1) if cfg.zipf_s > 0 else None
+    lg, ids, w = om.route(x, router, bias, cfg.k)
+    used = sorted(set(ids.reshape(-1).tolist()))
+    remap = {e: j for j, e in enumerate(used)}
+    sub_cfg = W.MoeConfig("cpu", t_s, cfg.h, len(used), cfg.i, cfg.k, cfg.shared, cfg.shared_i)
+    wts = W.moe_weights(sub_cfg, seed=1)
+    wts["router"] = router
+    ids_sub = ids.clone().apply_(lambda e: remap[e])
+    rates = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        lg2, ids2, w2 = om.route(x, router, bias, cfg.k)
+        om.moe_ref(x, wts, cfg.k, route_out=(lg2, ids_sub, w2))
+        rates.append(t_s / (time.perf_counter() - t0))
+    return {"value": round(statistics.median(rates), 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{t_s} of {cfg.t} tokens through the full layer (router over all {cfg.e} experts, the "
+                      f"{len(used)} experts they route to, shared expert), oracle/moe.py, median of {len(rates)}"}
+
+
+# ------------------------------------------------------------------------------------------------ main
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        line = run_reference(args, _RefDist())
+        print(json.dumps(line), flush=True)
+        return 0
+    dist = Dist()
+    try:
+        if args.workload.startswith("proj"):
+            line = bench_proj(args, dist)
+        elif args.workload.startswith("moe"):
+            line = bench_moe(args, dist)
+        else:
+            raise SystemExit(f"unknown workload {args.workload}")
+        if line is not None and dist.rank == 0:
+            if dist.world > 1:
+                line.pop("cpu_baseline", None)
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+    return 0
+
+
+class _RefDist:
+    rank = 0
+    world = 1
+    local = 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,81 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point include/kdb200.h declares,
+and rejects bad arguments before touching the device."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from kdb200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "kdb200.h"
+
+
+def _declared() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(kdb_[a-z0-9_]+)\s*\(", text))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("kdb_proj_bf16", "kdb_moe_forward", "kdb_moe_route", "kdb_moe_plan", "kdb_status_read"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in sorted(_declared()):
+        assert hasattr(lib, name), f"{name} declared in include/kdb200.h but not exported"
+
+
+def test_python_binding_covers_header():
+    assert _declared() <= set(_lib.SIGNATURES), sorted(_declared() - set(_lib.SIGNATURES))
+
+
+def test_abi_version_and_strerror(lib):
+    assert lib.kdb_abi_version() == 1
+    assert lib.kdb_strerror(0) == b"ok"
+    assert b"timed out" in lib.kdb_strerror(_lib.KDB_ERR_TIMEOUT)
+    assert lib.kdb_strerror(999) == b"unknown status"
+
+
+def test_proj_argument_checks_without_device(lib):
+    vp = ctypes.c_void_p
+    # negative size, ldy < n, K not a multiple of 8, null pointers: all rejected on the host
+    assert lib.kdb_proj_bf16(vp(16), vp(16), vp(16), -1, 8, 8, 8, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16(vp(16), vp(16), vp(16), 4, 8, 8, 4, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16(vp(16), vp(16), vp(16), 4, 8, 12, 8, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16(None, vp(16), vp(16), 4, 8, 8, 8, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16(vp(17), vp(16), vp(16), 4, 8, 8, 8, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16_cfg(vp(16), vp(16), vp(16), 4, 8, 8, 8, 96, None) == _lib.KDB_ERR_INVALID_ARG
+    # empty problems are no-ops
+    assert lib.kdb_proj_bf16(None, None, None, 0, 8, 8, 8, None) == 0
+    assert lib.kdb_proj_bf16(None, None, None, 8, 0, 8, 8, None) == 0
+
+
+def test_moe_workspace_and_shape_checks(lib):
+    assert lib.kdb_moe_workspace_bytes(64, 4096, 64, 1024, 8, 0, 0) > 0
+    # prefill: 8192 x 7168, 256 experts, top-8, shared expert: per-slot rows dominate
+    big = lib.kdb_moe_workspace_bytes(8192, 7168, 256, 2048, 8, 1, 2048)
+    assert 1.0e9 < big < 2.0e9
+    assert lib.kdb_moe_workspace_bytes(64, 4096, 64, 1000, 8, 0, 0) == 0      # i % 128 != 0
+    assert lib.kdb_moe_workspace_bytes(64, 4100, 64, 1024, 8, 0, 0) == 0      # h % 8 != 0
+    assert lib.kdb_moe_workspace_bytes(64, 4096, 4, 1024, 8, 0, 0) == 0       # k > e
+    assert lib.kdb_moe_workspace_bytes(64, 4096, 2048, 1024, 8, 0, 0) == 0    # e > 1024
+    vp = ctypes.c_void_p
+    rc = lib.kdb_moe_forward(*([vp(256)] * 10), 64, 4096, 64, 1024, 8, 0, 0, vp(256), 16, None)
+    assert rc == _lib.KDB_ERR_WORKSPACE
+    rc = lib.kdb_moe_route(vp(16), vp(16), None, vp(16), vp(16), vp(16), 4, 64, 8, 9, None)
+    assert rc == _lib.KDB_ERR_INVALID_ARG
+    rc = lib.kdb_moe_pack_gate_up(vp(16), vp(16), 2, 100, 64, None)
+    assert rc == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_moe_plan_workspace_bytes(100, 16, 4) > 0
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "nope.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        _lib.lib()

@@ -1,0 +1,99 @@
+"""The drop-in boundary, exercised through kdev's own OKC adapter (CPU only).
+
+kdev's OkcAdapter (src/kdev/adapters/okc.py:318-577) loads this build's problem dirs and TOMLs
+(oracle/problems/) and a submission file, and calls prepare / make_inputs / call / check exactly as
+`kdev check` does (src/kdev/checks/check.py:362-448).  The real submissions need a GPU, so the call
+path uses a CPU stand-in with the same two entry points; the real submission files are loaded (not
+called) to show they import cleanly through kdev's loader.  Skipped when kdev's sources are absent
+(KDEV_SRC, default: the reference checkout of this container)."""
+from __future__ import annotations
+
+import os
+import sys
+import textwrap
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+KDEV_SRC = Path(os.environ.get("KDEV_SRC", "/root/reference/src"))
+PROBLEMS = ROOT / "oracle" / "problems"
+SUBS = ROOT / "kernel-development_b200" / "submissions"
+
+pytestmark = pytest.mark.skipif(not (KDEV_SRC / "kdev" / "adapters" / "okc.py").exists(),
+                                reason="kdev sources not available")
+
+
+@pytest.fixture(scope="module")
+def okc():
+    sys.path.insert(0, str(KDEV_SRC))
+    try:
+        from kdev.adapters import okc as mod
+    except Exception as e:  # noqa: BLE001
+        pytest.skip(f"kdev not importable: {e}")
+    yield mod
+    sys.path.remove(str(KDEV_SRC))
+
+
+CPU_PROJ_SUB = textwrap.dedent('''\
+    # CPU stand-in with the submission's entry points (the real one launches libkdb200 kernels)
+    import torch
+    def prepare(weights):
+        return {k: w.contiguous() for k, w in weights.items()}
+    def kernel_fn(data, state):
+        return (data["x"].float() @ state[data["config"]["layer"]].float().T).to(torch.bfloat16)
+    ''')
+
+
+def test_projection_problem_through_kdev(okc, tmp_path):
+    a = okc.OkcAdapter(str(PROBLEMS / "b200_bf16_proj"), str(PROBLEMS / "b200_bf16_proj.toml"))
+    assert a.problem == "b200_bf16_proj" and a.kernel_fn_args() == 2
+    assert [s.shape_id for s in a.tests()] == ["t0", "t1", "t2"]
+    assert any(s.case == {"m": 4096, "layer": "k7168_n7168"} for s in a.shapes())
+    sub = tmp_path / "cpu_sub.py"
+    sub.write_text(CPU_PROJ_SUB)
+    mod = a.load(str(sub), "cpu")
+    state = a.prepare(mod)
+    for shape in a.tests()[:2]:
+        data = a.make_inputs(shape, seed=7)
+        out = a.call(mod, state, data)
+        res = a.check(data, out)
+        assert res.ok, res.message
+        assert res.max_rel_err is not None and res.max_rel_err < 1e-2
+        assert res.tol == pytest.approx(1e-2)
+    bad = a.check(data, out * 1.5)
+    assert not bad.ok
+    sol = a.speed_of_light_us(a.shapes()[-2], {"hbm_bytes_per_s": 6.55e12, "bf16_dense_flops_per_s": 1.657e15})
+    assert 200 < sol < 300      # 4096 x 7168 x 7168 at the measured bf16 peak
+
+
+def test_real_submissions_load_through_kdev(okc):
+    a = okc.OkcAdapter(str(PROBLEMS / "b200_bf16_proj"), str(PROBLEMS / "b200_bf16_proj.toml"))
+    mod = a.load(str(SUBS / "b200_bf16_proj.py"), "real")
+    assert callable(mod.prepare) and callable(mod.kernel_fn)
+    for p in ("decode", "prefill", "skewed"):
+        m = okc.OkcAdapter(str(PROBLEMS / f"b200_moe_{p}"), str(PROBLEMS / f"b200_moe_{p}.toml"))
+        sm = m.load(str(SUBS / f"b200_moe_{p}.py"), f"real_{p}")
+        assert callable(sm.prepare) and callable(sm.kernel_fn)
+
+
+def test_moe_problem_check_through_kdev(okc, tmp_path, monkeypatch):
+    """The decode MoE problem's reference checks an oracle-computed output as passing and a perturbed
+    routing as failing, with kdev parsing the message."""
+    sys.path.insert(0, str(ROOT))
+    from kdb200 import workloads as W
+    from oracle import moe as om
+    small = W.MoeConfig("moe_decode", 64, 256, 16, 128, 4)
+    monkeypatch.setitem(W.MOE_CONFIGS, "moe_decode", small)
+    for name in [n for n in list(sys.modules) if n.startswith("_kdev_ref_")]:
+        del sys.modules[name]
+    a = okc.OkcAdapter(str(PROBLEMS / "b200_moe_decode"), str(PROBLEMS / "b200_moe_decode.toml"))
+    w = a.weights()
+    data = a.make_inputs(a.tests()[1], seed=3)
+    ref = om.moe_ref(data["x"], w, small.k)
+    res = a.check(data, (ref["y"], ref["w"], ref["ids"]))
+    assert res.ok, res.message
+    ids = ref["ids"].clone()
+    ids[0, 0] = (ids[0, 0] + 1) % small.e
+    res2 = a.check(data, (ref["y"], ref["w"], ids))
+    assert not res2.ok and "mismatched 1" in res2.message

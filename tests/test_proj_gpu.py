@@ -1,0 +1,138 @@
+"""GPU parity tests of the bf16 projection (libkdb200 kdb_proj_bf16) against the fp32 oracle.
+
+Tolerance (written here, shared with the oracle's check): max-abs <= 2e-2 and relative Frobenius
+<= 1e-2 against x.float() @ w.float().T; the bf16 rounding of Y alone gives ~1.7e-3."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from kdb200 import _lib, proj, proj_into
+from kdb200 import workloads as W
+from oracle import proj as op
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+MAX_ABS = 2e-2
+REL_FRO = 1e-2
+
+
+def _pair(m, k, n, seed=0):
+    x = W.proj_input(m, k, seed)
+    w = W.proj_weight(k, n, seed)
+    return x, w, x.cuda(), w.cuda()
+
+
+def _assert_close(y, ref):
+    c = op.compare(y, ref)
+    assert c["nonfinite"] == 0, c
+    assert c["max_abs"] <= MAX_ABS and c["rel_fro"] <= REL_FRO, c
+
+
+@pytest.mark.parametrize("m,k,n", [
+    (128, 2048, 2048),     # projection config of the CPU-runnable case
+    (1, 64, 256), (16, 7168, 512), (200, 300 - 4, 300), (129, 136, 257), (257, 512, 1000),
+    (64, 8, 64), (512, 1024, 768), (1000, 520, 64),
+])
+def test_proj_matches_oracle(m, k, n):
+    x, w, gx, gw = _pair(m, k, n, seed=m + n)
+    y = proj(gx, gw)
+    torch.cuda.synchronize()
+    _assert_close(y, op.proj_ref(x, w))
+
+
+@pytest.mark.parametrize("tile_n", [64, 128, 256])
+def test_every_tile_width(tile_n):
+    x, w, gx, gw = _pair(300, 256, 520, seed=tile_n)
+    y = torch.empty((300, 520), dtype=torch.bfloat16, device="cuda")
+    proj_into(gx, gw, y, tile_n=tile_n)
+    torch.cuda.synchronize()
+    _assert_close(y, op.proj_ref(x, w))
+
+
+def test_output_into_column_slice():
+    """Column-parallel layout: write into a slice of a wider Y (row stride ldy > n)."""
+    x, w, gx, gw = _pair(64, 128, 96, seed=5)
+    big = torch.full((64, 256), 7.0, dtype=torch.bfloat16, device="cuda")
+    proj_into(gx, gw, big[:, 64:160])
+    torch.cuda.synchronize()
+    _assert_close(big[:, 64:160], op.proj_ref(x, w))
+    assert bool((big[:, :64] == 7).all()) and bool((big[:, 160:] == 7).all())
+
+
+def test_k_zero_writes_zeros():
+    gx = torch.empty((4, 0), dtype=torch.bfloat16, device="cuda")
+    gw = torch.empty((8, 0), dtype=torch.bfloat16, device="cuda")
+    y = proj(gx, gw)
+    torch.cuda.synchronize()
+    assert bool((y == 0).all())
+
+
+def test_bad_arguments_raise():
+    gx = torch.zeros((4, 12), dtype=torch.bfloat16, device="cuda")
+    gw = torch.zeros((8, 12), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.KdbError):
+        proj(gx, gw)                       # K % 8 != 0
+    with pytest.raises(ValueError):
+        proj(gx.float(), gw)
+
+
+def test_golden_fixtures():
+    for name in ("proj_small", "proj_ragged"):
+        f = np.load(GOLDEN / f"{name}.npz")
+        x = torch.from_numpy(f["x_bits"].view(np.int16)).view(torch.bfloat16)
+        w = torch.from_numpy(f["w_bits"].view(np.int16)).view(torch.bfloat16)
+        y = proj(x.cuda(), w.cuda())
+        torch.cuda.synchronize()
+        _assert_close(y, torch.from_numpy(f["y32"]))
+
+
+def test_graph_replay_bitwise_equal_to_eager():
+    """kdev replays the op inside a CUDA graph with fresh inputs copied into the captured buffers."""
+    x, w, gx, gw = _pair(256, 512, 768, seed=9)
+    eager = proj(gx, gw).clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        proj(gx, gw)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = proj(gx, gw)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    x2 = W.proj_input(256, 512, 99)
+    gx.copy_(x2.cuda())
+    g.replay()
+    torch.cuda.synchronize()
+    _assert_close(out, op.proj_ref(x2, w))
+
+
+def test_full_size_sampled_rows():
+    """4096 x 7168 x 7168 (the headline configuration): rows sampled across the whole output are
+    checked against the oracle; row-independence makes the sample representative."""
+    m, k, n = 4096, 7168, 7168
+    gx = W.proj_input(m, k, 3, device="cuda")
+    gw = W.proj_weight(k, n, 3, device="cuda")
+    y = proj(gx, gw)
+    torch.cuda.synchronize()
+    rows = torch.tensor([0, 1, 127, 128, 1000, 2047, 2048, 3333, 4094, 4095])
+    ref = gx[rows].cpu().float() @ gw.cpu().float().T
+    _assert_close(y[rows], ref)
+
+
+def test_deterministic_and_row_independent():
+    """Same input twice -> bitwise equal; permuting X's rows permutes Y's rows bitwise."""
+    gx = W.proj_input(384, 1024, 4, device="cuda")
+    gw = W.proj_weight(1024, 512, 4, device="cuda")
+    y1 = proj(gx, gw)
+    y2 = proj(gx, gw)
+    perm = torch.randperm(384, generator=torch.Generator().manual_seed(0)).cuda()
+    y3 = proj(gx[perm].contiguous(), gw)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert torch.equal(y3, y1[perm])
