@@ -94,10 +94,10 @@ int moe_forward(const void* x, const float* router_w, const float* router_bias, 
                 cudaStream_t s) {
   int rc = moe_check_shape(sh);
   if (rc) return rc;
+  if (sh.t == 0) return KDB_OK;   // nothing to route (empty tensors may carry null pointers)
   if (!x || !router_w || !w_gate_up_packed || !w_down || !y || !topk_w || !topk_ids) return KDB_ERR_INVALID_ARG;
   if (sh.shared && (!shared_gate_up_packed || !shared_down)) return KDB_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(y) || !aligned16(w_gate_up_packed) || !aligned16(w_down)) return KDB_ERR_INVALID_ARG;
-  if (sh.t == 0) return KDB_OK;
   const Carve c = carve(sh);
   if (!workspace || workspace_bytes < c.total) return KDB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1)) != 0) return KDB_ERR_INVALID_ARG;

@@ -114,7 +114,15 @@ static int launch_proj_cfg(const void* x, const void* w, void* y, int M, int N, 
   sp.K = K;
   sp.num_m = (M + BM - 1) / BM;
   sp.num_n = (N + BN - 1) / BN;
-  sp.group_m = 16;
+  // M-blocks per raster group: as many as keep the group's X rows (group_m x 128 x K bf16) within
+  // 64 MiB of L2, so W is streamed from DRAM once per group and the whole of X when it fits.
+  {
+    const long long per_block = static_cast<long long>(BM) * K * 2;
+    long long g = (64ll << 20) / (per_block > 0 ? per_block : 1);
+    if (g < 1) g = 1;
+    if (g > sp.num_m) g = sp.num_m;
+    sp.group_m = static_cast<int>(g);
+  }
   typename Epi::Params ep;
   ep.y = static_cast<__nv_bfloat16*>(y);
   ep.ldy = ldy;
