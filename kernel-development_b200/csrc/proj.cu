@@ -140,13 +140,13 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
               int force_bn, cudaStream_t stream) {
   if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return KDB_OK;
-  if (!x || !w || !y) return KDB_ERR_INVALID_ARG;
-  if (ldy < N) return KDB_ERR_INVALID_ARG;
+  if (!y || ldy < N) return KDB_ERR_INVALID_ARG;
   if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 30)) return KDB_ERR_UNSUPPORTED;
-  if (K == 0) {
+  if (K == 0) {   // empty reduction: Y = 0 (X and W are empty and may be null)
     return cuda_status(cudaMemset2DAsync(y, static_cast<size_t>(ldy) * 2, 0, static_cast<size_t>(N) * 2,
                                          static_cast<size_t>(M), stream));
   }
+  if (!x || !w) return KDB_ERR_INVALID_ARG;
   // TMA: 16-byte aligned base and row stride.
   if (K % 8 != 0 || !aligned16(x) || !aligned16(w)) return KDB_ERR_INVALID_ARG;
 

@@ -18,7 +18,7 @@ def _check_operand(name: str, t: torch.Tensor) -> None:
         raise TypeError(f"{name} must be bfloat16, got {t.dtype}")
     if t.dim() != 2:
         raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
-    if t.stride(1) != 1 or t.stride(0) != t.shape[1]:
+    if not t.is_contiguous():
         raise ValueError(f"{name} must be row-major contiguous")
 
 

@@ -76,8 +76,8 @@ def test_bad_arguments_raise():
     gw = torch.zeros((8, 12), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.KdbError):
         proj(gx, gw)                       # K % 8 != 0
-    with pytest.raises(ValueError):
-        proj(gx.float(), gw)
+    with pytest.raises(TypeError):
+        proj(gx.float(), gw)                 # not bf16
 
 
 def test_golden_fixtures():
