@@ -119,6 +119,19 @@ int kdb_moe_plan(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_
                  void* stream);
 
 /*
+ * The permutation plan of kdb_moe_plan without a caller workspace.  No counterpart in the
+ * reference: an addition for callers that cannot allocate device memory (a runtime that reserves
+ * all memory at start-up and reaches this library through a C FFI, or code that must not call
+ * cudaMalloc), who pass only their inputs and outputs.  Its scratch is a fixed 1,577,216-byte array
+ * inside the library (held on every GPU that loads it until exit); limits t*k <= 131072,
+ * e <= 1024, ceil(t/256)*e <= 65536, else KDB_ERR_UNSUPPORTED.  The first call on a device resolves
+ * the array's address (a runtime call): make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race, so issue them on one stream.  Outputs as kdb_moe_plan.
+ */
+int kdb_moe_plan_noalloc(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_t e, int64_t k,
+                         int32_t* counts, int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* stream);
+
+/*
  * The whole layer.  x bf16 [t, h]; y bf16 [t, h]; topk_w fp32 [t, k]; topk_ids int32 [t, k] (the
  * routing outputs the reference's routing problems report at output index 2,
  * src/kdev/adapters/okc_problems/muse_prefill_layer.toml:148).  workspace: >= kdb_moe_workspace_bytes,

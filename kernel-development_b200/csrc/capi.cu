@@ -105,6 +105,12 @@ int kdb_moe_plan(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_
                             workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int kdb_moe_plan_noalloc(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_t e, int64_t k,
+                         int32_t* counts, int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* stream) {
+  return kdb::moe_plan_noalloc(topk_ids, topk_w, t, e, k, counts, offsets, perm_slot, slot_pos,
+                               static_cast<cudaStream_t>(stream));
+}
+
 int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
                     const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                     float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,

@@ -5,4 +5,5 @@
 #include "moe_route.cu"
 #include "moe_gemm.cu"
 #include "moe.cu"
+#include "moe_noalloc.cu"
 #include "capi.cu"

@@ -37,6 +37,10 @@ size_t moe_plan_scratch_bytes(long long t, long long e, long long k);
 int moe_plan_only(const int* ids, const float* topk_w, int T, int E, int k, int* counts, int* offsets,
                   int* perm_slot, int* slot_pos, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
+// kdb_moe_plan_noalloc: the plan with scratch in a fixed device array (moe_noalloc.cu).
+int moe_plan_noalloc(const int* ids, const float* topk_w, long long T, long long E, long long k, int* counts,
+                     int* offsets, int* perm_slot, int* slot_pos, cudaStream_t s);
+
 int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
                 const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                 float* topk_w, int* topk_ids, const MoeShape& sh, void* workspace, size_t workspace_bytes,

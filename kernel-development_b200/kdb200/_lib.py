@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_moe_plan_workspace_bytes": (_c_size, [_c_i64] * 3),
     "kdb_moe_plan": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_size,
                               _c_vp]),
+    "kdb_moe_plan_noalloc": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
     "kdb_moe_forward": (_c_int, [_c_vp] * 10 + [_c_i64] * 7 + [_c_vp, _c_size, _c_vp]),
 }
 
