@@ -132,12 +132,40 @@ int kdb_moe_plan_noalloc(const int32_t* topk_ids, const float* topk_w, int64_t t
                          int32_t* counts, int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* stream);
 
 /*
+ * One-time router preparation for the tensor-core routing path: router_split bf16 [e, 2h] receives
+ * [bf16(W) | bf16(W - bf16(W))] per expert row and router_norms fp32 [e] an upper bound of each
+ * row's 2-norm.  Lossless for the layer (router_w itself stays the source of the exact logits).
+ */
+int kdb_moe_prepare_router(const float* router_w, void* router_split, float* router_norms, int64_t e, int64_t h,
+                           void* stream);
+
+/* approx fp32 [t, e] = x · [W_hi | W_mid]ᵀ on the tensor cores (h % 64 == 0): the routing pre-pass. */
+int kdb_moe_router_approx(const void* x, const void* router_split, float* approx, int64_t t, int64_t h, int64_t e,
+                          void* stream);
+
+/* Scratch bytes of kdb_moe_route_fast. */
+size_t kdb_moe_route_fast_workspace_bytes(int64_t t, int64_t e);
+
+/*
+ * Router stage on the tensor-core path: ids and weights identical to kdb_moe_route (the candidates
+ * of a rigorous error bound around the k-th approximate logit are recomputed in the fixed fp64
+ * order), without computing every fp64 logit.  h % 64 == 0.  Counterpart of the routing plan's
+ * top-k read (x3_h.cu:346-365) with the router inside the layer.
+ */
+int kdb_moe_route_fast(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                       const float* router_norms, float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e,
+                       int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * The whole layer.  x bf16 [t, h]; y bf16 [t, h]; topk_w fp32 [t, k]; topk_ids int32 [t, k] (the
  * routing outputs the reference's routing problems report at output index 2,
  * src/kdev/adapters/okc_problems/muse_prefill_layer.toml:148).  workspace: >= kdb_moe_workspace_bytes,
  * 256-byte aligned.  shared_gate_up_packed / shared_down may be NULL when shared == 0.
+ * router_split / router_norms (from kdb_moe_prepare_router) select the tensor-core routing path;
+ * NULL computes every logit in the fixed fp64 order.  Both give identical ids and weights.
  */
-int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                    const float* router_norms, const void* w_gate_up_packed,
                     const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                     float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,
                     int64_t shared, int64_t shared_i, void* workspace, size_t workspace_bytes, void* stream);

@@ -111,11 +111,48 @@ int kdb_moe_plan_noalloc(const int32_t* topk_ids, const float* topk_w, int64_t t
                                static_cast<cudaStream_t>(stream));
 }
 
-int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+int kdb_moe_prepare_router(const float* router_w, void* router_split, float* router_norms, int64_t e, int64_t h,
+                           void* stream) {
+  if (e <= 0 || h <= 0 || e > 1024 || e * h > (1ll << 31)) return KDB_ERR_INVALID_ARG;
+  if (!router_w || !router_split || !router_norms) return KDB_ERR_INVALID_ARG;
+  return kdb::router_prepare(router_w, router_split, router_norms, (int)e, (int)h, static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_router_approx(const void* x, const void* router_split, float* approx, int64_t t, int64_t h, int64_t e,
+                          void* stream) {
+  if (t < 0 || h <= 0 || e <= 0 || e > 1024 || h % 64 != 0) return KDB_ERR_INVALID_ARG;
+  if (t == 0) return KDB_OK;
+  if (!x || !router_split || !approx || !kdb::aligned16(x) || !kdb::aligned16(router_split)) return KDB_ERR_INVALID_ARG;
+  if (t * e > (1ll << 31) / 4) return KDB_ERR_UNSUPPORTED;
+  return kdb::router_approx(x, router_split, approx, (int)t, (int)h, (int)e, static_cast<cudaStream_t>(stream));
+}
+
+size_t kdb_moe_route_fast_workspace_bytes(int64_t t, int64_t e) {
+  if (t < 0 || e <= 0) return 0;
+  return kdb::router_fast_scratch_bytes(t, e);
+}
+
+int kdb_moe_route_fast(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                       const float* router_norms, float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e,
+                       int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (t < 0 || h <= 0 || h % 64 != 0 || e <= 0 || e > 1024 || k <= 0 || k > e || k > 32) return KDB_ERR_INVALID_ARG;
+  if (t * e > (1ll << 31) / 4) return KDB_ERR_UNSUPPORTED;
+  if (t == 0) return KDB_OK;
+  if (!x || !router_w || !router_split || !router_norms || !topk_w || !topk_ids) return KDB_ERR_INVALID_ARG;
+  if (!kdb::aligned16(x) || !kdb::aligned16(router_w) || !kdb::aligned16(router_split)) return KDB_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < kdb::router_fast_scratch_bytes(t, e)) return KDB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_route_fast(x, router_w, router_bias, router_split, router_norms, topk_w, topk_ids, (int)t, (int)h,
+                             (int)e, (int)k, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                    const float* router_norms, const void* w_gate_up_packed,
                     const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                     float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,
                     int64_t shared, int64_t shared_i, void* workspace, size_t workspace_bytes, void* stream) {
-  return kdb::moe_forward(x, router_w, router_bias, w_gate_up_packed, w_down, shared_gate_up_packed, shared_down, y,
+  return kdb::moe_forward(x, router_w, router_bias, router_split, router_norms, w_gate_up_packed, w_down,
+                          shared_gate_up_packed, shared_down, y,
                           topk_w, topk_ids, moe_shape(t, h, e, i, k, shared, shared_i), workspace, workspace_bytes,
                           static_cast<cudaStream_t>(stream));
 }

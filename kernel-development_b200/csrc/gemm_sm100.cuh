@@ -9,8 +9,9 @@
 //
 // Policies:
 //   Sched::Params, Sched(params), int num_tiles(), TileInfo tile(int t)
-//     TileInfo has a_row, b_row (TMA row coordinates), nkb (number of 64-wide k slices), and the
-//     fields the epilogue needs.
+//     TileInfo has a_row, b_row (TMA row coordinates), nkb (number of 64-wide k slices), a_kwrap
+//     (0, or the number of k slices after which A's k coordinate starts again at 0, so one A tile
+//     multiplies B's k range [0, nkb*64) as [A | A | ...]), and the fields the epilogue needs.
 //   Epi::Params, static void run(params, tile_info, row_in_tile, taddr_row)
 //     row_in_tile in [0, 128); taddr_row addresses TMEM lane row_in_tile, column 0 of the tile.
 //
@@ -129,7 +130,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(sA + stage * L::kABytes, &tmA, &full[stage], kb * kBK, ti.a_row, pol_a);
+          const int a_kb = ti.a_kwrap > 0 ? kb % ti.a_kwrap : kb;   // A's k coordinate may wrap
+          tma_load_2d(sA + stage * L::kABytes, &tmA, &full[stage], a_kb * kBK, ti.a_row, pol_a);
           tma_load_2d(sB + stage * L::kBBytes, &tmB, &full[stage], kb * kBK, ti.b_row, pol_b);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);

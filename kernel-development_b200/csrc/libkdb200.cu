@@ -4,6 +4,7 @@
 #include "proj.cu"
 #include "moe_route.cu"
 #include "moe_gemm.cu"
+#include "moe_router_fast.cu"
 #include "moe.cu"
 #include "moe_noalloc.cu"
 #include "capi.cu"

@@ -27,7 +27,7 @@ Carve carve(const MoeShape& sh) {
   const size_t R = T * K;
   const size_t C = (T + kChunk - 1) / kChunk;
   size_t o = 0;
-  c.logits = o;       o += up(sizeof(float) * T * E);
+  c.logits = o;       o += router_fast_scratch_bytes(T, E);   // exact logits, or approx + candidates
   c.chunk_counts = o; o += up(sizeof(int) * C * E);
   c.chunk_base = o;   o += up(sizeof(int) * C * E);
   c.counts = o;       o += up(sizeof(int) * E);
@@ -88,7 +88,8 @@ int moe_plan_only(const int* ids, const float* topk_w, int T, int E, int k, int*
                   perm_token, perm_w, s);
 }
 
-int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                const float* router_norms, const void* w_gate_up_packed,
                 const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                 float* topk_w, int* topk_ids, const MoeShape& sh, void* workspace, size_t workspace_bytes,
                 cudaStream_t s) {
@@ -109,7 +110,14 @@ int moe_forward(const void* x, const float* router_w, const float* router_bias, 
   const int I = static_cast<int>(sh.i), K = static_cast<int>(sh.k);
   const int R = T * K;
 
-  rc = moe_route(x, router_w, router_bias, F(c.logits), topk_w, topk_ids, T, H, E, K, s);
+  // Routing: the tensor-core pre-pass with exact re-evaluation of the candidates when the router has
+  // been prepared (kdb_moe_prepare_router) and H is a multiple of 64; otherwise every logit in the
+  // fixed fp64 order.  Both give identical ids and weights.
+  if (router_split && router_norms && H % 64 == 0 && aligned16(router_w) && aligned16(router_split))
+    rc = moe_route_fast(x, router_w, router_bias, router_split, router_norms, topk_w, topk_ids, T, H, E, K,
+                        ws + c.logits, s);
+  else
+    rc = moe_route(x, router_w, router_bias, F(c.logits), topk_w, topk_ids, T, H, E, K, s);
   if (rc) return rc;
   rc = moe_plan(topk_ids, topk_w, T, E, K, Ip(c.chunk_counts), Ip(c.chunk_base), Ip(c.counts), Ip(c.offsets),
                 Ip(c.mtile_start), Ip(c.perm_slot), Ip(c.slot_pos), Ip(c.perm_token), F(c.perm_w), s);

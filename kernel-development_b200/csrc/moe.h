@@ -41,7 +41,15 @@ int moe_plan_only(const int* ids, const float* topk_w, int T, int E, int k, int*
 int moe_plan_noalloc(const int* ids, const float* topk_w, long long T, long long E, long long k, int* counts,
                      int* offsets, int* perm_slot, int* slot_pos, cudaStream_t s);
 
-int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* w_gate_up_packed,
+// Fast router (moe_router_fast.cu): prepare splits the fp32 router into [bf16 hi | bf16 mid] and row norms.
+int router_prepare(const float* wr, void* wcat, float* norms, int E, int H, cudaStream_t s);
+int router_approx(const void* x, const void* wcat, float* approx, int T, int H, int E, cudaStream_t s);
+size_t router_fast_scratch_bytes(long long T, long long E);
+int moe_route_fast(const void* x, const float* wr, const float* bias, const void* wcat, const float* norms,
+                   float* topk_w, int* topk_ids, int T, int H, int E, int k, void* scratch, cudaStream_t s);
+
+int moe_forward(const void* x, const float* router_w, const float* router_bias, const void* router_split,
+                const float* router_norms, const void* w_gate_up_packed,
                 const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,
                 float* topk_w, int* topk_ids, const MoeShape& sh, void* workspace, size_t workspace_bytes,
                 cudaStream_t s);

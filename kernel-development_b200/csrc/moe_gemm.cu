@@ -18,7 +18,7 @@
 namespace kdb {
 
 struct GroupTile {
-  int a_row, b_row, nkb;
+  int a_row, b_row, nkb, a_kwrap;
   int row0, valid, n0;
 };
 
@@ -62,6 +62,7 @@ struct GroupSched {
     ti.a_row = ti.row0;
     ti.b_row = g * p.b_rows_per_group + nb * BN;
     ti.nkb = p.nkb;
+    ti.a_kwrap = 0;
     return ti;
   }
 };

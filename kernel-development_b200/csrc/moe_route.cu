@@ -8,10 +8,10 @@
 // tokens ascending within an expert, so the result is deterministic and matches the CPU oracle
 // exactly.
 //
-// Router logits use a fixed fp64 summation order so they are bit-identical to the oracle: lane l
-// of a warp accumulates h = l, l+32, ... with fma, then the 32 partials are combined by an xor
-// butterfly with offsets 16, 8, 4, 2, 1; the fp64 sum is rounded once to fp32, then the optional
-// fp32 bias is added.
+// Router logits use a fixed fp64 summation order so they are bit-identical to the oracle: h is cut
+// into blocks of 256; lane l of a warp accumulates, block by block, h = 256*b + 8*l + j for
+// j = 0..7 with fma; then the 32 partials are combined by an xor butterfly with offsets 16, 8, 4,
+// 2, 1; the fp64 sum is rounded once to fp32, then the optional fp32 bias is added.
 #include "moe.h"
 #include "host_util.h"
 #include "sm100_common.cuh"
@@ -21,7 +21,7 @@ namespace kdb {
 constexpr int kRouteTokTile = 16;   // tokens per CTA
 constexpr int kRouteExpPerWarp = 2; // experts per warp
 constexpr int kRouteWarps = 8;      // -> 16 experts per CTA
-constexpr int kRouteHChunk = 256;   // hidden elements staged per pass (multiple of 32)
+constexpr int kRouteHChunk = 256;   // hidden elements staged per pass: one block of the fixed order
 
 __global__ void __launch_bounds__(kRouteWarps * 32)
     moe_router_logits_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
@@ -44,8 +44,11 @@ __global__ void __launch_bounds__(kRouteWarps * 32)
       xs[t][hh] = (tok < T && h < H) ? static_cast<double>(__bfloat162float(x[static_cast<long long>(tok) * H + h])) : 0.0;
     }
     __syncthreads();
-    const int hend = min(kRouteHChunk, H - h0);
-    for (int hh = lane; hh < hend; hh += 32) {
+    // this lane's 8 consecutive elements of the 256-block (kRouteHChunk == 256)
+#pragma unroll 1
+    for (int j = 0; j < 8; ++j) {
+      const int hh = 8 * lane + j;
+      if (h0 + hh >= H) break;
       double wv[kRouteExpPerWarp];
 #pragma unroll
       for (int q = 0; q < kRouteExpPerWarp; ++q) {

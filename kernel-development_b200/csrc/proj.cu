@@ -11,7 +11,7 @@
 namespace kdb {
 
 struct ProjTile {
-  int a_row, b_row, nkb;
+  int a_row, b_row, nkb, a_kwrap;
   int m0, n0;
 };
 
@@ -20,6 +20,7 @@ struct ProjSched {
   struct Params {
     int M, N, K;
     int num_m, num_n, group_m;
+    int kwrap;   // 0, or k slices after which A's k coordinate wraps (K spans several copies of A's K)
   };
   Params p;
   __device__ explicit ProjSched(const Params& pp) : p(pp) {}
@@ -40,6 +41,7 @@ struct ProjSched {
     ti.a_row = ti.m0;
     ti.b_row = ti.n0;
     ti.nkb = (p.K + kBK - 1) / kBK;
+    ti.a_kwrap = p.kwrap;
     return ti;
   }
 };
@@ -114,6 +116,7 @@ static int launch_proj_cfg(const void* x, const void* w, void* y, int M, int N, 
   sp.K = K;
   sp.num_m = (M + BM - 1) / BM;
   sp.num_n = (N + BN - 1) / BN;
+  sp.kwrap = 0;
   // M-blocks per raster group: as many as keep the group's X rows (group_m x 128 x K bf16) within
   // 64 MiB of L2, so W is streamed from DRAM once per group and the whole of X when it fits.
   {

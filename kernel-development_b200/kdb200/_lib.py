@@ -40,7 +40,11 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_moe_plan": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_size,
                               _c_vp]),
     "kdb_moe_plan_noalloc": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
-    "kdb_moe_forward": (_c_int, [_c_vp] * 10 + [_c_i64] * 7 + [_c_vp, _c_size, _c_vp]),
+    "kdb_moe_prepare_router": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "kdb_moe_router_approx": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
+    "kdb_moe_route_fast_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
+    "kdb_moe_route_fast": (_c_int, [_c_vp] * 7 + [_c_i64] * 4 + [_c_vp, _c_size, _c_vp]),
+    "kdb_moe_forward": (_c_int, [_c_vp] * 12 + [_c_i64] * 7 + [_c_vp, _c_size, _c_vp]),
 }
 
 _lock = threading.Lock()

@@ -84,6 +84,48 @@ def plan(ids: torch.Tensor, topk_w: torch.Tensor, e: int) -> dict:
     return {"counts": counts, "offsets": offsets, "perm_slot": perm_slot, "slot_pos": slot_pos}
 
 
+def prepare_router(router: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(router_split bf16 [E, 2H], router_norms fp32 [E]) for the tensor-core routing path."""
+    _need("router", router, torch.float32, 2)
+    e, h = router.shape
+    split = torch.empty((e, 2 * h), dtype=torch.bfloat16, device=router.device)
+    norms = torch.empty(e, dtype=torch.float32, device=router.device)
+    with torch.cuda.device(router.device):
+        rc = _lib.lib().kdb_moe_prepare_router(router.data_ptr(), split.data_ptr(), norms.data_ptr(), e, h,
+                                               _vp(_stream(router.device)))
+    _lib.check("kdb_moe_prepare_router", rc)
+    return split, norms
+
+
+def router_approx(x: torch.Tensor, split: torch.Tensor) -> torch.Tensor:
+    """fp32 [T, E] tensor-core pre-pass logits x · [W_hi | W_mid]ᵀ (without bias)."""
+    t, h = x.shape
+    e = split.shape[0]
+    out = torch.empty((t, e), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().kdb_moe_router_approx(x.data_ptr(), split.data_ptr(), out.data_ptr(), t, h, e,
+                                              _vp(_stream(x.device)))
+    _lib.check("kdb_moe_router_approx", rc)
+    return out
+
+
+def route_fast(x: torch.Tensor, router: torch.Tensor, bias: Optional[torch.Tensor], split: torch.Tensor,
+               norms: torch.Tensor, k: int):
+    """(topk_w, topk_ids) of the tensor-core routing path (identical to route()'s)."""
+    t, h = x.shape
+    e = router.shape[0]
+    w = torch.empty((t, k), dtype=torch.float32, device=x.device)
+    ids = torch.empty((t, k), dtype=torch.int32, device=x.device)
+    nbytes = int(_lib.lib().kdb_moe_route_fast_workspace_bytes(t, e))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().kdb_moe_route_fast(x.data_ptr(), router.data_ptr(), _ptr(bias), split.data_ptr(),
+                                           norms.data_ptr(), w.data_ptr(), ids.data_ptr(), t, h, e, k, ws.data_ptr(),
+                                           ws.numel(), _vp(_stream(x.device)))
+    _lib.check("kdb_moe_route_fast", rc)
+    return w, ids
+
+
 def workspace_bytes(t: int, h: int, e: int, i: int, k: int, shared: int = 0, shared_i: int = 0) -> int:
     n = int(_lib.lib().kdb_moe_workspace_bytes(t, h, e, i, k, shared, shared_i))
     if n == 0 and t > 0:
@@ -92,8 +134,9 @@ def workspace_bytes(t: int, h: int, e: int, i: int, k: int, shared: int = 0, sha
 
 
 @torch.library.custom_op("kdb200::moe", mutates_args=())
-def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tensor], w_gate_up_packed: torch.Tensor,
-        w_down: torch.Tensor, shared_gate_up_packed: Optional[torch.Tensor], shared_down: Optional[torch.Tensor],
+def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tensor], router_split: Optional[torch.Tensor],
+        router_norms: Optional[torch.Tensor], w_gate_up_packed: torch.Tensor, w_down: torch.Tensor,
+        shared_gate_up_packed: Optional[torch.Tensor], shared_down: Optional[torch.Tensor],
         k: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """The fused MoE layer; returns (y bf16[T, H], topk_w fp32[T, k], topk_ids int32[T, k])."""
     _need("x", x, torch.bfloat16, 2)
@@ -120,7 +163,8 @@ def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tenso
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
         rc = _lib.lib().kdb_moe_forward(
-            x.data_ptr(), router.data_ptr(), _ptr(router_bias), w_gate_up_packed.data_ptr(), w_down.data_ptr(),
+            x.data_ptr(), router.data_ptr(), _ptr(router_bias), _ptr(router_split), _ptr(router_norms),
+            w_gate_up_packed.data_ptr(), w_down.data_ptr(),
             _ptr(shared_gate_up_packed), _ptr(shared_down), y.data_ptr(), w.data_ptr(), ids.data_ptr(),
             t, h, e, i, k, shared, shared_i, ws.data_ptr(), ws.numel(), _vp(_stream(dev)))
     _lib.check("kdb_moe_forward", rc)
@@ -128,7 +172,8 @@ def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tenso
 
 
 @moe.register_fake
-def _moe_fake(x, router, router_bias, w_gate_up_packed, w_down, shared_gate_up_packed, shared_down, k):
+def _moe_fake(x, router, router_bias, router_split, router_norms, w_gate_up_packed, w_down, shared_gate_up_packed,
+              shared_down, k):
     t, h = x.shape
     return (x.new_empty((t, h)), x.new_empty((t, k), dtype=torch.float32), x.new_empty((t, k), dtype=torch.int32))
 
@@ -141,9 +186,13 @@ def prepare(weights: dict, k: int) -> dict:
         raise ValueError("MoE weights must be on a CUDA device")
     sgu = weights.get("shared_gate_up")
     bias = weights.get("router_bias")
+    router = weights["router"].contiguous()
+    split, norms = prepare_router(router) if router.shape[1] % 64 == 0 else (None, None)
     return {
         "k": int(k),
-        "router": weights["router"].contiguous(),
+        "router": router,
+        "router_split": split,
+        "router_norms": norms,
         "router_bias": None if bias is None else bias.to(dev).contiguous(),
         "w_gate_up_packed": pack_gate_up(weights["w_gate_up"].contiguous()),
         "w_down": weights["w_down"].contiguous(),
@@ -153,5 +202,6 @@ def prepare(weights: dict, k: int) -> dict:
 
 
 def forward(x: torch.Tensor, state: dict):
-    return moe(x, state["router"], state["router_bias"], state["w_gate_up_packed"], state["w_down"],
-               state["shared_gate_up_packed"], state["shared_down"], state["k"])
+    return moe(x, state["router"], state["router_bias"], state.get("router_split"), state.get("router_norms"),
+               state["w_gate_up_packed"], state["w_down"], state["shared_gate_up_packed"], state["shared_down"],
+               state["k"])

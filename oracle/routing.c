@@ -14,8 +14,10 @@
  *      logit is the correctly rounded dot product except when the fp64 sum lands within ~2^-29
  *      relative of an fp32 rounding boundary; the fixed order makes the GPU and this oracle agree
  *      bit for bit even then.
- *      Fixed order: 32 partial sums, partial l accumulating h = l, l+32, l+64, ... ascending with
- *      fma; then an xor butterfly over the 32 partials with offsets 16, 8, 4, 2, 1 (p[l] + p[l^o]).
+ *      Fixed order: 32 partial sums; h is cut into blocks of 256 and partial l accumulates, block by
+ *      block in ascending order, the 8 consecutive elements h = 256*b + 8*l + j, j = 0..7 (those below
+ *      H), with fma; then an xor butterfly over the 32 partials with offsets 16, 8, 4, 2, 1
+ *      (p[l] + p[l^o]).  The order lets a GPU lane read 8 consecutive elements (16/32-byte vectors).
  *   2. top-k per token: the k largest logits in descending order; equal logits: lower expert first
  *      (torch.topk on a stable sort, and the `lst` order of x3_h.cu:371-385).
  *   3. permutation: rows grouped by expert (ascending), within an expert by token (ascending);
@@ -36,7 +38,11 @@ static double canon_dot(const uint16_t* x, const float* w, int64_t H) {
   double part[32];
   for (int l = 0; l < 32; ++l) {
     double acc = 0.0;
-    for (int64_t h = l; h < H; h += 32) acc = fma((double)bf16_to_f32(x[h]), (double)w[h], acc);
+    for (int64_t base = 0; base < H; base += 256)
+      for (int j = 0; j < 8; ++j) {
+        const int64_t h = base + 8 * l + j;
+        if (h < H) acc = fma((double)bf16_to_f32(x[h]), (double)w[h], acc);
+      }
     part[l] = acc;
   }
   for (int off = 16; off >= 1; off >>= 1) {

@@ -65,7 +65,7 @@ def test_moe_workspace_and_shape_checks(lib):
     assert lib.kdb_moe_workspace_bytes(64, 4096, 4, 1024, 8, 0, 0) == 0       # k > e
     assert lib.kdb_moe_workspace_bytes(64, 4096, 2048, 1024, 8, 0, 0) == 0    # e > 1024
     vp = ctypes.c_void_p
-    rc = lib.kdb_moe_forward(*([vp(256)] * 10), 64, 4096, 64, 1024, 8, 0, 0, vp(256), 16, None)
+    rc = lib.kdb_moe_forward(*([vp(256)] * 12), 64, 4096, 64, 1024, 8, 0, 0, vp(256), 16, None)
     assert rc == _lib.KDB_ERR_WORKSPACE
     rc = lib.kdb_moe_route(vp(16), vp(16), None, vp(16), vp(16), vp(16), 4, 64, 8, 9, None)
     assert rc == _lib.KDB_ERR_INVALID_ARG

@@ -220,3 +220,63 @@ def test_prefill_full_size_properties():
     ref += state["shared_down"][0].cpu().float() @ h
     c = om.compare(y[t:t + 1].cpu(), ref[None])
     assert c["max_abs"] <= MAX_ABS and c["rel_fro"] <= REL_FRO, c
+
+
+# ------------------------------------------------------------------------------ tensor-core routing path
+def _gamma(h: int) -> float:
+    steps = (2 * h + 15) // 16
+    return 2.0 ** -16 + 1.01 * 17.0 * 2.0 ** -23 * steps + 2.0 ** -20
+
+
+@pytest.mark.parametrize("cfg", [
+    W.MoeConfig("fast_small", 300, 512, 16, 128, 4),
+    W.MoeConfig("fast_odd_e", 200, 640, 37, 128, 8),
+    W.MoeConfig("fast_skew", 4096, 1024, 128, 128, 4, zipf_s=1.2),
+    W.MoeConfig("fast_e256", 1024, 7168, 256, 128, 8),
+    W.MoeConfig("fast_k32", 64, 256, 64, 128, 32),
+])
+def test_fast_route_equals_fixed_order_route(cfg):
+    """ids and weights of the tensor-core path are bitwise those of the full fixed-order router."""
+    x = W.moe_input(cfg.t, cfg.h, 5, device="cuda")
+    router = W._randn((cfg.e, cfg.h), 77, "cuda", 1.0 / cfg.h ** 0.5, torch.float32)
+    bias = W.zipf_router_bias(cfg.e, cfg.zipf_s, 5).cuda() if cfg.zipf_s > 0 else None
+    lg, w0, i0 = M.route(x, router, bias, cfg.k)
+    split, norms = M.prepare_router(router)
+    w1, i1 = M.route_fast(x, router, bias, split, norms, cfg.k)
+    torch.cuda.synchronize()
+    assert torch.equal(i1, i0)
+    assert torch.equal(w1.view(torch.int32), w0.view(torch.int32))
+    rows = torch.arange(0, cfg.t, max(1, cfg.t // 16))
+    olg = om.router_logits(x[rows].cpu(), router.cpu(), None if bias is None else bias.cpu())
+    oids, _ = om.topk(olg, cfg.k)
+    assert torch.equal(i1[rows].cpu(), oids)
+
+
+def test_router_prepass_error_inside_bound():
+    """Prefill-width router (H=7168, E=256): the tensor-core pre-pass stays far inside the bound the
+    candidate selection relies on (the bound allows a worst-case accumulation; measured errors are
+    orders of magnitude smaller)."""
+    T, H, E = 2048, 7168, 256
+    x = W.moe_input(T, H, 6, device="cuda")
+    router = W._randn((E, H), 78, "cuda", 1.0 / H ** 0.5, torch.float32)
+    split, norms = M.prepare_router(router)
+    approx = M.router_approx(x, split)
+    exact = (x.double() @ router.double().T)
+    torch.cuda.synchronize()
+    xn = x.double().norm(dim=1, keepdim=True)
+    assert bool((norms.double() >= router.double().norm(dim=1)).all())
+    delta = _gamma(H) * xn * norms.double().max() * 1.01
+    ratio = float(((approx.double() - exact).abs() / delta).max())
+    assert ratio < 0.05, ratio
+
+
+def test_prefill_fast_and_exact_paths_agree():
+    """The whole prefill routing (T=8192, E=256, H=7168): tensor-core path == fixed-order path."""
+    cfg = W.MOE_CONFIGS["moe_prefill"]
+    x = W.moe_input(cfg.t, cfg.h, 9, device="cuda")
+    router = W._randn((cfg.e, cfg.h), 79, "cuda", 1.0 / cfg.h ** 0.5, torch.float32)
+    _, w0, i0 = M.route(x, router, None, cfg.k)
+    split, norms = M.prepare_router(router)
+    w1, i1 = M.route_fast(x, router, None, split, norms, cfg.k)
+    torch.cuda.synchronize()
+    assert torch.equal(i1, i0) and torch.equal(w1, w0)

@@ -18,24 +18,27 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def _canon_logits_np(x: torch.Tensor, w: torch.Tensor) -> np.ndarray:
-    """The fixed fp64 order of routing.c written with numpy arrays: 32 strided partials
-    (products of bf16 x fp32 are exact in fp64, so a*b + c is one rounding like fma), then the
-    xor butterfly 16, 8, 4, 2, 1, then one rounding to fp32."""
+    """The fixed fp64 order of routing.c written with numpy arrays: 32 partials, partial l taking
+    h = 256*b + 8*l + j (j = 0..7) block by block (products of bf16 x fp32 are exact in fp64, so
+    a*b + c is one rounding like fma), then the xor butterfly 16, 8, 4, 2, 1, then one rounding
+    to fp32."""
     xd = x.float().double().numpy()
     wd = w.double().numpy()
     T, H = xd.shape
     E = wd.shape[0]
     acc = np.zeros((T, E, 32))
-    for base in range(0, H, 32):
-        n = min(32, H - base)
-        acc[:, :, :n] = acc[:, :, :n] + xd[:, None, base:base + n] * wd[None, :, base:base + n]
     lanes = np.arange(32)
+    for base in range(0, H, 256):
+        for j in range(8):
+            hs = base + 8 * lanes + j
+            ok = hs < H
+            acc[:, :, ok] = acc[:, :, ok] + xd[:, None, hs[ok]] * wd[None, :, hs[ok]]
     for off in (16, 8, 4, 2, 1):
         acc = acc + acc[:, :, lanes ^ off]
     return acc[:, :, 0].astype(np.float32)
 
 
-@pytest.mark.parametrize("T,H,E", [(5, 64, 8), (17, 520, 33), (3, 7, 5), (8, 4096, 64)])
+@pytest.mark.parametrize("T,H,E", [(5, 64, 8), (17, 520, 33), (3, 7, 5), (8, 4096, 64), (4, 300, 9)])
 def test_router_logits_fixed_order(T, H, E):
     g = torch.Generator().manual_seed(T * 131 + H)
     x = torch.randn((T, H), generator=g).to(torch.bfloat16)
