@@ -156,6 +156,57 @@ int kdb_moe_route_fast(const void* x, const float* router_w, const float* router
                        const float* router_norms, float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e,
                        int64_t k, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Stage entry points (composition, expert parallelism) ----------------------------------- */
+
+/* out[r, :] = x[index[r] / div, :] for r < rows (x bf16 [t, h], h % 8 == 0); a bad index is reported
+ * in the device status word (KDB_ERR_DEVICE_BOUNDS) and its row is skipped.  With index = perm_slot
+ * and div = k this lays a token batch out in the plan's expert order. */
+int kdb_moe_gather_rows(const void* x, const int32_t* index, int64_t div, void* out, int64_t rows, int64_t h,
+                        int64_t t, void* stream);
+
+/*
+ * Grouped SwiGLU gate_up: for each group g, rows [offsets[g], offsets[g+1]) of a (bf16 [a_rows, h])
+ * times packed w_gate_up[g] (bf16 [2i, h], from kdb_moe_pack_gate_up), epilogue silu(gate) * up ->
+ * out bf16 [a_rows, i].  offsets / mtile_start (int32 [groups + 1], mtile_start = exclusive prefix of
+ * ceil(count / 128), as kdb_moe_plan / kdb_moe_ep_regroup produce) are read on the device; both NULL
+ * means one dense group of a_rows rows.  Counterpart: the gate_up stage + SwiGLU epilogue warp of the
+ * reference engines (okc-challenge/engines/sc_h.cu:164-187, 322-340).
+ */
+int kdb_moe_expert_gate_up(const void* a, int64_t a_rows, const void* w_gate_up_packed, int64_t groups, int64_t i,
+                           int64_t h, const int32_t* offsets, const int32_t* mtile_start, void* out, void* stream);
+
+/*
+ * Grouped down projection: rows of a (bf16 [a_rows, i]) times w_down[g] (bf16 [h, i]) -> out bf16
+ * [a_rows, h], each row scaled by row_scale[row] when row_scale is not NULL.  Grouping as above.
+ * Counterpart: the down stage of the reference engines (sc_h.cu:341-381, x7_h.cu:438-590).
+ */
+int kdb_moe_expert_down(const void* a, int64_t a_rows, const void* w_down, int64_t groups, int64_t i, int64_t h,
+                        const int32_t* offsets, const int32_t* mtile_start, const float* row_scale, void* out,
+                        void* stream);
+
+/*
+ * Weighted combine: y[t] = sum_j (slot_w[t*k+j] or 1) * rows[slot_pos[t*k+j]] (+ shared_rows[t]),
+ * summed in fp32 in slot order (deterministic), bf16 out.  slot_w NULL: rows are already scaled.
+ * Counterpart: the weighted combine of the reference engines (sc_h.cu:374-381).
+ */
+int kdb_moe_combine(const void* rows, const int32_t* slot_pos, const float* slot_w, const void* shared_rows, void* y,
+                    int64_t t, int64_t h, int64_t k, void* stream);
+
+/* Scratch bytes of kdb_moe_ep_regroup. */
+size_t kdb_moe_ep_regroup_workspace_bytes(int64_t p, int64_t er);
+
+/*
+ * Expert-parallel regroup on an expert's owner rank.  counts int32 [p, er] (device): rows received from
+ * source rank s for local expert e.  to_expert_major != 0 copies rows from source-major blocks (s, e)
+ * (the all-to-all receive order) to expert-major order (what the grouped GEMMs read); 0 copies back.
+ * Always writes the expert-major offsets int32 [er + 1] and mtile_start int32 [er + 1]; in/out may
+ * both be NULL for the tables alone.  No host synchronisation.  No counterpart in the reference, whose
+ * engines simulate a single expert-parallel rank (okc_problems/muse_moe_w4a16.toml:136).
+ */
+int kdb_moe_ep_regroup(const int32_t* counts, int64_t p, int64_t er, int to_expert_major, const void* in, void* out,
+                       int64_t h, int32_t* offsets, int32_t* mtile_start, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
 /*
  * The whole layer.  x bf16 [t, h]; y bf16 [t, h]; topk_w fp32 [t, k]; topk_ids int32 [t, k] (the
  * routing outputs the reference's routing problems report at output index 2,

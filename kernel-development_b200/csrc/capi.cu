@@ -146,6 +146,70 @@ int kdb_moe_route_fast(const void* x, const float* router_w, const float* router
                              (int)e, (int)k, workspace, static_cast<cudaStream_t>(stream));
 }
 
+int kdb_moe_gather_rows(const void* x, const int32_t* index, int64_t div, void* out, int64_t rows, int64_t h,
+                        int64_t t, void* stream) {
+  if (rows < 0 || h <= 0 || h % 8 != 0 || t < 0 || div <= 0 || rows > (1ll << 31) || t > (1ll << 31)) return KDB_ERR_INVALID_ARG;
+  if (rows == 0) return KDB_OK;
+  if (!x || !index || !out || !kdb::aligned16(x) || !kdb::aligned16(out)) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_gather_rows(x, index, out, (int)rows, (int)h, (int)t, static_cast<cudaStream_t>(stream), (int)div);
+}
+
+static int expert_gemm_args(const void* a, int64_t a_rows, const void* w, int64_t groups, int64_t i, int64_t h,
+                            const int32_t* offsets, const int32_t* mtile_start, const void* out) {
+  if (a_rows < 0 || groups <= 0 || i <= 0 || h <= 0 || i % 128 != 0 || h % 8 != 0) return KDB_ERR_INVALID_ARG;
+  if ((offsets == nullptr) != (mtile_start == nullptr)) return KDB_ERR_INVALID_ARG;
+  if (!offsets && groups != 1) return KDB_ERR_INVALID_ARG;
+  if (a_rows > (1ll << 30) || groups * 2 * i > (1ll << 31) || groups * h > (1ll << 31)) return KDB_ERR_UNSUPPORTED;
+  if (a_rows == 0) return KDB_OK;
+  if (!a || !w || !out || !kdb::aligned16(a) || !kdb::aligned16(w) || !kdb::aligned16(out)) return KDB_ERR_INVALID_ARG;
+  return -1;   // arguments fine, work to do
+}
+
+int kdb_moe_expert_gate_up(const void* a, int64_t a_rows, const void* w_gate_up_packed, int64_t groups, int64_t i,
+                           int64_t h, const int32_t* offsets, const int32_t* mtile_start, void* out, void* stream) {
+  const int rc = expert_gemm_args(a, a_rows, w_gate_up_packed, groups, i, h, offsets, mtile_start, out);
+  if (rc >= 0) return rc;
+  return kdb::moe_gemm_gate_up(a, (int)a_rows, w_gate_up_packed, (int)groups, (int)i, (int)h, offsets, mtile_start,
+                               out, static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_expert_down(const void* a, int64_t a_rows, const void* w_down, int64_t groups, int64_t i, int64_t h,
+                        const int32_t* offsets, const int32_t* mtile_start, const float* row_scale, void* out,
+                        void* stream) {
+  const int rc = expert_gemm_args(a, a_rows, w_down, groups, i, h, offsets, mtile_start, out);
+  if (rc >= 0) return rc;
+  return kdb::moe_gemm_down(a, (int)a_rows, w_down, (int)groups, (int)i, (int)h, offsets, mtile_start, row_scale, out,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int kdb_moe_combine(const void* rows, const int32_t* slot_pos, const float* slot_w, const void* shared_rows, void* y,
+                    int64_t t, int64_t h, int64_t k, void* stream) {
+  if (t < 0 || h <= 0 || h % 8 != 0 || k <= 0 || k > 32 || t * k > (1ll << 31)) return KDB_ERR_INVALID_ARG;
+  if (t == 0) return KDB_OK;
+  if (!rows || !slot_pos || !y || !kdb::aligned16(rows) || !kdb::aligned16(y)) return KDB_ERR_INVALID_ARG;
+  if (shared_rows && !kdb::aligned16(shared_rows)) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_combine(rows, slot_pos, shared_rows, y, (int)t, (int)h, (int)k, static_cast<cudaStream_t>(stream),
+                          slot_w);
+}
+
+size_t kdb_moe_ep_regroup_workspace_bytes(int64_t p, int64_t er) {
+  if (p <= 0 || er <= 0 || er > 1024 || p > 1024) return 0;
+  return kdb::moe_ep_regroup_scratch_bytes((int)p, (int)er);
+}
+
+int kdb_moe_ep_regroup(const int32_t* counts, int64_t p, int64_t er, int to_expert_major, const void* in, void* out,
+                       int64_t h, int32_t* offsets, int32_t* mtile_start, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (p <= 0 || p > 1024 || er <= 0 || er > 1024 || h <= 0 || h % 8 != 0) return KDB_ERR_INVALID_ARG;
+  if (!counts || !offsets || !mtile_start) return KDB_ERR_INVALID_ARG;
+  if ((in == nullptr) != (out == nullptr)) return KDB_ERR_INVALID_ARG;
+  if (in && (!kdb::aligned16(in) || !kdb::aligned16(out) || in == out)) return KDB_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < kdb::moe_ep_regroup_scratch_bytes((int)p, (int)er)) return KDB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_ep_regroup(counts, (int)p, (int)er, to_expert_major, in, out, (int)h, offsets, mtile_start,
+                             workspace, static_cast<cudaStream_t>(stream));
+}
+
 int kdb_moe_forward(const void* x, const float* router_w, const float* router_bias, const void* router_split,
                     const float* router_norms, const void* w_gate_up_packed,
                     const void* w_down, const void* shared_gate_up_packed, const void* shared_down, void* y,

@@ -6,5 +6,6 @@
 #include "moe_gemm.cu"
 #include "moe_router_fast.cu"
 #include "moe.cu"
+#include "moe_ep.cu"
 #include "moe_noalloc.cu"
 #include "capi.cu"

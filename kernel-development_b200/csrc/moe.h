@@ -10,9 +10,15 @@ int moe_route(const void* x, const float* wr, const float* bias, float* logits, 
 int moe_plan(const int* ids, const float* topk_w, int T, int E, int k, int* chunk_counts, int* chunk_base,
              int* counts, int* offsets, int* mtile_start, int* perm_slot, int* slot_pos, int* perm_token,
              float* perm_w, cudaStream_t s);
-int moe_gather_rows(const void* x, const int* perm_token, void* x_perm, int R, int H, int T, cudaStream_t s);
+int moe_gather_rows(const void* x, const int* perm_token, void* x_perm, int R, int H, int T, cudaStream_t s,
+                    int div = 1);
 int moe_combine(const void* yperm, const int* slot_pos, const void* yshared, void* y, int T, int H, int k,
-                cudaStream_t s);
+                cudaStream_t s, const float* slot_w = nullptr);
+// Expert-parallel regroup (moe_ep.cu): rows held as blocks (source rank s, local expert e) in
+// source-major order <-> expert-major order.  counts: int32 [P, Er] on the device.
+int moe_ep_regroup(const int* counts, int P, int Er, int to_expert_major, const void* in, void* out, int H,
+                   int* offsets, int* mtile_start, void* scratch, cudaStream_t s);
+size_t moe_ep_regroup_scratch_bytes(int P, int Er);
 int moe_pack_gate_up(const void* w, void* packed, int E, int I, int H, cudaStream_t s);
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
                      const int* mtile_start, void* out, cudaStream_t s);

@@ -270,15 +270,15 @@ __global__ void __launch_bounds__(32)
   }
 }
 
-// x_perm[p, :] = x[perm_token[p], :]  (16-byte vectors; H % 8 == 0)
+// x_perm[p, :] = x[perm_token[p] / div, :]  (16-byte vectors; H % 8 == 0)
 __global__ void __launch_bounds__(256)
     moe_gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ perm_token,
-                           __nv_bfloat16* __restrict__ x_perm, int R, int H, int T) {
+                           __nv_bfloat16* __restrict__ x_perm, int R, int H, int T, int div) {
   const int vec_per_row = H / 8;
   const int warps_per_cta = blockDim.x / 32;
   const int row = blockIdx.x * warps_per_cta + (threadIdx.x >> 5);
   if (row >= R) return;
-  const int t = perm_token[row];
+  const int t = perm_token[row] / div;
   if (t < 0 || t >= T) {
     if ((threadIdx.x & 31) == 0) report(KDB_ERR_DEVICE_BOUNDS, 0x202);
     return;
@@ -288,11 +288,11 @@ __global__ void __launch_bounds__(256)
   for (int v = threadIdx.x & 31; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
 }
 
-// y[t, :] = sum_j yperm[slot_pos[t*k + j], :] + sum_s yshared[s][t, :]   (fp32 sum, bf16 out)
+// y[t, :] = sum_j [w[t*k + j] *] yperm[slot_pos[t*k + j], :] + yshared[t, :]   (fp32 sum in slot order, bf16 out)
 __global__ void __launch_bounds__(256)
     moe_combine_kernel(const __nv_bfloat16* __restrict__ yperm, const int* __restrict__ slot_pos,
-                       const __nv_bfloat16* __restrict__ yshared, __nv_bfloat16* __restrict__ y, int T, int H,
-                       int k) {
+                       const float* __restrict__ slot_w, const __nv_bfloat16* __restrict__ yshared,
+                       __nv_bfloat16* __restrict__ y, int T, int H, int k) {
   const int vec_per_row = H / 8;
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long t = gid / vec_per_row;
@@ -306,11 +306,21 @@ __global__ void __launch_bounds__(256)
     if (p < 0) continue;
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(yperm + static_cast<long long>(p) * H) + v);
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+    if (slot_w) {   // rows not yet scaled by their routing weight (expert-parallel path)
+      const float wj = slot_w[t * k + j];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 f = __bfloat1622float2(b[q]);
-      acc[2 * q] += f.x;
-      acc[2 * q + 1] += f.y;
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b[q]);
+        acc[2 * q] = fmaf(wj, f.x, acc[2 * q]);
+        acc[2 * q + 1] = fmaf(wj, f.y, acc[2 * q + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(b[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
     }
   }
   if (yshared) {
@@ -390,19 +400,20 @@ int moe_plan(const int* ids, const float* topk_w, int T, int E, int k, int* chun
   return cuda_status(cudaGetLastError());
 }
 
-int moe_gather_rows(const void* x, const int* perm_token, void* x_perm, int R, int H, int T, cudaStream_t s) {
+int moe_gather_rows(const void* x, const int* perm_token, void* x_perm, int R, int H, int T, cudaStream_t s,
+                    int div) {
   if (R <= 0) return KDB_OK;
   moe_gather_rows_kernel<<<(R + 7) / 8, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), perm_token,
-                                                      static_cast<__nv_bfloat16*>(x_perm), R, H, T);
+                                                      static_cast<__nv_bfloat16*>(x_perm), R, H, T, div);
   return cuda_status(cudaGetLastError());
 }
 
 int moe_combine(const void* yperm, const int* slot_pos, const void* yshared, void* y, int T, int H, int k,
-                cudaStream_t s) {
+                cudaStream_t s, const float* slot_w) {
   if (T <= 0) return KDB_OK;
   const long long threads = static_cast<long long>(T) * (H / 8);
   moe_combine_kernel<<<static_cast<unsigned int>((threads + 255) / 256), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(yperm), slot_pos, static_cast<const __nv_bfloat16*>(yshared),
+      static_cast<const __nv_bfloat16*>(yperm), slot_pos, slot_w, static_cast<const __nv_bfloat16*>(yshared),
       static_cast<__nv_bfloat16*>(y), T, H, k);
   return cuda_status(cudaGetLastError());
 }

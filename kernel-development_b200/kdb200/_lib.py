@@ -44,6 +44,14 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_moe_router_approx": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
     "kdb_moe_route_fast_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
     "kdb_moe_route_fast": (_c_int, [_c_vp] * 7 + [_c_i64] * 4 + [_c_vp, _c_size, _c_vp]),
+    "kdb_moe_gather_rows": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
+    "kdb_moe_expert_gate_up": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "kdb_moe_expert_down": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp,
+                                     _c_vp]),
+    "kdb_moe_combine": (_c_int, [_c_vp] * 5 + [_c_i64] * 3 + [_c_vp]),
+    "kdb_moe_ep_regroup_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
+    "kdb_moe_ep_regroup": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp,
+                                    _c_size, _c_vp]),
     "kdb_moe_forward": (_c_int, [_c_vp] * 12 + [_c_i64] * 7 + [_c_vp, _c_size, _c_vp]),
 }
 

@@ -1,0 +1,137 @@
+"""Expert-parallel fused MoE layer over P ranks (one process per GPU, torch.distributed NCCL).
+
+Rank r owns experts [r*Er, (r+1)*Er) with Er = E / P and its own batch of tokens; the router and the
+shared expert are replicated.  One layer call on rank r:
+
+  1. route its tokens (bit-exact ids and weights: the single-GPU router)           kdb_moe_route_fast
+  2. plan: slots grouped by expert, hence by owner rank                            kdb_moe_plan
+  3. gather the token rows in that order                                           kdb_moe_gather_rows
+  4. all-to-all of the per-(owner, expert) counts, then of the rows (NCCL; the row split sizes are
+     read back to the host once per call, so this path is eager, not graph-captured)
+  5. owner: regroup source-major blocks to expert-major                             kdb_moe_ep_regroup
+  6. owner: grouped gate_up (SwiGLU) and down over its Er experts, unscaled         kdb_moe_expert_*
+  7. owner: regroup back to source-major, all-to-all the rows home
+  8. combine: y[t] = sum_j w[t, j] * row(t, j) (+ shared expert on local tokens)   kdb_moe_combine
+
+The reference simulates a single expert-parallel rank and computes only its local routes
+(src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:31,136); this is the real exchange.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import moe as M
+
+
+class ExpertParallelMoE:
+    """One rank's part of an expert-parallel MoE layer.
+
+    `weights` is the full layer (router fp32 [E, H], w_gate_up [E, 2I, H], w_down [E, H, I], optional
+    router_bias and shared expert) or only this rank's expert slice when `local_experts=True`
+    (w_gate_up/w_down then hold Er experts).  Tensors must be on this rank's GPU.
+    """
+
+    def __init__(self, weights: dict, k: int, group: Optional[dist.ProcessGroup] = None,
+                 local_experts: bool = False, ranks: Optional[tuple[int, int]] = None, ops=None):
+        """`ranks` = (P, rank) places this instance in a P-rank layout without a process group (several
+        instances in one process exchange rows through dispatch / owner_compute / finish).  `ops` is
+        the module of device stages (default kdb200.moe, the libkdb200 kernels); a test harness may pass
+        a stand-in with the same functions to exercise this host logic elsewhere."""
+        self.group = group
+        self.ops = M if ops is None else ops
+        if ranks is not None:
+            self.P, self.rank = int(ranks[0]), int(ranks[1])
+        else:
+            self.P = dist.get_world_size(group) if dist.is_initialized() else 1
+            self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        router = weights["router"].contiguous()
+        self.E = router.shape[0]
+        if self.E % self.P:
+            raise ValueError(f"{self.E} experts do not split over {self.P} ranks")
+        self.Er = self.E // self.P
+        self.k = int(k)
+        gu, dn = weights["w_gate_up"], weights["w_down"]
+        if not local_experts:
+            sl = slice(self.rank * self.Er, (self.rank + 1) * self.Er)
+            gu, dn = gu[sl], dn[sl]
+        if gu.shape[0] != self.Er:
+            raise ValueError(f"expected {self.Er} local experts, got {gu.shape[0]}")
+        self.router = router
+        bias = weights.get("router_bias")
+        self.router_bias = None if bias is None else bias.to(router.device).contiguous()
+        ops = self.ops
+        self.split, self.norms = (ops.prepare_router(router) if router.shape[1] % 64 == 0 else (None, None))
+        self.w_gate_up_packed = ops.pack_gate_up(gu.contiguous())
+        self.w_down = dn.contiguous()
+        sgu = weights.get("shared_gate_up")
+        self.shared_gate_up_packed = None if sgu is None else ops.pack_gate_up(sgu.contiguous())
+        self.shared_down = None if sgu is None else weights["shared_down"].contiguous()
+
+    # -------------------------------------------------------------------------------------------------
+    def _route(self, x: torch.Tensor):
+        if self.split is not None:
+            return self.ops.route_fast(x, self.router, self.router_bias, self.split, self.norms, self.k)
+        _, w, ids = self.ops.route(x, self.router, self.router_bias, self.k)
+        return w, ids
+
+    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
+        if self.P == 1:
+            out.copy_(inp)
+            return
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    # Phases of one call (forward composes them around the two all-to-alls; tests on one GPU emulate
+    # the exchange between several instances).
+    def dispatch(self, x: torch.Tensor) -> dict:
+        """Route this rank's tokens and lay their rows out owner-major.  Returns the call state with
+        send rows [T*k, H] and send_counts int32 [P, Er] (rows for owner p's local expert e)."""
+        w, ids = self._route(x)
+        plan = self.ops.plan(ids, w, self.E)
+        send = self.ops.gather_rows(x, plan["perm_slot"], div=self.k)
+        return {"x": x, "w": w, "ids": ids, "slot_pos": plan["slot_pos"], "send": send,
+                "send_counts": plan["counts"].view(self.P, self.Er)}
+
+    def owner_compute(self, recv: torch.Tensor, recv_counts: torch.Tensor) -> torch.Tensor:
+        """Owner side: rows received source-major (counts int32 [P, Er]) -> expert outputs, unscaled,
+        in the same source-major order."""
+        ops = self.ops
+        grouped, offsets, mtile = ops.ep_regroup(recv_counts, recv, to_expert_major=True)
+        hbuf = ops.expert_gate_up(grouped, self.w_gate_up_packed, offsets, mtile)
+        yg = ops.expert_down(hbuf, self.w_down, offsets, mtile)
+        back, _, _ = ops.ep_regroup(recv_counts, yg, to_expert_major=False)
+        return back
+
+    def finish(self, st: dict, ret: torch.Tensor):
+        """Weighted combine of the returned rows (+ shared expert on the local tokens)."""
+        x = st["x"]
+        T = x.shape[0]
+        shared = None
+        if self.shared_gate_up_packed is not None:
+            hs = self.ops.expert_gate_up(x, self.shared_gate_up_packed[0:1])
+            shared = self.ops.expert_down(hs, self.shared_down[0:1])
+        y = self.ops.combine(ret, st["slot_pos"], T, self.k, slot_w=st["w"], shared_rows=shared)
+        return y, st["w"], st["ids"]
+
+    def forward(self, x: torch.Tensor):
+        """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32)."""
+        T, H = x.shape
+        st = self.dispatch(x)
+        send_counts = st["send_counts"]
+        recv_counts = torch.empty_like(send_counts)
+        if self.P > 1:
+            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        else:
+            recv_counts.copy_(send_counts)
+        both = torch.stack([send_counts.sum(1), recv_counts.sum(1)]).cpu()    # the one host read-back
+        send_rows, recv_rows = both[0].tolist(), both[1].tolist()
+        recv = torch.empty((int(sum(recv_rows)), H), dtype=st["send"].dtype, device=x.device)
+        self._all_to_all(recv, st["send"], recv_rows, send_rows)
+        back = self.owner_compute(recv, recv_counts)
+        ret = torch.empty((T * self.k, H), dtype=back.dtype, device=x.device)
+        self._all_to_all(ret, back, send_rows, recv_rows)
+        return self.finish(st, ret)
+
+    __call__ = forward

@@ -205,3 +205,73 @@ def forward(x: torch.Tensor, state: dict):
     return moe(x, state["router"], state["router_bias"], state.get("router_split"), state.get("router_norms"),
                state["w_gate_up_packed"], state["w_down"], state["shared_gate_up_packed"], state["shared_down"],
                state["k"])
+
+
+# ------------------------------------------------------------------------------------ stage entry points
+def gather_rows(x: torch.Tensor, index: torch.Tensor, div: int = 1, rows: Optional[int] = None) -> torch.Tensor:
+    """out[r] = x[index[r] // div] (bf16 rows)."""
+    _need("x", x, torch.bfloat16, 2)
+    n = index.numel() if rows is None else int(rows)
+    out = torch.empty((n, x.shape[1]), dtype=torch.bfloat16, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().kdb_moe_gather_rows(x.data_ptr(), index.data_ptr(), div, out.data_ptr(), n, x.shape[1],
+                                            x.shape[0], _vp(_stream(x.device)))
+    _lib.check("kdb_moe_gather_rows", rc)
+    return out
+
+
+def expert_gate_up(a: torch.Tensor, w_packed: torch.Tensor, offsets: Optional[torch.Tensor] = None,
+                   mtile_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped gate_up + SwiGLU: a bf16 [R, H] (rows grouped as offsets say) -> bf16 [R, I]."""
+    groups, two_i, h = w_packed.shape
+    out = torch.empty((a.shape[0], two_i // 2), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        rc = _lib.lib().kdb_moe_expert_gate_up(a.data_ptr(), a.shape[0], w_packed.data_ptr(), groups, two_i // 2, h,
+                                               _ptr(offsets), _ptr(mtile_start), out.data_ptr(), _vp(_stream(a.device)))
+    _lib.check("kdb_moe_expert_gate_up", rc)
+    return out
+
+
+def expert_down(a: torch.Tensor, w_down: torch.Tensor, offsets: Optional[torch.Tensor] = None,
+                mtile_start: Optional[torch.Tensor] = None, row_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped down projection: a bf16 [R, I] -> bf16 [R, H] (rows scaled by row_scale when given)."""
+    groups, h, i = w_down.shape
+    out = torch.empty((a.shape[0], h), dtype=torch.bfloat16, device=a.device)
+    with torch.cuda.device(a.device):
+        rc = _lib.lib().kdb_moe_expert_down(a.data_ptr(), a.shape[0], w_down.data_ptr(), groups, i, h, _ptr(offsets),
+                                            _ptr(mtile_start), _ptr(row_scale), out.data_ptr(), _vp(_stream(a.device)))
+    _lib.check("kdb_moe_expert_down", rc)
+    return out
+
+
+def combine(rows: torch.Tensor, slot_pos: torch.Tensor, t: int, k: int, slot_w: Optional[torch.Tensor] = None,
+            shared_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[t] = sum_j (slot_w or 1) * rows[slot_pos[t*k + j]] (+ shared_rows[t]) in fp32, bf16 out."""
+    h = rows.shape[1] if rows.dim() == 2 else shared_rows.shape[1]
+    y = torch.empty((t, h), dtype=torch.bfloat16, device=slot_pos.device)
+    with torch.cuda.device(slot_pos.device):
+        rc = _lib.lib().kdb_moe_combine(rows.data_ptr(), slot_pos.data_ptr(), _ptr(slot_w), _ptr(shared_rows),
+                                        y.data_ptr(), t, h, k, _vp(_stream(slot_pos.device)))
+    _lib.check("kdb_moe_combine", rc)
+    return y
+
+
+def ep_regroup(counts: torch.Tensor, rows_in: Optional[torch.Tensor], to_expert_major: bool,
+               rows_out: Optional[torch.Tensor] = None):
+    """Block transpose between source-major (s, e) and expert-major rows for counts int32 [P, Er];
+    returns (rows_out, offsets [Er + 1], mtile_start [Er + 1])."""
+    p, er = counts.shape
+    dev = counts.device
+    offsets = torch.empty(er + 1, dtype=torch.int32, device=dev)
+    mtile = torch.empty(er + 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(max(int(_lib.lib().kdb_moe_ep_regroup_workspace_bytes(p, er)), 256), dtype=torch.uint8,
+                     device=dev)
+    if rows_in is not None and rows_out is None:
+        rows_out = torch.empty_like(rows_in)
+    h = rows_in.shape[1] if rows_in is not None else 8
+    with torch.cuda.device(dev):
+        rc = _lib.lib().kdb_moe_ep_regroup(counts.data_ptr(), p, er, 1 if to_expert_major else 0, _ptr(rows_in),
+                                           _ptr(rows_out), h, offsets.data_ptr(), mtile.data_ptr(), ws.data_ptr(),
+                                           ws.numel(), _vp(_stream(dev)))
+    _lib.check("kdb_moe_ep_regroup", rc)
+    return rows_out, offsets, mtile
