@@ -12,7 +12,8 @@ A step is one pass of the op over one batch already resident in HBM, replayed fr
 The L2 is flushed (a 512 MiB device write, untimed) before every timed step; each step is timed
 with CUDA events on its own stream; the time is the max over ranks.  At N > 1 the projection is
 column-parallel with N·7168 global output columns (each rank its own 7168-column shard, no
-collective: weak scaling); the MoE layer runs as N replicas until the expert-parallel path lands.
+collective: weak scaling); the MoE layer runs expert-parallel (E/N experts and T tokens per GPU, NCCL
+all-to-all dispatch and combine: weak scaling).
 
 --impl reference times the oracle (the CPU restatement of the same math) on this host's cores on a
 bounded sample of the workload, and prints the same line with "impl": "reference".
@@ -353,19 +354,38 @@ def bench_moe(args, dist: Dist) -> dict | None:
     dev = torch.device("cuda", dist.local)
     torch.cuda.set_device(dev)
     x = W.moe_input(cfg.t, cfg.h, seed=1 + dist.rank, device=dev)
-    wts = W.moe_weights(cfg, seed=1, device=dev)
-    state = M.prepare(wts, cfg.k)
-    del wts
-    torch.cuda.empty_cache()
     flush = _flusher(dev)
     holder = {}
-
-    def step():
-        holder["out"] = M.forward(x, state)
-
-    g = _capture(step)
     sampler = ClockSampler(_physical_index(dist.local)) if dist.rank == 0 else None
-    per_step, region_ms = timed_steps(g.replay, args.steps, args.warmup, flush, dist, sampler)
+    ep = dist.world > 1
+    if ep:
+        # Expert parallel: this rank's T tokens, its E/P experts; rows cross NVLink by NCCL all-to-all.
+        from kdb200 import ep as EP
+        er = cfg.e // dist.world
+        wts = W.moe_weights(cfg, seed=1, device=dev, experts=range(dist.rank * er, (dist.rank + 1) * er))
+        layer = EP.ExpertParallelMoE(wts, cfg.k, local_experts=True)
+        del wts
+        torch.cuda.empty_cache()
+
+        def step():
+            holder["out"] = layer(x)
+
+        run_step = step
+        forward = layer
+    else:
+        wts = W.moe_weights(cfg, seed=1, device=dev)
+        state = M.prepare(wts, cfg.k)
+        del wts
+        torch.cuda.empty_cache()
+
+        def step():
+            holder["out"] = M.forward(x, state)
+
+        run_step = _capture(step).replay
+
+        def forward(xx):
+            return M.forward(xx, state)
+    per_step, region_ms = timed_steps(run_step, args.steps, args.warmup, flush, dist, sampler)
     ms = dist.max(statistics.mean(per_step))
     value = cfg.t * dist.world / (ms * 1e-3)
     ids = holder["out"][2]
@@ -379,7 +399,7 @@ def bench_moe(args, dist: Dist) -> dict | None:
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        y, w, i = M.forward(x_dev, state)
+        y, w, i = forward(x_dev)
         y_host.copy_(y, non_blocking=True)
         w_host.copy_(w, non_blocking=True)
         i_host.copy_(i, non_blocking=True)
@@ -389,8 +409,8 @@ def bench_moe(args, dist: Dist) -> dict | None:
     if dist.rank != 0:
         return None
     peaks = _peaks()
-    flops = W.moe_flops(cfg)
-    nbytes = W.moe_bytes(cfg, distinct)
+    flops = W.moe_flops(cfg)                   # per rank: T tokens' routed work (weak scaling under EP)
+    nbytes = W.moe_bytes(cfg, cfg.e // dist.world if ep else distinct)
     t_c = flops / (peaks["bf16_tflops_sustained"] * 1e12)
     t_m = nbytes / (peaks["hbm_gbs"] * 1e9)
     layer_s = statistics.mean(per_step) * 1e-3
@@ -406,20 +426,30 @@ def bench_moe(args, dist: Dist) -> dict | None:
     roof.update({"traffic": None, "peak_source": f"{peaks['source']} (sustained for tensor)",
                  "kernel": "whole layer (route, plan, gather, grouped gate_up, grouped down, combine)",
                  "layer_roofline_ms": round(max(t_c, t_m) * 1e3, 4)})
-    launches = 9 + (2 if cfg.shared else 0)
+    # ours per step: router pre-pass GEMM, candidates, exact top-k; plan (3); gather; [EP: 2 regroups of
+    # 2 kernels]; grouped gate_up; grouped down; [shared gate_up + down]; combine
+    launches = 10 + (4 if ep else 0) + (2 if cfg.shared else 0)
+    if ep:
+        par = (f"expert-parallel over {dist.world} GPUs ({cfg.e // dist.world} experts each, NCCL all-to-all "
+               "dispatch and combine, weak scaling: T tokens per GPU)")
+        graph = "eager (row split sizes read back to the host once per call)"
+        path = "kdb200.ep.ExpertParallelMoE -> kdb_moe_* stage entry points + NCCL all_to_all_single"
+    else:
+        par, graph = "1 GPU", "CUDA graph replay per step"
+        path = "kdb200.moe.forward (kdev kernel_fn path) -> kdb_moe_forward"
     return {
         "metric": "MoE layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; x~N(0,1) bf16, router N(0,1/H) fp32, experts N(0,1/fan_in) bf16)",
         "config": {"workload": args.workload, **cfg.as_case(), "distinct_experts_hit": distinct,
-                   "parallelism": f"{dist.world} independent replica(s)",
+                   "parallelism": par,
                    "l2": "flushed before every timed step (512 MiB device write, untimed)",
-                   "graph": "CUDA graph replay per step"},
+                   "graph": graph},
         "e2e": {"value": round(cfg.t * dist.world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": cfg.t * cfg.h * 2,
                 "d2h_bytes_per_step": cfg.t * cfg.h * 2 + cfg.t * cfg.k * 8,
-                "path": "kdb200.moe.forward (kdev kernel_fn path) -> kdb_moe_forward",
+                "path": path,
                 "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": launches * args.steps,
         "roofline": roof,

@@ -135,22 +135,25 @@ def zipf_router_bias(e: int, s: float, seed: int = 0) -> torch.Tensor:
     return (-s * tau * torch.log(ranks)).to(torch.float32)
 
 
-def moe_weights(cfg: MoeConfig, seed: int = 0, device="cpu") -> dict:
+def moe_weights(cfg: MoeConfig, seed: int = 0, device="cpu", experts: range | None = None) -> dict:
     """Layer weights.  w_gate_up[e] = [gate rows (I); up rows (I)] x H, w_down[e] = H x I.
 
     Keys: router fp32[E, H], router_bias fp32[E] or None, w_gate_up bf16[E, 2I, H],
     w_down bf16[E, H, I], shared_gate_up bf16[S, 2Is, H] or None, shared_down bf16[S, H, Is] or None.
-    Expert tensors are drawn expert by expert so that no fp32 copy of a whole stack is ever held."""
+    Expert tensors are drawn expert by expert (each from its own seed) so that no fp32 copy of a
+    whole stack is ever held; `experts` restricts them to a range (an expert-parallel rank's slice,
+    equal to that slice of the full layer)."""
     E, H, I = cfg.e, cfg.h, cfg.i
+    ex = range(E) if experts is None else experts
     out = {
         "router": _randn((E, H), seed * 1000 + _TID_ROUTER, device, 1.0 / math.sqrt(H), torch.float32),
         "router_bias": zipf_router_bias(E, cfg.zipf_s, seed).to(device) if cfg.zipf_s > 0 else None,
     }
-    gu = torch.empty((E, 2 * I, H), dtype=torch.bfloat16, device=device)
-    dn = torch.empty((E, H, I), dtype=torch.bfloat16, device=device)
-    for e in range(E):
-        gu[e] = _randn((2 * I, H), (seed * 1000 + _TID_GU) * 4096 + e, device, 1.0 / math.sqrt(H))
-        dn[e] = _randn((H, I), (seed * 1000 + _TID_DOWN) * 4096 + e, device, 1.0 / math.sqrt(I))
+    gu = torch.empty((len(ex), 2 * I, H), dtype=torch.bfloat16, device=device)
+    dn = torch.empty((len(ex), H, I), dtype=torch.bfloat16, device=device)
+    for j, e in enumerate(ex):
+        gu[j] = _randn((2 * I, H), (seed * 1000 + _TID_GU) * 4096 + e, device, 1.0 / math.sqrt(H))
+        dn[j] = _randn((H, I), (seed * 1000 + _TID_DOWN) * 4096 + e, device, 1.0 / math.sqrt(I))
     out["w_gate_up"], out["w_down"] = gu, dn
     if cfg.shared:
         Is = cfg.shared_i
