@@ -63,7 +63,7 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream);
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream);
 
-/* As kdb_proj_bf16 with the output tile width forced to 64, 128 or 256 (0 = automatic). */
+/* As kdb_proj_bf16 with the output tile width forced to 64, 128, 192, 224 or 256 (0 = automatic). */
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                       int tile_n, void* stream);
 

@@ -1,50 +1,55 @@
-// moe_gemm.cu — grouped expert GEMMs of the MoE layer on the persistent tcgen05 core.
+// moe_gemm.cu — grouped expert GEMMs of the MoE layer on the persistent tcgen05 core with swapped
+// operands (gemm_swap_sm100.cuh: weights as M, each expert's tokens as N rounded up to 16).
 //
-//   gate_up:  H_e = X_perm[rows of e] · Wgu_e(packed)ᵀ, epilogue silu(gate) * up -> bf16 intermediate
-//   down:     Y_e = H[rows of e] · Wd_eᵀ,  epilogue * routing weight of the row -> bf16 per-slot rows
+//   gate_up:  H_e = silu(X_e · Wg_eᵀ) * (X_e · Wu_eᵀ) -> bf16 intermediate; one tile = 128 gate rows and
+//             the matching 128 up rows of the packed weights against <= 128 token rows
+//   down:     Y_e = H_e · Wd_eᵀ (* routing weight of the row) -> bf16; one tile = 256 output features
+//             against <= 128 token rows
 //
 // The tile schedule is read on the device from the routing plan (offsets[g], mtile_start[g]), so no
 // host synchronisation separates routing from the GEMMs and the whole layer is graph-capturable.
-// Tiles are ordered group-major, then by N-tile, with M-tiles fastest: the tiles in flight at once
-// share an expert's weight tiles in L2.
+// Tiles are ordered expert-major, then by weight tile, with token tiles fastest: the tiles in flight
+// at once share an expert's weight tiles in L2.
 //
 // Reference counterparts: the gate_up stage + SwiGLU epilogue warp of the H200 engines
 // (okc-challenge/engines/sc_h.cu:164-187, 322-340) and their down stage + weighted output
 // (sc_h.cu:341-381, x7_h.cu:438-590), which stream NVFP4 weights through mma.sync.
 #include "gemm_sm100.cuh"
+#include "gemm_swap_sm100.cuh"
 #include "host_util.h"
 #include "moe.h"
 
 namespace kdb {
 
-struct GroupTile {
-  int a_row, b_row, nkb, a_kwrap;
-  int row0, valid, n0;
+// ---------------------------------------------------------------------------------------------------
+// Swapped-operand grouped schedule: tiles (group g, weight tile f, token tile tt), tt fastest.
+struct SwapTile {
+  int a_row, a_part_stride, b_row, nkb, n_valid;
+  int f0, row0;
 };
 
-template <int BM, int BN>
-struct GroupSched {
+struct SwapSched {
   struct Params {
-    const int* offsets;       // [groups + 1] row offsets, or null: one dense group of `rows` rows
-    const int* mtile_start;   // [groups + 1] exclusive prefix of ceil(count / BM), or null
-    int groups, rows, n_tiles, nkb;
-    int b_rows_per_group;     // B row of (group g, n-tile nb) = g * b_rows_per_group + nb * BN
+    const int* offsets;       // [groups + 1] token-row offsets, or null: one dense group of `rows` rows
+    const int* mtile_start;   // [groups + 1] exclusive prefix of ceil(count / 128), or null
+    int groups, rows, f_tiles, nkb;
+    int a_rows_per_group;     // weight rows of one group
+    int a_tile_rows;          // weight rows one tile spans (two 128-row parts)
+    int f_step;               // feature index advance per weight tile
   };
   Params p;
   int total_mt;
-  __device__ explicit GroupSched(const Params& pp) : p(pp) {
-    total_mt = p.mtile_start ? p.mtile_start[p.groups] : (p.rows + BM - 1) / BM;
+  __device__ explicit SwapSched(const Params& pp) : p(pp) {
+    total_mt = p.mtile_start ? p.mtile_start[p.groups] : (p.rows + 127) / 128;
   }
-  __device__ int num_tiles() const { return total_mt * p.n_tiles; }
-  __device__ GroupTile tile(int t) const {
-    GroupTile ti;
+  __device__ int num_tiles() const { return total_mt * p.f_tiles; }
+  __device__ SwapTile tile(int t) const {
     int g = 0, mstart = 0, mcount = total_mt, row_begin = 0, count = p.rows;
     if (p.mtile_start) {
-      // largest g with mtile_start[g] * n_tiles <= t (empty groups share their successor's start)
       int lo = 0, hi = p.groups - 1;
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (__ldg(p.mtile_start + mid) * p.n_tiles <= t) lo = mid;
+        if (__ldg(p.mtile_start + mid) * p.f_tiles <= t) lo = mid;
         else hi = mid - 1;
       }
       g = lo;
@@ -53,91 +58,80 @@ struct GroupSched {
       row_begin = __ldg(p.offsets + g);
       count = __ldg(p.offsets + g + 1) - row_begin;
     }
-    const int local = t - mstart * p.n_tiles;
-    const int nb = local / mcount;
-    const int mt = local - nb * mcount;
-    ti.row0 = row_begin + mt * BM;
-    ti.valid = min(BM, count - mt * BM);
-    ti.n0 = nb * BN;
-    ti.a_row = ti.row0;
-    ti.b_row = g * p.b_rows_per_group + nb * BN;
+    const int local = t - mstart * p.f_tiles;
+    const int f = local / mcount;
+    const int tt = local - f * mcount;
+    SwapTile ti;
+    ti.row0 = row_begin + tt * 128;
+    ti.n_valid = min(128, count - tt * 128);
+    ti.b_row = ti.row0;
+    ti.a_row = g * p.a_rows_per_group + f * p.a_tile_rows;
+    ti.a_part_stride = 128;
+    ti.f0 = f * p.f_step;
     ti.nkb = p.nkb;
-    ti.a_kwrap = 0;
     return ti;
   }
 };
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_swap(float g) { return g / (1.0f + __expf(-g)); }
 
-// BN = 256 tile of the packed gate_up weights: TMEM columns [0, 128) hold gate rows j0..j0+127 and
-// [128, 256) the up rows of the same j, so each thread computes silu(g) * u for 128 outputs.
-struct SwigluEpi {
+// gate_up: accumulator part 0 = gate rows f0..f0+127, part 1 = the up rows of the same features.
+struct SwigluSwapEpi {
   struct Params {
-    __nv_bfloat16* out;   // [rows, ld_out]
+    __nv_bfloat16* out;   // [rows, ld_out] intermediate
     int ld_out;
   };
-  __device__ static void run(const Params& p, const GroupTile& ti, int r, uint32_t taddr) {
-    const bool ok = r < ti.valid;
-    __nv_bfloat16* orow = p.out + static_cast<long long>(ti.row0 + r) * p.ld_out + ti.n0 / 2;
+  template <int NB>
+  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
+    __nv_bfloat16* col = p.out + ti.f0 + r;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
       uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(taddr + c * 32, g);
-      tmem_ld_32x32b_x32(taddr + 128 + c * 32, u);
+      tmem_ld_32x32b_x32(taddr + c0, g);
+      tmem_ld_32x32b_x32(taddr + NB + c0, u);
       tmem_ld_wait();
-      if (!ok) continue;
-      uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+      const int n = min(32, ti.n_valid - c0);
+      __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float h[8];
-#pragma unroll
-        for (int z = 0; z < 8; ++z) h[z] = silu_f(__uint_as_float(g[q * 8 + z])) * __uint_as_float(u[q * 8 + z]);
-        uint4 o;
-        o.x = pack_bf16x2(h[0], h[1]);
-        o.y = pack_bf16x2(h[2], h[3]);
-        o.z = pack_bf16x2(h[4], h[5]);
-        o.w = pack_bf16x2(h[6], h[7]);
-        dst[q] = o;
-      }
+      for (int i = 0; i < 32; ++i)
+        if (i < n)
+          dst[static_cast<long long>(i) * p.ld_out] =
+              __float2bfloat16_rn(silu_swap(__uint_as_float(g[i])) * __uint_as_float(u[i]));
     }
   }
 };
 
-// Down projection: each output row is scaled by its routing weight (1 when row_scale is null).
-template <int BN>
-struct ScaleEpi {
+// down: accumulator parts 0 and 1 = output features f0..f0+127 and f0+128..f0+255, each token row
+// scaled by its routing weight (1 when row_scale is null).
+struct ScaleSwapEpi {
   struct Params {
     __nv_bfloat16* out;       // [rows, ld_out]
     const float* row_scale;   // [rows] or null
     int ld_out;
-    int n_total;              // valid output columns
+    int n_total;              // valid output features
   };
-  __device__ static void run(const Params& p, const GroupTile& ti, int r, uint32_t taddr) {
-    const bool ok = r < ti.valid;
-    const int row = ti.row0 + r;
-    const float sc = (ok && p.row_scale) ? __ldg(p.row_scale + row) : 1.0f;
-    __nv_bfloat16* orow = p.out + static_cast<long long>(row) * p.ld_out;
+  template <int NB>
+  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(taddr + c * 32, v);
-      tmem_ld_wait();
-      const int col0 = ti.n0 + c * 32;
-      if (!ok || col0 >= p.n_total) continue;
-      if (col0 + 32 <= p.n_total) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+    for (int a = 0; a < 2; ++a) {
+      const int feat = ti.f0 + a * 128 + r;
+      const bool ok = feat < p.n_total;
+      __nv_bfloat16* col = p.out + feat;
+#pragma unroll 1
+      for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + a * NB + c0, v);
+        tmem_ld_wait();
+        const int n = min(32, ti.n_valid - c0);
+        if (!ok) continue;
+        __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 o;
-          o.x = pack_bf16x2(__uint_as_float(v[q * 8 + 0]) * sc, __uint_as_float(v[q * 8 + 1]) * sc);
-          o.y = pack_bf16x2(__uint_as_float(v[q * 8 + 2]) * sc, __uint_as_float(v[q * 8 + 3]) * sc);
-          o.z = pack_bf16x2(__uint_as_float(v[q * 8 + 4]) * sc, __uint_as_float(v[q * 8 + 5]) * sc);
-          o.w = pack_bf16x2(__uint_as_float(v[q * 8 + 6]) * sc, __uint_as_float(v[q * 8 + 7]) * sc);
-          dst[q] = o;
+        for (int i = 0; i < 32; ++i) {
+          if (i < n) {
+            const float sc = p.row_scale ? __ldg(p.row_scale + ti.row0 + c0 + i) : 1.0f;
+            dst[static_cast<long long>(i) * p.ld_out] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
+          }
         }
-      } else {
-        for (int j = 0; j < 32 && col0 + j < p.n_total; ++j)
-          orow[col0 + j] = __float2bfloat16_rn(__uint_as_float(v[j]) * sc);
       }
     }
   }
@@ -156,77 +150,77 @@ static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
   return KDB_OK;
 }
 
-constexpr int kGroupBM = 128, kGroupBN = 256, kGroupStages = 4;
+static int make_token_maps(TokenMaps* m, const void* rows, uint64_t n_rows, uint64_t k) {
+  for (int i = 0; i < 5; ++i) {
+    const int rc = make_tmap_bf16_2d(&m->m[i], rows, k, n_rows, k, kBK, 16u << i);
+    if (rc) return rc;
+  }
+  return KDB_OK;
+}
 
-int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
-                     const int* mtile_start, void* out, cudaStream_t s) {
-  using L = GemmLayout<kGroupBM, kGroupBN, kGroupStages>;
-  using Sched = GroupSched<kGroupBM, kGroupBN>;
-  auto kern = gemm_tn_kernel<Sched, SwigluEpi, kGroupBM, kGroupBN, kGroupStages>;
+constexpr int kSwapMA = 2, kSwapNB = 128, kSwapStages = 4;
+
+template <class Epi>
+static int launch_swap(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
+                       const SwapSched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
+  using L = SwapLayout<kSwapMA, kSwapNB, kSwapStages>;
+  auto kern = gemm_swap_kernel<SwapSched, Epi, kSwapMA, kSwapNB, kSwapStages>;
   static bool done[64] = {false};
   int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
   if (rc) return rc;
-  if (a_rows <= 0) return KDB_OK;
-  CUtensorMap ta, tb;
-  rc = make_tmap_bf16_2d(&ta, a, H, a_rows, H, kBK, kGroupBM);
+  CUtensorMap ta;
+  TokenMaps tb;
+  rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, 128);
   if (rc) return rc;
-  rc = make_tmap_bf16_2d(&tb, w_packed, H, static_cast<uint64_t>(groups) * 2 * I, H, kBK, kGroupBN);
+  rc = make_token_maps(&tb, tokens, a_rows, K);
   if (rc) return rc;
-  Sched::Params sp;
-  sp.offsets = offsets;
-  sp.mtile_start = mtile_start;
-  sp.groups = groups;
-  sp.rows = a_rows;
-  sp.n_tiles = (2 * I) / kGroupBN;
-  sp.nkb = (H + kBK - 1) / kBK;
-  sp.b_rows_per_group = 2 * I;
-  SwigluEpi::Params ep;
-  ep.out = static_cast<__nv_bfloat16*>(out);
-  ep.ld_out = I;
   int grid = num_sms();
-  if (!mtile_start) {
-    const int tiles = ((a_rows + kGroupBM - 1) / kGroupBM) * sp.n_tiles;
+  if (!sp.mtile_start) {
+    const int tiles = ((a_rows + 127) / 128) * sp.f_tiles;
     grid = tiles < grid ? tiles : grid;
   }
   kern<<<grid, kGemmThreads, L::kSmemBytes, s>>>(ta, tb, sp, ep);
   return cuda_status(cudaGetLastError());
 }
 
-int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
-                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s) {
-  using L = GemmLayout<kGroupBM, kGroupBN, kGroupStages>;
-  using Sched = GroupSched<kGroupBM, kGroupBN>;
-  using Epi = ScaleEpi<kGroupBN>;
-  auto kern = gemm_tn_kernel<Sched, Epi, kGroupBM, kGroupBN, kGroupStages>;
-  static bool done[64] = {false};
-  int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
-  if (rc) return rc;
+int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
+                     const int* mtile_start, void* out, cudaStream_t s) {
   if (a_rows <= 0) return KDB_OK;
-  CUtensorMap ta, tb;
-  rc = make_tmap_bf16_2d(&ta, a, I, a_rows, I, kBK, kGroupBM);
-  if (rc) return rc;
-  rc = make_tmap_bf16_2d(&tb, w_down, I, static_cast<uint64_t>(groups) * H, I, kBK, kGroupBN);
-  if (rc) return rc;
-  Sched::Params sp;
+  SwapSched::Params sp;
   sp.offsets = offsets;
   sp.mtile_start = mtile_start;
   sp.groups = groups;
   sp.rows = a_rows;
-  sp.n_tiles = (H + kGroupBN - 1) / kGroupBN;
+  sp.f_tiles = I / 128;               // 128 intermediate features (256 packed weight rows) per tile
+  sp.nkb = (H + kBK - 1) / kBK;
+  sp.a_rows_per_group = 2 * I;
+  sp.a_tile_rows = 256;
+  sp.f_step = 128;
+  SwigluSwapEpi::Params ep;
+  ep.out = static_cast<__nv_bfloat16*>(out);
+  ep.ld_out = I;
+  return launch_swap<SwigluSwapEpi>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp, ep, s);
+}
+
+int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
+                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s) {
+  if (a_rows <= 0) return KDB_OK;
+  SwapSched::Params sp;
+  sp.offsets = offsets;
+  sp.mtile_start = mtile_start;
+  sp.groups = groups;
+  sp.rows = a_rows;
+  sp.f_tiles = (H + 255) / 256;       // 256 output features per tile
   sp.nkb = (I + kBK - 1) / kBK;
-  sp.b_rows_per_group = H;
-  Epi::Params ep;
+  sp.a_rows_per_group = H;
+  sp.a_tile_rows = 256;
+  sp.f_step = 256;
+  ScaleSwapEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(out);
   ep.row_scale = row_scale;
   ep.ld_out = H;
   ep.n_total = H;
-  int grid = num_sms();
-  if (!mtile_start) {
-    const int tiles = ((a_rows + kGroupBM - 1) / kGroupBM) * sp.n_tiles;
-    grid = tiles < grid ? tiles : grid;
-  }
-  kern<<<grid, kGemmThreads, L::kSmemBytes, s>>>(ta, tb, sp, ep);
-  return cuda_status(cudaGetLastError());
+  return launch_swap<ScaleSwapEpi>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep, s);
 }
 
 }  // namespace kdb

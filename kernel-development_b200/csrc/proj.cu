@@ -139,6 +139,36 @@ static int launch_proj_cfg(const void* x, const void* w, void* y, int M, int N, 
   return cuda_status(cudaGetLastError());
 }
 
+// Output tile width.  A persistent grid runs ceil(tiles / SMs) rounds of tiles, so the tile count's
+// remainder idles SMs in the last round (896 tiles of 128 x 256 on 148 SMs: 6.05 rounds, 7 paid); a
+// narrower tile can fill the last round.  Score = wave efficiency x column efficiency x a per-width
+// factor for the operand traffic per FLOP of narrower tiles; with fewer tiles than SMs, the widest
+// width that still gives every SM a tile (weight-streaming shapes).
+int pick_tile_n(long long M, long long N, long long sms) {
+  const long long mb = (M + 127) / 128;
+  if (mb * ((N + 255) / 256) < sms) {
+    if (mb * ((N + 127) / 128) >= sms) return 128;
+    return 64;
+  }
+  static const int widths[4] = {256, 224, 192, 128};
+  static const double tile_eff[4] = {1.0, 0.985, 0.965, 0.85};
+  int best = 256;
+  double best_score = -1.0;
+  for (int i = 0; i < 4; ++i) {
+    const long long nb = (N + widths[i] - 1) / widths[i];
+    const long long tiles = mb * nb;
+    const long long rounds = (tiles + sms - 1) / sms;
+    const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * sms);
+    const double cols = static_cast<double>(N) / static_cast<double>(nb * widths[i]);
+    const double score = wave * cols * tile_eff[i];
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = widths[i];
+    }
+  }
+  return best;
+}
+
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
               int force_bn, cudaStream_t stream) {
   if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
@@ -154,16 +184,11 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
   if (K % 8 != 0 || !aligned16(x) || !aligned16(w)) return KDB_ERR_INVALID_ARG;
 
   int bn = force_bn;
-  if (bn == 0) {
-    // Widest tile that still gives every SM a tile; narrower tiles for weight-streaming shapes.
-    const long long sms = num_sms();
-    const long long mb = (M + 127) / 128;
-    if (mb * ((N + 255) / 256) >= sms) bn = 256;
-    else if (mb * ((N + 127) / 128) >= sms) bn = 128;
-    else bn = 64;
-  }
+  if (bn == 0) bn = pick_tile_n(M, N, num_sms());
   switch (bn) {
     case 256: return launch_proj_cfg<256, 4>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+    case 224: return launch_proj_cfg<224, 5>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+    case 192: return launch_proj_cfg<192, 5>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
     case 128: return launch_proj_cfg<128, 6>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
     case 64: return launch_proj_cfg<64, 8>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
     default: return KDB_ERR_INVALID_ARG;

@@ -65,6 +65,9 @@ MOE_CONFIGS = {
     "moe_decode": MoeConfig("moe_decode", 64, 4096, 64, 1024, 8),
     "moe_prefill": MoeConfig("moe_prefill", 8192, 7168, 256, 2048, 8, shared=1, shared_i=2048),
     "moe_skewed": MoeConfig("moe_skewed", 16384, 4096, 128, 1536, 4, zipf_s=1.2),
+    # profiling stand-in for moe_prefill: same widths and rows per expert (256), 1/8 of the experts
+    # and tokens, so an ncu capture holds ~3 GB on the device
+    "moe_prefill_e32": MoeConfig("moe_prefill_e32", 1024, 7168, 32, 2048, 8, shared=1, shared_i=2048),
 }
 
 # tensor ids (added to the seed)

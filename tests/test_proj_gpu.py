@@ -44,7 +44,7 @@ def test_proj_matches_oracle(m, k, n):
     _assert_close(y, op.proj_ref(x, w))
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 256])
+@pytest.mark.parametrize("tile_n", [64, 128, 192, 224, 256])
 def test_every_tile_width(tile_n):
     x, w, gx, gw = _pair(300, 256, 520, seed=tile_n)
     y = torch.empty((300, 520), dtype=torch.bfloat16, device="cuda")
