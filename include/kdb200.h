@@ -63,9 +63,11 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream);
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream);
 
-/* As kdb_proj_bf16 with the output tile width forced to 64, 128, 192, 224 or 256 (0 = automatic). */
+/* As kdb_proj_bf16 with the output tile forced: tile_n 64, 128, 192, 224 or 256 with cta_pair 0
+ * (128-row tiles, one CTA each), or tile_n 192, 224, 256 with cta_pair 1 (256-row tiles computed by
+ * 2-CTA clusters); tile_n 0 with cta_pair 0 chooses automatically. */
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
-                      int tile_n, void* stream);
+                      int tile_n, int cta_pair, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- */
 /* Fused MoE layer                                                                                 */

@@ -51,12 +51,12 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream) {
 
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream) {
-  return kdb::proj_bf16(x, w, y, m, n, k, ldy, 0, static_cast<cudaStream_t>(stream));
+  return kdb::proj_bf16(x, w, y, m, n, k, ldy, 0, 0, static_cast<cudaStream_t>(stream));
 }
 
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
-                      int tile_n, void* stream) {
-  return kdb::proj_bf16(x, w, y, m, n, k, ldy, tile_n, static_cast<cudaStream_t>(stream));
+                      int tile_n, int cta_pair, void* stream) {
+  return kdb::proj_bf16(x, w, y, m, n, k, ldy, tile_n, cta_pair, static_cast<cudaStream_t>(stream));
 }
 
 static kdb::MoeShape moe_shape(int64_t t, int64_t h, int64_t e, int64_t i, int64_t k, int64_t shared,

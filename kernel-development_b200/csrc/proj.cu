@@ -4,6 +4,7 @@
 // (kdev: src/kdev/adapters/okc.py:534-537, config src/kdev/adapters/okc_problems/muse_bf16_proj.toml).
 // One persistent tcgen05 kernel (gemm_sm100.cuh); the tile width BN is picked per shape so that
 // small-M, weight-streaming shapes still put a tile on every SM.
+#include "gemm_pair_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "host_util.h"
 #include "proj.h"
@@ -139,38 +140,102 @@ static int launch_proj_cfg(const void* x, const void* w, void* y, int M, int N, 
   return cuda_status(cudaGetLastError());
 }
 
-// Output tile width.  A persistent grid runs ceil(tiles / SMs) rounds of tiles, so the tile count's
-// remainder idles SMs in the last round (896 tiles of 128 x 256 on 148 SMs: 6.05 rounds, 7 paid); a
-// narrower tile can fill the last round.  Score = wave efficiency x column efficiency x a per-width
-// factor for the operand traffic per FLOP of narrower tiles; with fewer tiles than SMs, the widest
-// width that still gives every SM a tile (weight-streaming shapes).
-int pick_tile_n(long long M, long long N, long long sms) {
-  const long long mb = (M + 127) / 128;
-  if (mb * ((N + 255) / 256) < sms) {
-    if (mb * ((N + 127) / 128) >= sms) return 128;
-    return 64;
+// CTA-pair variant: 256 x BN tiles on 2-CTA clusters (gemm_pair_sm100.cuh).
+template <int BN, int STAGES>
+static int launch_proj_pair(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
+                            cudaStream_t stream) {
+  constexpr int BM = 256;
+  using L = PairLayout<BN, STAGES>;
+  using Sched = ProjSched<BM, BN>;
+  using Epi = ProjEpi<BN>;
+  auto kern = gemm_tn_pair_kernel<Sched, Epi, BN, STAGES>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_done[dev] = true;
   }
-  static const int widths[4] = {256, 224, 192, 128};
-  static const double tile_eff[4] = {1.0, 0.985, 0.965, 0.85};
-  int best = 256;
-  double best_score = -1.0;
-  for (int i = 0; i < 4; ++i) {
-    const long long nb = (N + widths[i] - 1) / widths[i];
-    const long long tiles = mb * nb;
-    const long long rounds = (tiles + sms - 1) / sms;
-    const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * sms);
-    const double cols = static_cast<double>(N) / static_cast<double>(nb * widths[i]);
-    const double score = wave * cols * tile_eff[i];
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = widths[i];
+  CUtensorMap ta, tb;
+  int rc = make_tmap_bf16_2d(&ta, x, K, M, K, kBK, 128);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tb, w, K, N, K, kBK, BN / 2);
+  if (rc) return rc;
+  typename Sched::Params sp;
+  sp.M = M;
+  sp.N = N;
+  sp.K = K;
+  sp.num_m = (M + BM - 1) / BM;
+  sp.num_n = (N + BN - 1) / BN;
+  sp.kwrap = 0;
+  {
+    const long long per_block = static_cast<long long>(BM) * K * 2;
+    long long g = (64ll << 20) / (per_block > 0 ? per_block : 1);
+    if (g < 1) g = 1;
+    if (g > sp.num_m) g = sp.num_m;
+    sp.group_m = static_cast<int>(g);
+  }
+  typename Epi::Params ep;
+  ep.y = static_cast<__nv_bfloat16*>(y);
+  ep.ldy = ldy;
+  ep.M = M;
+  ep.N = N;
+  ep.vec_ok = aligned16(y) && (ldy % 8 == 0);
+  const int tiles = sp.num_m * sp.num_n;
+  const int max_pairs = num_sms() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
+}
+
+// Output tile shape.  A persistent grid runs ceil(tiles / workers) rounds of tiles, so the tile
+// count's remainder idles SMs in the last round (896 tiles of 128 x 256 on 148 SMs: 6.05 rounds, 7
+// paid).  Candidates are scored by wave efficiency x column efficiency x the shape's intrinsic
+// efficiency, measured on B200 with the L2 flushed: 256-row tiles on CTA pairs (half the B bytes per
+// FLOP staged per SM) 1.00 at width 256 and 0.89 at 224; 128-row single-CTA tiles 0.85 / 0.81 / 0.78 at
+// 256 / 224 / 192.  With fewer 128 x 256 tiles than SMs (weight-streaming shapes) the widest
+// single-CTA width that still gives every SM a tile.
+void pick_tile(long long M, long long N, long long sms, int* bn, int* pair) {
+  const long long mb = (M + 127) / 128;
+  *pair = 0;
+  if (mb * ((N + 255) / 256) < sms) {
+    *bn = (mb * ((N + 127) / 128) >= sms) ? 128 : 64;
+    return;
+  }
+  struct Cand { int bn, pair; double eff; };
+  static const Cand cands[5] = {{256, 1, 1.0}, {224, 1, 0.89}, {256, 0, 0.85}, {224, 0, 0.81}, {192, 0, 0.78}};
+  double best = -1.0;
+  for (const Cand& c : cands) {
+    const long long rows = c.pair ? 256 : 128;
+    const long long workers = c.pair ? sms / 2 : sms;
+    const long long nb = (N + c.bn - 1) / c.bn;
+    const long long tiles = ((M + rows - 1) / rows) * nb;
+    const long long rounds = (tiles + workers - 1) / workers;
+    const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * workers);
+    const double cols = static_cast<double>(N) / static_cast<double>(nb * c.bn);
+    const double score = wave * cols * c.eff;
+    if (score > best + 1e-9) {
+      best = score;
+      *bn = c.bn;
+      *pair = c.pair;
     }
   }
-  return best;
 }
 
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
-              int force_bn, cudaStream_t stream) {
+              int force_bn, int cta_pair, cudaStream_t stream) {
   if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return KDB_OK;
   if (!y || ldy < N) return KDB_ERR_INVALID_ARG;
@@ -184,7 +249,16 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
   if (K % 8 != 0 || !aligned16(x) || !aligned16(w)) return KDB_ERR_INVALID_ARG;
 
   int bn = force_bn;
-  if (bn == 0) bn = pick_tile_n(M, N, num_sms());
+  if (bn == 0 && cta_pair == 0) pick_tile(M, N, num_sms(), &bn, &cta_pair);
+  if (cta_pair > 0) {
+    if (bn == 0) bn = 256;
+    switch (bn) {
+      case 256: return launch_proj_pair<256, 6>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+      case 224: return launch_proj_pair<224, 7>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+      case 192: return launch_proj_pair<192, 7>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
+      default: return KDB_ERR_INVALID_ARG;
+    }
+  }
   switch (bn) {
     case 256: return launch_proj_cfg<256, 4>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
     case 224: return launch_proj_cfg<224, 5>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);

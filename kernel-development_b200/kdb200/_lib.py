@@ -32,7 +32,7 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_last_cuda_error": (_c_int, []),
     "kdb_status_read": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int, _c_vp]),
     "kdb_proj_bf16": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp]),
-    "kdb_proj_bf16_cfg": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp]),
+    "kdb_proj_bf16_cfg": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp]),
     "kdb_moe_workspace_bytes": (_c_size, [_c_i64] * 7),
     "kdb_moe_pack_gate_up": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
     "kdb_moe_route": (_c_int, [_c_vp] * 6 + [_c_i64] * 4 + [_c_vp]),

@@ -22,8 +22,9 @@ def _check_operand(name: str, t: torch.Tensor) -> None:
         raise ValueError(f"{name} must be row-major contiguous")
 
 
-def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0) -> torch.Tensor:
-    """Writes X · Wᵀ into `y` ([M, N] bf16; a column slice of a wider row-major matrix is allowed)."""
+def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0, cta_pair: int = 0) -> torch.Tensor:
+    """Writes X · Wᵀ into `y` ([M, N] bf16; a column slice of a wider row-major matrix is allowed).
+    tile_n / cta_pair force the tile shape (0 = automatic; cta_pair=1: 256-row tiles on CTA pairs)."""
     _check_operand("x", x)
     _check_operand("w", w)
     m, k = x.shape
@@ -37,7 +38,7 @@ def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
         rc = _lib.lib().kdb_proj_bf16_cfg(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, y.stride(0),
-                                          int(tile_n), stream)
+                                          int(tile_n), int(cta_pair), stream)
     _lib.check("kdb_proj_bf16", rc)
     return y
 

@@ -49,7 +49,8 @@ def test_proj_argument_checks_without_device(lib):
     assert lib.kdb_proj_bf16(vp(16), vp(16), vp(16), 4, 8, 12, 8, None) == _lib.KDB_ERR_INVALID_ARG
     assert lib.kdb_proj_bf16(None, vp(16), vp(16), 4, 8, 8, 8, None) == _lib.KDB_ERR_INVALID_ARG
     assert lib.kdb_proj_bf16(vp(17), vp(16), vp(16), 4, 8, 8, 8, None) == _lib.KDB_ERR_INVALID_ARG
-    assert lib.kdb_proj_bf16_cfg(vp(16), vp(16), vp(16), 4, 8, 8, 8, 96, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16_cfg(vp(16), vp(16), vp(16), 4, 8, 8, 8, 96, 0, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_bf16_cfg(vp(16), vp(16), vp(16), 4, 8, 8, 8, 128, 1, None) == _lib.KDB_ERR_INVALID_ARG
     # empty problems are no-ops
     assert lib.kdb_proj_bf16(None, None, None, 0, 8, 8, 8, None) == 0
     assert lib.kdb_proj_bf16(None, None, None, 8, 0, 8, 8, None) == 0

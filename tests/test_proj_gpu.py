@@ -44,13 +44,29 @@ def test_proj_matches_oracle(m, k, n):
     _assert_close(y, op.proj_ref(x, w))
 
 
-@pytest.mark.parametrize("tile_n", [64, 128, 192, 224, 256])
-def test_every_tile_width(tile_n):
-    x, w, gx, gw = _pair(300, 256, 520, seed=tile_n)
+@pytest.mark.parametrize("tile_n,cta_pair", [(64, 0), (128, 0), (192, 0), (224, 0), (256, 0),
+                                             (192, 1), (224, 1), (256, 1)])
+def test_every_tile_shape(tile_n, cta_pair):
+    x, w, gx, gw = _pair(300, 256, 520, seed=tile_n + cta_pair)
     y = torch.empty((300, 520), dtype=torch.bfloat16, device="cuda")
-    proj_into(gx, gw, y, tile_n=tile_n)
+    proj_into(gx, gw, y, tile_n=tile_n, cta_pair=cta_pair)
     torch.cuda.synchronize()
     _assert_close(y, op.proj_ref(x, w))
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 64, 256), (1000, 520, 700), (4096, 7168, 7168)])
+def test_cta_pair_tiles_match_single_cta(m, k, n):
+    """256-row tiles on 2-CTA clusters give the same result as 128-row tiles (same K order per element)."""
+    gx = W.proj_input(m, k, 7, device="cuda")
+    gw = W.proj_weight(k, n, 7, device="cuda")
+    y1 = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    y2 = torch.empty_like(y1)
+    proj_into(gx, gw, y1, tile_n=256, cta_pair=0)
+    proj_into(gx, gw, y2, tile_n=256, cta_pair=1)
+    torch.cuda.synchronize()
+    rows = torch.arange(0, m, max(1, m // 64))
+    _assert_close(y2[rows], gx[rows].cpu().float() @ gw.cpu().float().T)
+    assert float((y1.float() - y2.float()).abs().max()) <= 2e-2
 
 
 def test_output_into_column_slice():
