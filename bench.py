@@ -277,7 +277,10 @@ def bench_proj(args, dist: Dist) -> dict | None:
                 "frac": round(gbs / peaks["hbm_gbs"], 4)}
     roof["traffic"] = traffic
     roof["peak_source"] = f"{peaks['source']} (burst)"
-    roof["kernel"] = "gemm_tn_kernel<ProjSched, ProjEpi> (one launch per step)"
+    from kdb200.proj import tile_shape
+    bn, pair = tile_shape(cfg.m, cfg.n)
+    roof["kernel"] = (f"gemm_tn_pair_kernel<ProjSched<256,{bn}>> (256 x {bn} tiles on 2-CTA clusters)" if pair else
+                      f"gemm_tn_kernel<ProjSched<128,{bn}>> (128 x {bn} tiles)") + ", one launch per step"
     line = {
         "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in roofline.frac)",
         "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,

@@ -63,6 +63,10 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream);
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream);
 
+/* The output tile kdb_proj_bf16 picks for an m x n output on the current device: out[0] = tile width,
+ * out[1] = 1 for 256-row tiles on CTA pairs, 0 for 128-row single-CTA tiles.  Host-only. */
+int kdb_proj_tile_shape(int64_t m, int64_t n, int32_t out[2]);
+
 /* As kdb_proj_bf16 with the output tile forced: tile_n 64, 128, 192, 224 or 256 with cta_pair 0
  * (128-row tiles, one CTA each), or tile_n 192, 224, 256 with cta_pair 1 (256-row tiles computed by
  * 2-CTA clusters); tile_n 0 with cta_pair 0 chooses automatically. */

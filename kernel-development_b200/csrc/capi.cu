@@ -54,6 +54,15 @@ int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, i
   return kdb::proj_bf16(x, w, y, m, n, k, ldy, 0, 0, static_cast<cudaStream_t>(stream));
 }
 
+int kdb_proj_tile_shape(int64_t m, int64_t n, int32_t out[2]) {
+  if (!out || m <= 0 || n <= 0) return KDB_ERR_INVALID_ARG;
+  int bn = 0, pair = 0;
+  kdb::pick_tile(m, n, kdb::num_sms(), &bn, &pair);
+  out[0] = bn;
+  out[1] = pair;
+  return KDB_OK;
+}
+
 int kdb_proj_bf16_cfg(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                       int tile_n, int cta_pair, void* stream) {
   return kdb::proj_bf16(x, w, y, m, n, k, ldy, tile_n, cta_pair, static_cast<cudaStream_t>(stream));

@@ -5,6 +5,9 @@
 namespace kdb {
 // Y[M, N] (row stride ldy) = X[M, K] · W[N, K]ᵀ.  force_bn: 0 = pick per shape, else 64/128/192/224/256;
 // cta_pair: 1 = 256-row tiles on 2-CTA clusters (widths 192/224/256), 0 = one CTA per 128-row tile.
+// Automatic tile shape: width *bn (64..256) and *pair (1 = 256-row tiles on CTA pairs).
+void pick_tile(long long M, long long N, long long sms, int* bn, int* pair);
+
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
               int force_bn, int cta_pair, cudaStream_t stream);
 }  // namespace kdb

@@ -43,6 +43,14 @@ def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0
     return y
 
 
+def tile_shape(m: int, n: int) -> tuple[int, bool]:
+    """(tile width, CTA pair) the projection picks for an m x n output on the current device."""
+    import ctypes
+    out = (ctypes.c_int32 * 2)()
+    _lib.check("kdb_proj_tile_shape", _lib.lib().kdb_proj_tile_shape(m, n, out))
+    return int(out[0]), bool(out[1])
+
+
 @torch.library.custom_op("kdb200::proj", mutates_args=())
 def proj(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Y[M, N] = X[M, K] · W[N, K]ᵀ, bf16 in/out, fp32 accumulation (tcgen05 on sm_100a)."""
