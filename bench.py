@@ -9,7 +9,7 @@ the ≥70 %-of-bf16-peak target is quoted on).  Other workloads: proj_2048, proj
 moe_decode, moe_prefill, moe_skewed (see kernel-development_b200/kdb200/workloads.py).
 
 A step is one pass of the op over one batch already resident in HBM, replayed from a CUDA graph.
-The L2 is flushed (a 512 MiB device write, untimed) before every timed step; each step is timed
+The L2 is flushed (a 512 MiB device write, then a read of it, untimed) before every timed step; each step is timed
 with CUDA events on its own stream; the time is the max over ranks.  At N > 1 the projection is
 column-parallel with N·7168 global output columns (each rank its own 7168-column shard, no
 collective: weak scaling); the MoE layer runs expert-parallel (E/N experts and T tokens per GPU, NCCL
@@ -160,10 +160,15 @@ class Dist:
 
 
 def _flusher(dev):
+    """L2 flush before a timed step: write a buffer 4x the L2, then read it back, so the L2 holds only
+    clean lines of the flush buffer and the timed step pays no write-back of the flush's dirty lines
+    (kdev's protocol flushes with a read for the same reason)."""
     buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def flush():
         buf.fill_(1.0)
+        torch.amax(buf, dim=0, out=sink)
     return flush
 
 
@@ -289,7 +294,7 @@ def bench_proj(args, dist: Dist) -> dict | None:
         "config": {"workload": args.workload, "m": cfg.m, "k": cfg.k, "n_per_gpu": cfg.n,
                    "n_total": cfg.n * dist.world,
                    "parallelism": f"column-parallel over N, {dist.world} shard(s), no collective",
-                   "l2": "flushed before every timed step (512 MiB device write, untimed)",
+                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
                    "graph": "CUDA graph replay per step"},
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
@@ -447,7 +452,7 @@ def bench_moe(args, dist: Dist) -> dict | None:
         "data": "synthetic (seeded; x~N(0,1) bf16, router N(0,1/H) fp32, experts N(0,1/fan_in) bf16)",
         "config": {"workload": args.workload, **cfg.as_case(), "distinct_experts_hit": distinct,
                    "parallelism": par,
-                   "l2": "flushed before every timed step (512 MiB device write, untimed)",
+                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
                    "graph": graph},
         "e2e": {"value": round(cfg.t * dist.world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": cfg.t * cfg.h * 2,

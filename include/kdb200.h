@@ -63,6 +63,16 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream);
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream);
 
+/* Workspace bytes kdb_proj_bf16_ws can use for this shape (0 when it needs none): fp32 partial sums of
+ * the K split that small-M (m <= 128, weight-streaming) shapes use to put every SM on the weights. */
+size_t kdb_proj_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
+/* kdb_proj_bf16 with a workspace (16-byte aligned, >= kdb_proj_workspace_bytes) for the small-M K split;
+ * the partials are summed in slice order, so results are deterministic.  With a smaller or NULL
+ * workspace it runs without the split. */
+int kdb_proj_bf16_ws(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* The output tile kdb_proj_bf16 picks for an m x n output on the current device: out[0] = tile width,
  * out[1] = 1 for 256-row tiles on CTA pairs, 0 for 128-row single-CTA tiles.  Host-only. */
 int kdb_proj_tile_shape(int64_t m, int64_t n, int32_t out[2]);

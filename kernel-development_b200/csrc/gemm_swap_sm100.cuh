@@ -18,13 +18,17 @@
 
 #include <cuda.h>
 #include "gemm_sm100.cuh"
+#include "host_util.h"
 
 namespace kdb {
 
-// Five B tensor maps over the same token matrix, box rows 16, 32, 64, 128, 256.
-struct TokenMaps {
-  CUtensorMap m[5];
+// One tile of a swapped-operand GEMM: weight rows [a_row, a_row + 128*MA) (parts a_part_stride apart),
+// token rows [b_row, b_row + n_valid), k slices [kb0, kb0 + nkb); f0 / row0 / split locate the output.
+struct SwapTile {
+  int a_row, a_part_stride, b_row, kb0, nkb, n_valid;
+  int f0, row0, split;
 };
+
 
 __host__ __device__ constexpr int box_index(int rows) {
   return rows <= 16 ? 0 : rows <= 32 ? 1 : rows <= 64 ? 2 : rows <= 128 ? 3 : 4;
@@ -33,7 +37,7 @@ __host__ __device__ constexpr int box_index(int rows) {
 template <int MA, int NB, int STAGES>
 struct SwapLayout {
   static_assert(MA == 1 || MA == 2, "one or two 128-row weight blocks per tile");
-  static_assert(NB == 128 || NB == 256, "token block of a tile");
+  static_assert(NB == 32 || NB == 64 || NB == 128 || NB == 256, "token block of a tile");
   static_assert(MA * NB <= 256, "two accumulators of MA x NB columns must fit the 512 TMEM columns");
   static constexpr int kABytes = MA * 128 * kBK * 2;
   static constexpr int kBBytesMax = NB * kBK * 2;
@@ -113,9 +117,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[stage], bytes);
 #pragma unroll
           for (int a = 0; a < MA; ++a)
-            tma_load_2d(sA + stage * L::kABytes + a * 128 * kBK * 2, &tmA, &full[stage], kb * kBK,
+            tma_load_2d(sA + stage * L::kABytes + a * 128 * kBK * 2, &tmA, &full[stage], (ti.kb0 + kb) * kBK,
                         ti.a_row + a * ti.a_part_stride, pol_w);
-          tma_load_2d(sB + stage * L::kBBytesMax, &tmB.m[bi], &full[stage], kb * kBK, ti.b_row, pol_t);
+          tma_load_2d(sB + stage * L::kBBytesMax, &tmB.m[bi], &full[stage], (ti.kb0 + kb) * kBK, ti.b_row, pol_t);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {

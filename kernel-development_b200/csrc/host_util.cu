@@ -61,4 +61,12 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64
   return r == CUDA_SUCCESS ? KDB_OK : KDB_ERR_INVALID_ARG;
 }
 
+int make_token_maps(TokenMaps* m, const void* rows, uint64_t n_rows, uint64_t k) {
+  for (int i = 0; i < 5; ++i) {
+    const int rc = make_tmap_bf16_2d(&m->m[i], rows, k, n_rows, k, 64, 16u << i);
+    if (rc) return rc;
+  }
+  return KDB_OK;
+}
+
 }  // namespace kdb

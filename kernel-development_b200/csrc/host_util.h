@@ -22,6 +22,13 @@ int num_sms();
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t ld,
                       uint32_t box_inner, uint32_t box_rows);
 
+// Five tensor maps over one row-major bf16 [n_rows, k] matrix with boxes of 16, 32, 64, 128 and 256
+// rows (64 columns), for operands whose row count varies per tile.
+struct TokenMaps {
+  CUtensorMap m[5];
+};
+int make_token_maps(TokenMaps* m, const void* rows, uint64_t n_rows, uint64_t k);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace kdb

@@ -23,11 +23,6 @@ namespace kdb {
 
 // ---------------------------------------------------------------------------------------------------
 // Swapped-operand grouped schedule: tiles (group g, weight tile f, token tile tt), tt fastest.
-struct SwapTile {
-  int a_row, a_part_stride, b_row, nkb, n_valid;
-  int f0, row0;
-};
-
 struct SwapSched {
   struct Params {
     const int* offsets;       // [groups + 1] token-row offsets, or null: one dense group of `rows` rows
@@ -68,7 +63,9 @@ struct SwapSched {
     ti.a_row = g * p.a_rows_per_group + f * p.a_tile_rows;
     ti.a_part_stride = 128;
     ti.f0 = f * p.f_step;
+    ti.kb0 = 0;
     ti.nkb = p.nkb;
+    ti.split = 0;
     return ti;
   }
 };
@@ -146,14 +143,6 @@ static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return cuda_status(e);
     done[dev] = true;
-  }
-  return KDB_OK;
-}
-
-static int make_token_maps(TokenMaps* m, const void* rows, uint64_t n_rows, uint64_t k) {
-  for (int i = 0; i < 5; ++i) {
-    const int rc = make_tmap_bf16_2d(&m->m[i], rows, k, n_rows, k, kBK, 16u << i);
-    if (rc) return rc;
   }
   return KDB_OK;
 }

@@ -6,6 +6,7 @@
 // small-M, weight-streaming shapes still put a tile on every SM.
 #include "gemm_pair_sm100.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_swap_sm100.cuh"
 #include "host_util.h"
 #include "proj.h"
 
@@ -200,6 +201,163 @@ static int launch_proj_pair(const void* x, const void* w, void* y, int M, int N,
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Small M (weight streaming): W as the 128-row M operand, X's rows as N (rounded up to 16), K split
+// over `splits` slices so every SM streams a share of W.  With splits > 1 the epilogue writes fp32
+// partials [splits, M, N] into the caller's workspace and proj_reduce_kernel sums them in slice order
+// (deterministic) into bf16 Y.
+struct ProjSwapSched {
+  struct Params {
+    int M, N, f_tiles, t_tiles, splits, nkb_total, nkb_per, nb;   // nb: token rows per tile
+  };
+  Params p;
+  __device__ explicit ProjSwapSched(const Params& pp) : p(pp) {}
+  __device__ int num_tiles() const { return p.f_tiles * p.t_tiles * p.splits; }
+  // order: feature tile, then split, then token tile (fastest)
+  __device__ SwapTile tile(int t) const {
+    const int tt = t % p.t_tiles;
+    const int rest = t / p.t_tiles;
+    const int sp = rest % p.splits;
+    const int f = rest / p.splits;
+    SwapTile ti;
+    ti.a_row = f * 128;
+    ti.a_part_stride = 128;
+    ti.b_row = tt * p.nb;
+    ti.row0 = ti.b_row;
+    ti.n_valid = min(p.nb, p.M - ti.row0);
+    ti.kb0 = sp * p.nkb_per;
+    ti.nkb = min(p.nkb_per, p.nkb_total - ti.kb0);
+    ti.f0 = f * 128;
+    ti.split = sp;
+    return ti;
+  }
+};
+
+struct ProjSwapEpi {
+  struct Params {
+    __nv_bfloat16* y;   // used when partial is null
+    float* partial;     // [splits, M, N] fp32, or null
+    long long ldy;
+    int M, N;
+  };
+  template <int NB>
+  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
+    const int feat = ti.f0 + r;
+    const bool ok = feat < p.N;
+#pragma unroll 1
+    for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c0, v);
+      tmem_ld_wait();
+      const int n = min(32, ti.n_valid - c0);
+      if (!ok) continue;
+      if (p.partial) {
+        float* dst = p.partial + (static_cast<long long>(ti.split) * p.M + ti.row0 + c0) * p.N + feat;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < n) dst[static_cast<long long>(i) * p.N] = __uint_as_float(v[i]);
+      } else {
+        __nv_bfloat16* dst = p.y + static_cast<long long>(ti.row0 + c0) * p.ldy + feat;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < n) dst[static_cast<long long>(i) * p.ldy] = __float2bfloat16_rn(__uint_as_float(v[i]));
+      }
+    }
+  }
+};
+
+// y[m, n] = bf16(sum_s partial[s, m, n]), s ascending.
+__global__ void __launch_bounds__(256)
+    proj_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ y, long long ldy, int M, int N,
+                       int splits) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(M) * N;
+  if (idx >= total) return;
+  const long long m = idx / N, n = idx % N;
+  float acc = 0.f;
+  for (int s = 0; s < splits; ++s) acc += partial[static_cast<long long>(s) * total + idx];
+  y[m * ldy + n] = __float2bfloat16_rn(acc);
+}
+
+// K split of the small-M path: minimises (W bytes + partial traffic) / wave efficiency.
+int proj_small_m_splits(long long M, long long N, long long K, long long sms) {
+  const long long base = ((N + 127) / 128) * ((M + 127) / 128);
+  const long long nkb = (K + 63) / 64;
+  int best = 1;
+  double best_cost = 1e30;
+  const long long max_s = M <= 32 ? 32 : 16;
+  for (long long s = 1; s <= max_s && s <= nkb; ++s) {
+    const long long per = (nkb + s - 1) / s;
+    const long long used = (nkb + per - 1) / per;   // slices actually non-empty
+    if (used != s) continue;
+    const long long tiles = base * s;
+    const long long rounds = (tiles + sms - 1) / sms;
+    const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * sms);
+    const double traffic = 1.0 + (s > 1 ? 4.0 * s * static_cast<double>(M) / static_cast<double>(K) : 0.0);
+    const double cost = traffic / wave;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = static_cast<int>(s);
+    }
+  }
+  return best;
+}
+
+size_t proj_workspace_bytes(long long M, long long N, long long K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > 128) return 0;
+  const int s = proj_small_m_splits(M, N, K, num_sms());
+  return s > 1 ? static_cast<size_t>(s) * M * N * sizeof(float) : 0;
+}
+
+template <int NB, int STAGES>
+static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
+                               void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  constexpr int MA = 1;
+  using L = SwapLayout<MA, NB, STAGES>;
+  auto kern = gemm_swap_kernel<ProjSwapSched, ProjSwapEpi, MA, NB, STAGES>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_done[dev] = true;
+  }
+  int splits = proj_small_m_splits(M, N, K, num_sms());
+  const size_t need = splits > 1 ? static_cast<size_t>(splits) * M * N * sizeof(float) : 0;
+  if (splits > 1 && (!workspace || ws_bytes < need)) splits = 1;   // no workspace: one K slice
+  CUtensorMap ta;
+  TokenMaps tb;
+  int rc = make_tmap_bf16_2d(&ta, w, K, N, K, kBK, 128);
+  if (rc) return rc;
+  rc = make_token_maps(&tb, x, M, K);
+  if (rc) return rc;
+  ProjSwapSched::Params sp;
+  sp.M = M;
+  sp.N = N;
+  sp.f_tiles = (N + 127) / 128;
+  sp.t_tiles = (M + NB - 1) / NB;
+  sp.nb = NB;
+  sp.splits = splits;
+  sp.nkb_total = (K + kBK - 1) / kBK;
+  sp.nkb_per = (sp.nkb_total + splits - 1) / splits;
+  ProjSwapEpi::Params ep;
+  ep.y = static_cast<__nv_bfloat16*>(y);
+  ep.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  ep.ldy = ldy;
+  ep.M = M;
+  ep.N = N;
+  const int tiles = sp.f_tiles * sp.t_tiles * splits;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kGemmThreads, L::kSmemBytes, stream>>>(ta, tb, sp, ep);
+  rc = cuda_status(cudaGetLastError());
+  if (rc || splits == 1) return rc;
+  const long long total = static_cast<long long>(M) * N;
+  proj_reduce_kernel<<<static_cast<unsigned int>((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(y), ldy, M, N, splits);
+  return cuda_status(cudaGetLastError());
+}
+
 // Output tile shape.  A persistent grid runs ceil(tiles / workers) rounds of tiles, so the tile
 // count's remainder idles SMs in the last round (896 tiles of 128 x 256 on 148 SMs: 6.05 rounds, 7
 // paid).  Candidates are scored by wave efficiency x column efficiency x the shape's intrinsic
@@ -235,7 +393,7 @@ void pick_tile(long long M, long long N, long long sms, int* bn, int* pair) {
 }
 
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
-              int force_bn, int cta_pair, cudaStream_t stream) {
+              int force_bn, int cta_pair, cudaStream_t stream, void* workspace, size_t ws_bytes) {
   if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
   if (M == 0 || N == 0) return KDB_OK;
   if (!y || ldy < N) return KDB_ERR_INVALID_ARG;
@@ -249,7 +407,13 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
   if (K % 8 != 0 || !aligned16(x) || !aligned16(w)) return KDB_ERR_INVALID_ARG;
 
   int bn = force_bn;
-  if (bn == 0 && cta_pair == 0) pick_tile(M, N, num_sms(), &bn, &cta_pair);
+  if (bn == 0 && cta_pair == 0) {
+    // weight streaming: swapped operands with a K split; the narrower token block of M <= 32 leaves
+    // room for 11 pipeline stages (more weight bytes in flight per SM)
+    if (M <= 32) return launch_proj_small_m<32, 11>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    if (M <= 128) return launch_proj_small_m<128, 6>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    pick_tile(M, N, num_sms(), &bn, &cta_pair);
+  }
   if (cta_pair > 0) {
     if (bn == 0) bn = 256;
     switch (bn) {

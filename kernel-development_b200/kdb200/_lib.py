@@ -32,6 +32,8 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_last_cuda_error": (_c_int, []),
     "kdb_status_read": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int, _c_vp]),
     "kdb_proj_bf16": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp]),
+    "kdb_proj_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "kdb_proj_bf16_ws": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "kdb_proj_tile_shape": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(ctypes.c_int32)]),
     "kdb_proj_bf16_cfg": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp]),
     "kdb_moe_workspace_bytes": (_c_size, [_c_i64] * 7),

@@ -37,8 +37,15 @@ def proj_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, tile_n: int = 0
         raise ValueError("x, w and y must be on the same device")
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
-        rc = _lib.lib().kdb_proj_bf16_cfg(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, y.stride(0),
-                                          int(tile_n), int(cta_pair), stream)
+        if tile_n == 0 and cta_pair == 0:
+            # automatic shape; small-M shapes split K and sum fp32 partials from a workspace
+            nbytes = int(_lib.lib().kdb_proj_workspace_bytes(m, n, k)) if m > 0 and n > 0 and k > 0 else 0
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device) if nbytes else None
+            rc = _lib.lib().kdb_proj_bf16_ws(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, y.stride(0),
+                                             None if ws is None else ws.data_ptr(), nbytes, stream)
+        else:
+            rc = _lib.lib().kdb_proj_bf16_cfg(x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, k, y.stride(0),
+                                              int(tile_n), int(cta_pair), stream)
     _lib.check("kdb_proj_bf16", rc)
     return y
 

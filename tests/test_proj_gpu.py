@@ -69,6 +69,31 @@ def test_cta_pair_tiles_match_single_cta(m, k, n):
     assert float((y1.float() - y2.float()).abs().max()) <= 2e-2
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 7168, 7168), (16, 7168, 7168), (128, 7168, 7168), (128, 2048, 2048),
+                                   (37, 520, 1000), (100, 4096, 300)])
+def test_small_m_split_k(m, k, n):
+    """Weight-streaming shapes (M <= 128): swapped operands with a K split summed from fp32 partials;
+    deterministic (same result twice) and within tolerance of the oracle."""
+    x, w, gx, gw = _pair(m, k, n, seed=m * 3 + n)
+    y1 = proj(gx, gw)
+    y2 = proj(gx, gw)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    _assert_close(y1, op.proj_ref(x, w))
+
+
+def test_small_m_without_workspace():
+    """The C entry point without a workspace runs the same path with one K slice."""
+    import ctypes
+    x, w, gx, gw = _pair(16, 7168, 2048, seed=3)
+    y = torch.empty((16, 2048), dtype=torch.bfloat16, device="cuda")
+    rc = _lib.lib().kdb_proj_bf16(gx.data_ptr(), gw.data_ptr(), y.data_ptr(), 16, 2048, 7168, 2048,
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    _assert_close(y, op.proj_ref(x, w))
+
+
 def test_output_into_column_slice():
     """Column-parallel layout: write into a slice of a wider Y (row stride ldy > n)."""
     x, w, gx, gw = _pair(64, 128, 96, seed=5)
