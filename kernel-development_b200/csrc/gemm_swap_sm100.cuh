@@ -34,13 +34,17 @@ __host__ __device__ constexpr int box_index(int rows) {
   return rows <= 16 ? 0 : rows <= 32 ? 1 : rows <= 64 ? 2 : rows <= 128 ? 3 : 4;
 }
 
-template <int MA, int NB, int STAGES>
+// KC: 64-wide k chunks per pipeline stage.  Several chunks per stage ask HBM for KC adjacent 128-byte
+// pieces of every weight row together rather than one per stage, which weight-streaming tiles need.
+template <int MA, int NB, int STAGES, int KC = 1>
 struct SwapLayout {
   static_assert(MA == 1 || MA == 2, "one or two 128-row weight blocks per tile");
   static_assert(NB == 32 || NB == 64 || NB == 128 || NB == 256, "token block of a tile");
   static_assert(MA * NB <= 256, "two accumulators of MA x NB columns must fit the 512 TMEM columns");
-  static constexpr int kABytes = MA * 128 * kBK * 2;
-  static constexpr int kBBytesMax = NB * kBK * 2;
+  static constexpr int kAChunk = MA * 128 * kBK * 2;       // one k chunk of the weight parts
+  static constexpr int kBChunk = NB * kBK * 2;             // one k chunk of the token block
+  static constexpr int kABytes = KC * kAChunk;
+  static constexpr int kBBytesMax = KC * kBChunk;
   static constexpr int kStageBytes = kABytes + kBBytesMax;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
@@ -49,11 +53,11 @@ struct SwapLayout {
   static constexpr uint32_t kTmemCols = (2 * kAccCols <= 256) ? 256 : 512;
 };
 
-template <class Sched, class Epi, int MA, int NB, int STAGES>
+template <class Sched, class Epi, int MA, int NB, int STAGES, int KC = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ TokenMaps tmB,
                      const typename Sched::Params sp, const typename Epi::Params ep) {
-  using L = SwapLayout<MA, NB, STAGES>;
+  using L = SwapLayout<MA, NB, STAGES, KC>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -108,18 +112,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
         const auto ti = sched.tile(t);
         const int bi = box_index(ti.n_valid);
-        const uint32_t bytes = L::kABytes + (16u << bi) * kBK * 2;
-        for (int kb = 0; kb < ti.nkb; ++kb) {
+        const uint32_t chunk_bytes = L::kAChunk + (16u << bi) * kBK * 2;
+        for (int kb = 0; kb < ti.nkb; kb += KC) {   // one stage = nc <= KC k chunks of this tile
+          const int nc = min(KC, ti.nkb - kb);
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProdEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], bytes);
+          mbar_arrive_expect_tx(&full[stage], nc * chunk_bytes);
 #pragma unroll
-          for (int a = 0; a < MA; ++a)
-            tma_load_2d(sA + stage * L::kABytes + a * 128 * kBK * 2, &tmA, &full[stage], (ti.kb0 + kb) * kBK,
-                        ti.a_row + a * ti.a_part_stride, pol_w);
-          tma_load_2d(sB + stage * L::kBBytesMax, &tmB.m[bi], &full[stage], (ti.kb0 + kb) * kBK, ti.b_row, pol_t);
+          for (int c = 0; c < KC; ++c) {
+            if (c < nc) {
+              const int kc = (ti.kb0 + kb + c) * kBK;
+#pragma unroll
+              for (int a = 0; a < MA; ++a)
+                tma_load_2d(sA + stage * L::kABytes + c * L::kAChunk + a * 128 * kBK * 2, &tmA, &full[stage], kc,
+                            ti.a_row + a * ti.a_part_stride, pol_w);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < KC; ++c)
+            if (c < nc)
+              tma_load_2d(sB + stage * L::kBBytesMax + c * L::kBChunk, &tmB.m[bi], &full[stage],
+                          (ti.kb0 + kb + c) * kBK, ti.b_row, pol_t);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -145,21 +160,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, kSiteMmaTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d_base = tmem_base + acc * L::kAccCols;
-        for (int kb = 0; kb < ti.nkb; ++kb) {
+        for (int kb = 0; kb < ti.nkb; kb += KC) {
+          const int nc = min(KC, ti.nkb - kb);
           if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * L::kABytes);
-          const uint32_t b_addr = smem_u32(sB + stage * L::kBBytesMax);
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-            const uint64_t bdesc = sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2);
+          for (int c = 0; c < KC; ++c) {
+            if (c >= nc) break;
+            const uint32_t a_addr = smem_u32(sA + stage * L::kABytes + c * L::kAChunk);
+            const uint32_t b_addr = smem_u32(sB + stage * L::kBBytesMax + c * L::kBChunk);
 #pragma unroll
-            for (int a = 0; a < MA; ++a)
-              mma_bf16(d_base + a * NB, sdesc_sw128_kmajor(a_addr + a * 128 * kBK * 2 + kk * kUmmaK * 2), bdesc,
-                       idesc, (kb | kk) != 0);
+            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+              const uint64_t bdesc = sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2);
+#pragma unroll
+              for (int a = 0; a < MA; ++a)
+                mma_bf16(d_base + a * NB, sdesc_sw128_kmajor(a_addr + a * 128 * kBK * 2 + kk * kUmmaK * 2), bdesc,
+                         idesc, (kb | c | kk) != 0);
+            }
           }
           mma_commit(&empty[stage]);
           issued = true;

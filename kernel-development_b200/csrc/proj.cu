@@ -309,12 +309,12 @@ size_t proj_workspace_bytes(long long M, long long N, long long K) {
   return s > 1 ? static_cast<size_t>(s) * M * N * sizeof(float) : 0;
 }
 
-template <int NB, int STAGES>
+template <int NB, int STAGES, int KC>
 static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
                                void* workspace, size_t ws_bytes, cudaStream_t stream) {
   constexpr int MA = 1;
-  using L = SwapLayout<MA, NB, STAGES>;
-  auto kern = gemm_swap_kernel<ProjSwapSched, ProjSwapEpi, MA, NB, STAGES>;
+  using L = SwapLayout<MA, NB, STAGES, KC>;
+  auto kern = gemm_swap_kernel<ProjSwapSched, ProjSwapEpi, MA, NB, STAGES, KC>;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -410,8 +410,10 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
   if (bn == 0 && cta_pair == 0) {
     // weight streaming: swapped operands with a K split; the narrower token block of M <= 32 leaves
     // room for 11 pipeline stages (more weight bytes in flight per SM)
-    if (M <= 32) return launch_proj_small_m<32, 11>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
-    if (M <= 128) return launch_proj_small_m<128, 6>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    // two 64-wide k chunks per stage: 256 contiguous bytes of every weight row per request (7% faster
+    // than one chunk at 16 x 7168 x 7168)
+    if (M <= 32) return launch_proj_small_m<32, 5, 2>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    if (M <= 128) return launch_proj_small_m<128, 6, 1>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
     pick_tile(M, N, num_sms(), &bn, &cta_pair);
   }
   if (cta_pair > 0) {
