@@ -26,6 +26,9 @@ extern "C" {
 
 #define KDB200_ABI_VERSION 1
 
+/* Tokens of one grouped expert-GEMM tile; the routing plan's mtile_start counts ceil(count / this). */
+#define KDB_MOE_TOKEN_TILE 512
+
 /* ---------------------------------------------------------------------------------------------- */
 /* Library and status                                                                              */
 /* ---------------------------------------------------------------------------------------------- */
@@ -184,7 +187,7 @@ int kdb_moe_gather_rows(const void* x, const int32_t* index, int64_t div, void* 
  * Grouped SwiGLU gate_up: for each group g, rows [offsets[g], offsets[g+1]) of a (bf16 [a_rows, h])
  * times packed w_gate_up[g] (bf16 [2i, h], from kdb_moe_pack_gate_up), epilogue silu(gate) * up ->
  * out bf16 [a_rows, i].  offsets / mtile_start (int32 [groups + 1], mtile_start = exclusive prefix of
- * ceil(count / 128), as kdb_moe_plan / kdb_moe_ep_regroup produce) are read on the device; both NULL
+ * ceil(count / KDB_MOE_TOKEN_TILE), as kdb_moe_plan / kdb_moe_ep_regroup produce) are read on the device; both NULL
  * means one dense group of a_rows rows.  Counterpart: the gate_up stage + SwiGLU epilogue warp of the
  * reference engines (okc-challenge/engines/sc_h.cu:164-187, 322-340).
  */

@@ -126,10 +126,11 @@ int moe_forward(const void* x, const float* router_w, const float* router_bias, 
   void* hbuf = ws + c.hbuf;
   rc = moe_gather_rows(x, Ip(c.perm_token), xy_perm, R, H, T, s);
   if (rc) return rc;
-  rc = moe_gemm_gate_up(xy_perm, R, w_gate_up_packed, E, I, H, Ip(c.offsets), Ip(c.mtile_start), hbuf, s);
+  // a token picks an expert at most once: no group holds more than T rows
+  rc = moe_gemm_gate_up(xy_perm, R, w_gate_up_packed, E, I, H, Ip(c.offsets), Ip(c.mtile_start), hbuf, s, T);
   if (rc) return rc;
   // x_perm is dead once gate_up has run (stream order): its buffer takes the per-slot down output.
-  rc = moe_gemm_down(hbuf, R, w_down, E, I, H, Ip(c.offsets), Ip(c.mtile_start), F(c.perm_w), xy_perm, s);
+  rc = moe_gemm_down(hbuf, R, w_down, E, I, H, Ip(c.offsets), Ip(c.mtile_start), F(c.perm_w), xy_perm, s, T);
   if (rc) return rc;
   void* yshared = nullptr;
   if (sh.shared) {

@@ -5,6 +5,9 @@
 
 namespace kdb {
 
+// Tokens of one grouped-GEMM tile: the plan's tile prefix mtile_start[g] counts ceil(count_g / kMoeTokenTile).
+constexpr int kMoeTokenTile = 512;
+
 int moe_route(const void* x, const float* wr, const float* bias, float* logits, float* topk_w, int* topk_ids,
               int T, int H, int E, int k, cudaStream_t s);
 int moe_plan(const int* ids, const float* topk_w, int T, int E, int k, int* chunk_counts, int* chunk_base,
@@ -20,10 +23,12 @@ int moe_ep_regroup(const int* counts, int P, int Er, int to_expert_major, const 
                    int* offsets, int* mtile_start, void* scratch, cudaStream_t s);
 size_t moe_ep_regroup_scratch_bytes(int P, int Er);
 int moe_pack_gate_up(const void* w, void* packed, int E, int I, int H, cudaStream_t s);
+// Grouped expert GEMMs (moe_gemm.cu).  max_group_tokens: an upper bound on any group's row count that the
+// caller guarantees (0 = none known; a_rows is used); a bound <= 64 selects the weight-streaming variant.
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
-                     const int* mtile_start, void* out, cudaStream_t s);
+                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens = 0);
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
-                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s);
+                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens = 0);
 
 struct MoeShape {
   long long t, h, e, i, k, shared, shared_i;

@@ -9,8 +9,8 @@
 //   source-major offset of block (s, e):  so[s][e] = sum_{s' < s} sum_e' c[s'][e'] + sum_{e' < e} c[s][e']
 //   expert-major offset of block (s, e):  eo[s][e] = sum_{e' < e} sum_s' c[s'][e'] + sum_{s' < s} c[s'][e]
 //
-// The regroup also writes the expert-major offsets[Er + 1] and the m-tile prefix mtile_start[Er + 1]
-// the grouped GEMM schedule reads.  Counts stay on the device: nothing here synchronises.
+// The regroup also writes the expert-major offsets[Er + 1] and the tile prefix mtile_start[Er + 1]
+// (exclusive prefix of ceil(rows / kMoeTokenTile)) that the grouped GEMM schedule reads.  Counts stay on the device: nothing here synchronises.
 //
 // No counterpart kernel in the reference: its engines simulate one ep8 rank and compute only the
 // routes to local experts (okc_problems/muse_moe_w4a16.toml:136); the exchange is new.
@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(1024)
   int col = 0;
   if (e < Er)
     for (int s = 0; s < P; ++s) col += counts[s * Er + e];
-  const int mt = (col + 127) / 128;
+  const int mt = (col + kMoeTokenTile - 1) / kMoeTokenTile;
   int total_rows = 0, total_mt = 0;
   const int ebase = scan(e < Er ? col : 0, &total_rows);
   const int mbase = scan(e < Er ? mt : 0, &total_mt);

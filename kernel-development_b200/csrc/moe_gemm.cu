@@ -1,135 +1,189 @@
-// moe_gemm.cu — grouped expert GEMMs of the MoE layer on the persistent tcgen05 core with swapped
-// operands (gemm_swap_sm100.cuh: weights as M, each expert's tokens as N rounded up to 16).
+// moe_gemm.cu — grouped expert GEMMs of the MoE layer on CTA pairs (gemm_grouped_pair_sm100.cuh): the
+// weights are the M operand (256 rows per pair), all tokens of one expert (up to 512) the N operand.
 //
-//   gate_up:  H_e = silu(X_e · Wg_eᵀ) * (X_e · Wu_eᵀ) -> bf16 intermediate; one tile = 128 gate rows and
-//             the matching 128 up rows of the packed weights against <= 128 token rows
-//   down:     Y_e = H_e · Wd_eᵀ (* routing weight of the row) -> bf16; one tile = 256 output features
-//             against <= 128 token rows
+//   gate_up:  H_e = silu(X_e · Wg_eᵀ) * (X_e · Wu_eᵀ) -> bf16 intermediate.  A pair tile covers 128
+//             intermediate features; each CTA stages 64 gate rows and the 64 matching up rows (two 64-row
+//             boxes of the packed weights), so gate lands in TMEM lanes 0-63 and up in lanes 64-127; the
+//             up warps hand their values to the gate warps through shared memory.
+//   down:     Y_e = H_e · Wd_eᵀ (* routing weight of the row) -> bf16.  A pair tile covers 256 output
+//             features, 128 per CTA.
 //
-// The tile schedule is read on the device from the routing plan (offsets[g], mtile_start[g]), so no
-// host synchronisation separates routing from the GEMMs and the whole layer is graph-capturable.
-// Tiles are ordered expert-major, then by weight tile, with token tiles fastest: the tiles in flight
-// at once share an expert's weight tiles in L2.
+// The tile schedule is read on the device from the routing plan (offsets[g], and mtile_start[g], the
+// prefix of ceil(count / 512)), so no host synchronisation separates routing from the GEMMs and the whole
+// layer is graph-capturable.  Tiles are ordered expert-major, then by weight tile, then by 512-token chunk:
+// an expert with more than 512 tokens has its chunks of one weight tile in flight together.
 //
 // Reference counterparts: the gate_up stage + SwiGLU epilogue warp of the H200 engines
 // (okc-challenge/engines/sc_h.cu:164-187, 322-340) and their down stage + weighted output
 // (sc_h.cu:341-381, x7_h.cu:438-590), which stream NVFP4 weights through mma.sync.
+#include "gemm_grouped_pair_sm100.cuh"
 #include "gemm_sm100.cuh"
-#include "gemm_swap_sm100.cuh"
 #include "host_util.h"
 #include "moe.h"
 
 namespace kdb {
 
+static_assert(kMoeTokenTile == kGpTokens, "plan tile prefix and GEMM tile size agree");
+
 // ---------------------------------------------------------------------------------------------------
-// Swapped-operand grouped schedule: tiles (group g, weight tile f, token tile tt), tt fastest.
-struct SwapSched {
+// Tiles (group g, weight tile f, token chunk j), j fastest.
+struct GroupedPairSched {
   struct Params {
     const int* offsets;       // [groups + 1] token-row offsets, or null: one dense group of `rows` rows
-    const int* mtile_start;   // [groups + 1] exclusive prefix of ceil(count / 128), or null
+    const int* tile_start;    // [groups + 1] exclusive prefix of ceil(count / 512), or null
     int groups, rows, f_tiles, nkb;
     int a_rows_per_group;     // weight rows of one group
-    int a_tile_rows;          // weight rows one tile spans (two 128-row parts)
-    int f_step;               // feature index advance per weight tile
+    int a_f_stride;           // weight rows between consecutive weight tiles
+    int a_box_stride;         // offset of a CTA's second 64-row box (gate_up: gate -> up rows)
+    int a_rank_stride;        // offset of CTA 1's rows
+    int f_step;               // output features per weight tile
   };
   Params p;
-  int total_mt;
-  __device__ explicit SwapSched(const Params& pp) : p(pp) {
-    total_mt = p.mtile_start ? p.mtile_start[p.groups] : (p.rows + 127) / 128;
+  int total_tt;
+  __device__ explicit GroupedPairSched(const Params& pp) : p(pp) {
+    total_tt = p.tile_start ? p.tile_start[p.groups] : (p.rows + kGpTokens - 1) / kGpTokens;
   }
-  __device__ int num_tiles() const { return total_mt * p.f_tiles; }
-  __device__ SwapTile tile(int t) const {
-    int g = 0, mstart = 0, mcount = total_mt, row_begin = 0, count = p.rows;
-    if (p.mtile_start) {
+  __device__ int num_tiles() const { return total_tt * p.f_tiles; }
+  __device__ GpTile tile(int t) const {
+    int g = 0, tstart = 0, tcount = total_tt, row_begin = 0, count = p.rows;
+    if (p.tile_start) {
       int lo = 0, hi = p.groups - 1;
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (__ldg(p.mtile_start + mid) * p.f_tiles <= t) lo = mid;
+        if (__ldg(p.tile_start + mid) * p.f_tiles <= t) lo = mid;
         else hi = mid - 1;
       }
       g = lo;
-      mstart = __ldg(p.mtile_start + g);
-      mcount = __ldg(p.mtile_start + g + 1) - mstart;
+      tstart = __ldg(p.tile_start + g);
+      tcount = __ldg(p.tile_start + g + 1) - tstart;
       row_begin = __ldg(p.offsets + g);
       count = __ldg(p.offsets + g + 1) - row_begin;
     }
-    const int local = t - mstart * p.f_tiles;
-    const int f = local / mcount;
-    const int tt = local - f * mcount;
-    SwapTile ti;
-    ti.row0 = row_begin + tt * 128;
-    ti.n_valid = min(128, count - tt * 128);
-    ti.b_row = ti.row0;
-    ti.a_row = g * p.a_rows_per_group + f * p.a_tile_rows;
-    ti.a_part_stride = 128;
+    const int local = t - tstart * p.f_tiles;
+    const int f = local / tcount;
+    const int j = local - f * tcount;
+    GpTile ti;
+    ti.b_row = row_begin + j * kGpTokens;
+    ti.n_valid = min(kGpTokens, count - j * kGpTokens);
+    ti.a_row = g * p.a_rows_per_group + f * p.a_f_stride;
+    ti.a_box_stride = p.a_box_stride;
+    ti.a_rank_stride = p.a_rank_stride;
     ti.f0 = f * p.f_step;
-    ti.kb0 = 0;
     ti.nkb = p.nkb;
-    ti.split = 0;
     return ti;
   }
 };
 
-__device__ __forceinline__ float silu_swap(float g) { return g / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-// gate_up: accumulator part 0 = gate rows f0..f0+127, part 1 = the up rows of the same features.
-struct SwigluSwapEpi {
+// Copy-out of one transposed chunk: `rows` token rows of `width` bf16 features from shared memory
+// (row-major, width * 2 bytes per row) to out[row0 + r][f0 ...] with 16-byte stores, 128 threads.
+template <int kWidth>
+__device__ __forceinline__ void epi_copy_out(const __nv_bfloat16* tile, int rows, __nv_bfloat16* out, long long ld,
+                                             long long row0, int f0, int n_feat, bool vec_ok, int etid) {
+  constexpr int kVecPerRow = kWidth / 8;
+#pragma unroll
+  for (int pass = 0; pass < 32 * kVecPerRow / 128; ++pass) {
+    const int idx = pass * 128 + etid;
+    const int r = idx / kVecPerRow, c8 = (idx % kVecPerRow) * 8;
+    if (r >= rows) continue;
+    const int f = f0 + c8;
+    __nv_bfloat16* dst = out + (row0 + r) * ld + f;
+    const __nv_bfloat16* src = tile + r * kWidth + c8;
+    if (vec_ok && f + 8 <= n_feat) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (f + e < n_feat) dst[e] = src[e];
+    }
+  }
+}
+
+// gate_up: in each epilogue group, warps of lane quarters 0, 1 hold the gate rows of features 32q..32q+31 of
+// this CTA's 64, quarters 2, 3 the up rows of the same features.  Per 32-token chunk the gate warps hand
+// tokens 16..31 to the up warps and the up warps hand tokens 0..15 to the gate warps (fp32 through shared
+// memory, row stride 17: conflict-free), each side computes silu(gate) * up for its 16 tokens into a bf16
+// [32 tokens][64 features] tile, and the group stores the tile's rows with 16-byte vectors.
+struct SwigluGpEpi {
+  static constexpr int kXFloats = 64 * 17;
+  static constexpr int kSmemBytes = 2 * kXFloats * 4 + 32 * 64 * 2;
   struct Params {
     __nv_bfloat16* out;   // [rows, ld_out] intermediate
     int ld_out;
+    int n_feat;           // intermediate features (I)
+    bool vec_ok;          // out 16-byte aligned and ld_out % 8 == 0
   };
-  template <int NB>
-  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
-    __nv_bfloat16* col = p.out + ti.f0 + r;
+  __device__ static void run(const Params& p, const GpTile& ti, int quad, int lane, int rank, int grp,
+                             uint32_t taddr, int tok0, int ncols, uint8_t* smem, uint32_t&) {
+    float* xg = reinterpret_cast<float*>(smem);   // gate of tokens 16..31
+    float* xu = xg + kXFloats;                    // up of tokens 0..15
+    __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem + 2 * kXFloats * 4);
+    const int j = (quad & 1) * 32 + lane;
+    const bool up = quad >= 2;
+    const int fbase = ti.f0 + rank * 64;
 #pragma unroll 1
-    for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
-      uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(taddr + c0, g);
-      tmem_ld_32x32b_x32(taddr + NB + c0, u);
+    for (int c0 = 32 * grp; c0 < ncols; c0 += 64) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c0, v);
       tmem_ld_wait();
-      const int n = min(32, ti.n_valid - c0);
-      __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
+      if (up) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < n)
-          dst[static_cast<long long>(i) * p.ld_out] =
-              __float2bfloat16_rn(silu_swap(__uint_as_float(g[i])) * __uint_as_float(u[i]));
+        for (int i = 0; i < 16; ++i) xu[j * 17 + i] = __uint_as_float(v[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) xg[j * 17 + i] = __uint_as_float(v[16 + i]);
+      }
+      epi_bar_sync(grp);
+      if (up) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          tile[(16 + i) * 64 + j] = __float2bfloat16_rn(silu_f(xg[j * 17 + i]) * __uint_as_float(v[16 + i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          tile[i * 64 + j] = __float2bfloat16_rn(silu_f(__uint_as_float(v[i])) * xu[j * 17 + i]);
+      }
+      epi_bar_sync(grp);
+      epi_copy_out<64>(tile, min(32, ncols - c0), p.out, p.ld_out, ti.b_row + tok0 + c0, fbase, p.n_feat, p.vec_ok,
+                       quad * 32 + lane);
     }
   }
 };
 
-// down: accumulator parts 0 and 1 = output features f0..f0+127 and f0+128..f0+255, each token row
-// scaled by its routing weight (1 when row_scale is null).
-struct ScaleSwapEpi {
+// down: lane row r of this CTA = output feature f0 + 128 * rank + r; each token row scaled by its routing
+// weight (1 when row_scale is null).  Per 32-token chunk a group writes a bf16 [32 tokens][128 features]
+// tile (double-buffered) and stores its rows with 16-byte vectors.
+struct ScaleGpEpi {
+  static constexpr int kTileElems = 32 * 128;
+  static constexpr int kSmemBytes = 2 * kTileElems * 2;
   struct Params {
     __nv_bfloat16* out;       // [rows, ld_out]
     const float* row_scale;   // [rows] or null
     int ld_out;
     int n_total;              // valid output features
+    bool vec_ok;              // out 16-byte aligned and ld_out % 8 == 0
   };
-  template <int NB>
-  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
+  __device__ static void run(const Params& p, const GpTile& ti, int quad, int lane, int rank, int grp,
+                             uint32_t taddr, int tok0, int ncols, uint8_t* smem, uint32_t& seq) {
+    const int r = quad * 32 + lane;
+    const int fbase = ti.f0 + rank * 128;
+    const int row_base = ti.b_row + tok0;
 #pragma unroll 1
-    for (int a = 0; a < 2; ++a) {
-      const int feat = ti.f0 + a * 128 + r;
-      const bool ok = feat < p.n_total;
-      __nv_bfloat16* col = p.out + feat;
-#pragma unroll 1
-      for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + a * NB + c0, v);
-        tmem_ld_wait();
-        const int n = min(32, ti.n_valid - c0);
-        if (!ok) continue;
-        __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
+    for (int c0 = 32 * grp; c0 < ncols; c0 += 64, ++seq) {
+      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + (seq & 1u) * kTileElems;
+      const int n = min(32, ncols - c0);
+      const float my_scale = (p.row_scale && lane < n) ? __ldg(p.row_scale + row_base + c0 + lane) : 1.0f;
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c0, v);
+      tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (i < n) {
-            const float sc = p.row_scale ? __ldg(p.row_scale + ti.row0 + c0 + i) : 1.0f;
-            dst[static_cast<long long>(i) * p.ld_out] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
-          }
-        }
+      for (int i = 0; i < 32; ++i) {
+        const float sc = __shfl_sync(0xffffffffu, my_scale, i);
+        tile[i * 128 + r] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
       }
+      epi_bar_sync(grp);
+      epi_copy_out<128>(tile, n, p.out, p.ld_out, row_base + c0, fbase, p.n_total, p.vec_ok, r);
     }
   }
 };
@@ -147,69 +201,100 @@ static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
   return KDB_OK;
 }
 
-constexpr int kSwapMA = 2, kSwapNB = 128, kSwapStages = 4;
-
-template <class Epi>
-static int launch_swap(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
-                       const SwapSched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
-  using L = SwapLayout<kSwapMA, kSwapNB, kSwapStages>;
-  auto kern = gemm_swap_kernel<SwapSched, Epi, kSwapMA, kSwapNB, kSwapStages>;
-  static bool done[64] = {false};
-  int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
-  if (rc) return rc;
+// Wide staging (tiles up to 512 tokens) keeps 4 stages of 48 KB; narrow staging (at most 64 tokens per
+// group, as in decode) keeps 9 stages of 20 KB.
+template <class Epi, int ABOXES>
+static int launch_grouped_pair(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
+                               int max_group_tokens, const GroupedPairSched::Params& sp,
+                               const typename Epi::Params& ep, cudaStream_t s) {
   CUtensorMap ta;
   TokenMaps tb;
-  rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, 128);
+  int rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, 128 / ABOXES);
   if (rc) return rc;
   rc = make_token_maps(&tb, tokens, a_rows, K);
   if (rc) return rc;
-  int grid = num_sms();
-  if (!sp.mtile_start) {
-    const int tiles = ((a_rows + 127) / 128) * sp.f_tiles;
-    grid = tiles < grid ? tiles : grid;
+  int pairs = num_sms() / 2;
+  if (!sp.tile_start) {
+    const int tiles = ((a_rows + kGpTokens - 1) / kGpTokens) * sp.f_tiles;
+    pairs = tiles < pairs ? tiles : pairs;
   }
-  kern<<<grid, kGemmThreads, L::kSmemBytes, s>>>(ta, tb, sp, ep);
-  return cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGpThreads, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_group_tokens <= 64) {
+    using L = GpLayout<ABOXES, 32, 9, 2 * Epi::kSmemBytes>;
+    auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, 32, 9>;
+    static bool done[64] = {false};
+    rc = ensure_smem_attr(kern, L::kSmemBytes, done);
+    if (rc) return rc;
+    cfg.dynamicSmemBytes = L::kSmemBytes;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
+  }
+  using L = GpLayout<ABOXES, 128, 4, 2 * Epi::kSmemBytes>;
+  auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, 128, 4>;
+  static bool done[64] = {false};
+  rc = ensure_smem_attr(kern, L::kSmemBytes, done);
+  if (rc) return rc;
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
 }
 
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
-                     const int* mtile_start, void* out, cudaStream_t s) {
+                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens) {
   if (a_rows <= 0) return KDB_OK;
-  SwapSched::Params sp;
+  GroupedPairSched::Params sp;
   sp.offsets = offsets;
-  sp.mtile_start = mtile_start;
+  sp.tile_start = mtile_start;
   sp.groups = groups;
   sp.rows = a_rows;
-  sp.f_tiles = I / 128;               // 128 intermediate features (256 packed weight rows) per tile
+  sp.f_tiles = I / 128;        // one packed block (128 gate + 128 up rows) per pair tile
   sp.nkb = (H + kBK - 1) / kBK;
   sp.a_rows_per_group = 2 * I;
-  sp.a_tile_rows = 256;
+  sp.a_f_stride = 256;
+  sp.a_box_stride = 128;       // gate row r -> its up row r + 128 within the packed block
+  sp.a_rank_stride = 64;       // CTA 1 takes features 64..127 of the block
   sp.f_step = 128;
-  SwigluSwapEpi::Params ep;
+  SwigluGpEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(out);
   ep.ld_out = I;
-  return launch_swap<SwigluSwapEpi>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp, ep, s);
+  ep.n_feat = I;
+  ep.vec_ok = aligned16(out) && I % 8 == 0;
+  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
+  return launch_grouped_pair<SwigluGpEpi, 2>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, bound, sp,
+                                             ep, s);
 }
 
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
-                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s) {
+                  const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens) {
   if (a_rows <= 0) return KDB_OK;
-  SwapSched::Params sp;
+  GroupedPairSched::Params sp;
   sp.offsets = offsets;
-  sp.mtile_start = mtile_start;
+  sp.tile_start = mtile_start;
   sp.groups = groups;
   sp.rows = a_rows;
-  sp.f_tiles = (H + 255) / 256;       // 256 output features per tile
+  sp.f_tiles = (H + 255) / 256;   // 256 output features per pair tile
   sp.nkb = (I + kBK - 1) / kBK;
   sp.a_rows_per_group = H;
-  sp.a_tile_rows = 256;
+  sp.a_f_stride = 256;
+  sp.a_box_stride = 0;
+  sp.a_rank_stride = 128;
   sp.f_step = 256;
-  ScaleSwapEpi::Params ep;
+  ScaleGpEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(out);
   ep.row_scale = row_scale;
   ep.ld_out = H;
   ep.n_total = H;
-  return launch_swap<ScaleSwapEpi>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep, s);
+  ep.vec_ok = aligned16(out) && H % 8 == 0;
+  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
+  return launch_grouped_pair<ScaleGpEpi, 1>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, bound, sp, ep, s);
 }
 
 }  // namespace kdb

@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kPlanChunk)
 }
 
 // One CTA: counts[e], offsets[e] (exclusive, offsets[E] = T*k), chunk_base[c, e] (first row of
-// chunk c's slots for expert e) and mtile_start[e] (exclusive prefix of ceil(counts/128)).
+// chunk c's slots for expert e) and mtile_start[e] (exclusive prefix of ceil(counts / kMoeTokenTile)).
 __global__ void __launch_bounds__(1024)
     moe_plan_scan_kernel(const int* __restrict__ chunk_counts, int C, int E, int* __restrict__ chunk_base,
                          int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ mtile_start) {
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(1024)
   if (e < E) {
     for (int c = 0; c < C; ++c) total += chunk_counts[static_cast<long long>(c) * E + e];
   }
-  const int mt = (total + 127) / 128;
+  const int mt = (total + kMoeTokenTile - 1) / kMoeTokenTile;
   // block-wide exclusive scans of total and mt (E <= 1024)
   const int lane = e & 31, w = e >> 5;
   int a = total, b = mt;

@@ -59,7 +59,7 @@ def ep_regroup(counts, rows_in, to_expert_major, rows_out=None):
     col = c.sum(0)
     offsets = torch.zeros(Er + 1, dtype=torch.int32)
     offsets[1:] = torch.cumsum(col, 0).to(torch.int32)
-    mt = (col + 127) // 128
+    mt = (col + 511) // 512   # KDB_MOE_TOKEN_TILE
     mtile = torch.zeros(Er + 1, dtype=torch.int32)
     mtile[1:] = torch.cumsum(mt, 0).to(torch.int32)
     if rows_in is None:
