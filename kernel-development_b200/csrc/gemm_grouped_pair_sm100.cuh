@@ -31,7 +31,6 @@
 namespace kdb {
 
 constexpr int kGpTokens = 512;     // tokens of one tile at most
-constexpr unsigned int kSiteGpTokens = 0x110;   // status site: a tile exceeded the launch's token bound
 constexpr int kGpSlotCols = 256;   // TMEM columns of one accumulator slot
 
 // One pair tile.  CTA r stages weight rows a_row + r * a_rank_stride (+ a_box_stride for its second box).
@@ -43,19 +42,13 @@ struct GpTile {
   int f0;         // first output feature of the pair tile
 };
 
-// BROWS: token rows one CTA stages per token group.  128 (wide): tiles of up to 512 tokens, two groups.
-// 32 (narrow): tiles of at most 64 tokens, one group; the smaller stage leaves room for twice the stages,
-// which a weight-streaming (few tokens per expert) launch needs to keep enough HBM reads in flight.
-template <int ABOXES, int BROWS, int STAGES, int EPI_BYTES>
+template <int ABOXES, int STAGES, int EPI_BYTES>
 struct GpLayout {
   static_assert(ABOXES == 1 || ABOXES == 2, "one 128-row or two 64-row weight boxes per CTA");
-  static_assert(BROWS == 128 || BROWS == 32, "wide or narrow token staging");
-  static constexpr bool kWide = BROWS == 128;
-  static constexpr int kMaxTokens = kWide ? 512 : 64;
   static constexpr int kABoxRows = 128 / ABOXES;
   static constexpr int kABytes = 128 * kBK * 2;           // this CTA's 128 weight rows
-  static constexpr int kBRegion = BROWS * kBK * 2;        // <= BROWS token rows of one token group
-  static constexpr int kStageBytes = kABytes + (kWide ? 2 : 1) * kBRegion;
+  static constexpr int kBRegion = 128 * kBK * 2;          // <= 128 token rows of one token group
+  static constexpr int kStageBytes = kABytes + 2 * kBRegion;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   static constexpr int kBarOffset = kEpiOffset + EPI_BYTES;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
@@ -96,11 +89,11 @@ __device__ __forceinline__ void epi_bar_sync(int grp) {
   asm volatile("bar.sync %0, 128;" ::"r"(2 + 2 * grp) : "memory");
 }
 
-template <class Sched, class Epi, int ABOXES, int BROWS, int STAGES>
+template <class Sched, class Epi, int ABOXES, int STAGES>
 __global__ void __launch_bounds__(kGpThreads, 1)
     gemm_grouped_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ TokenMaps tmB,
                              const typename Sched::Params sp, const typename Epi::Params ep) {
-  using L = GpLayout<ABOXES, BROWS, STAGES, 2 * Epi::kSmemBytes>;
+  using L = GpLayout<ABOXES, STAGES, 2 * Epi::kSmemBytes>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_smem = smem + L::kEpiOffset;
@@ -157,10 +150,6 @@ __global__ void __launch_bounds__(kGpThreads, 1)
       bool ok = true;
       for (int t = pair; ok && t < ntiles; t += npairs) {
         const GpTile ti = sched.tile(t);
-        if (ti.n_valid > L::kMaxTokens) {   // the launcher's token bound was wrong: skip, flag
-          if (leader) report(KDB_ERR_DEVICE_BOUNDS, kSiteGpTokens);
-          continue;
-        }
         const GpSplit sp2(ti.n_valid);
         const int h1 = sp2.m1 / 2, h2 = sp2.m2 / 2;
         const int bi1 = box_index(h1), bi2 = box_index(h2 > 0 ? h2 : 1);
@@ -181,8 +170,7 @@ __global__ void __launch_bounds__(kGpThreads, 1)
           for (int b = 0; b < ABOXES; ++b)
             tma_load_2d_pair(st + b * L::kABoxRows * kBK * 2, &tmA, bar, kb * kBK, a_row + b * ti.a_box_stride, pol);
           tma_load_2d_pair(st + L::kABytes, &tmB.m[bi1], bar, kb * kBK, b1, pol);
-          if (L::kWide && h2 > 0)
-            tma_load_2d_pair(st + L::kABytes + L::kBRegion, &tmB.m[bi2], bar, kb * kBK, b2, pol);
+          if (h2 > 0) tma_load_2d_pair(st + L::kABytes + L::kBRegion, &tmB.m[bi2], bar, kb * kBK, b2, pol);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -210,7 +198,6 @@ __global__ void __launch_bounds__(kGpThreads, 1)
       bool issued = false, ok = true;
       for (int t = pair; ok && t < ntiles; t += npairs) {
         const GpTile ti = sched.tile(t);
-        if (ti.n_valid > L::kMaxTokens) continue;
         const GpSplit sp2(ti.n_valid);
         const int sa = next, sb = next ^ 1;
         const bool two = sp2.m2 > 0;
@@ -268,7 +255,6 @@ __global__ void __launch_bounds__(kGpThreads, 1)
     bool live = true;
     for (int t = pair; live && t < ntiles; t += npairs) {
       const GpTile ti = sched.tile(t);
-      if (ti.n_valid > L::kMaxTokens) continue;
       const GpSplit sp2(ti.n_valid);
       const int nslots = sp2.m2 > 0 ? 2 : 1;
       for (int k = 0; k < nslots; ++k) {

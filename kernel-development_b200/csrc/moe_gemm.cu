@@ -1,12 +1,16 @@
-// moe_gemm.cu — grouped expert GEMMs of the MoE layer on CTA pairs (gemm_grouped_pair_sm100.cuh): the
-// weights are the M operand (256 rows per pair), all tokens of one expert (up to 512) the N operand.
+// moe_gemm.cu — grouped expert GEMMs of the MoE layer.  Two kernels, chosen per launch by a bound on the
+// tokens any expert can hold (the caller's; T in the layer forward):
 //
-//   gate_up:  H_e = silu(X_e · Wg_eᵀ) * (X_e · Wu_eᵀ) -> bf16 intermediate.  A pair tile covers 128
-//             intermediate features; each CTA stages 64 gate rows and the 64 matching up rows (two 64-row
-//             boxes of the packed weights), so gate lands in TMEM lanes 0-63 and up in lanes 64-127; the
-//             up warps hand their values to the gate warps through shared memory.
-//   down:     Y_e = H_e · Wd_eᵀ (* routing weight of the row) -> bf16.  A pair tile covers 256 output
-//             features, 128 per CTA.
+// * more than 64: CTA pairs (gemm_grouped_pair_sm100.cuh), weights as the M operand (256 rows per pair),
+//   all tokens of one expert (up to 512) as N, so each expert's weights stream from HBM once.
+//     gate_up:  H_e = silu(X_e · Wg_eᵀ) * (X_e · Wu_eᵀ) -> bf16 intermediate.  A pair tile covers 128
+//               intermediate features; each CTA stages 64 gate rows and the 64 matching up rows (two 64-row
+//               boxes of the packed weights), so gate lands in TMEM lanes 0-63 and up in lanes 64-127, and
+//               the two halves meet through shared memory in the epilogue.
+//     down:     Y_e = H_e · Wd_eᵀ (* routing weight of the row) -> bf16.  A pair tile covers 256 output
+//               features, 128 per CTA.
+// * at most 64 (decode): one CTA per 256 weight rows on the swapped-operand core (gemm_swap_sm100.cuh),
+//   a pure weight stream; measured faster than the pairs when tiles carry this few tokens.
 //
 // The tile schedule is read on the device from the routing plan (offsets[g], and mtile_start[g], the
 // prefix of ceil(count / 512)), so no host synchronisation separates routing from the GEMMs and the whole
@@ -18,6 +22,7 @@
 // (sc_h.cu:341-381, x7_h.cu:438-590), which stream NVFP4 weights through mma.sync.
 #include "gemm_grouped_pair_sm100.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_swap_sm100.cuh"
 #include "host_util.h"
 #include "moe.h"
 
@@ -188,6 +193,118 @@ struct ScaleGpEpi {
   }
 };
 
+// ---------------------------------------------------------------------------------------------------
+// Weight-streaming path (every group holds <= 64 tokens, as in decode): one CTA per tile of 256 weight rows
+// (two 128-row parts) x the group's tokens on the single-CTA swapped-operand core (gemm_swap_sm100.cuh).
+// Measured faster than the pair kernel when the tiles carry so few tokens that the kernel only streams
+// weights.  Tiles (group g, weight tile f); a group's tile prefix counts 1 per non-empty group here.
+struct StreamSched {
+  struct Params {
+    const int* offsets;       // [groups + 1] token-row offsets, or null: one dense group of `rows` rows
+    const int* tile_start;    // [groups + 1] exclusive prefix of ceil(count / 512) (0 or 1 per group), or null
+    int groups, rows, f_tiles, nkb;
+    int a_rows_per_group;     // weight rows of one group
+    int a_tile_rows;          // weight rows one tile spans (two 128-row parts)
+    int a_part_stride;        // offset of part 1
+    int f_step;               // output features per weight tile
+  };
+  Params p;
+  int total_groups;
+  __device__ explicit StreamSched(const Params& pp) : p(pp) {
+    total_groups = p.tile_start ? p.tile_start[p.groups] : (p.rows > 0 ? 1 : 0);
+  }
+  __device__ int num_tiles() const { return total_groups * p.f_tiles; }
+  __device__ SwapTile tile(int t) const {
+    int g = 0, row_begin = 0, count = p.rows, gstart = 0;
+    if (p.tile_start) {
+      int lo = 0, hi = p.groups - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(p.tile_start + mid) * p.f_tiles <= t) lo = mid;
+        else hi = mid - 1;
+      }
+      g = lo;
+      gstart = __ldg(p.tile_start + g);
+      row_begin = __ldg(p.offsets + g);
+      count = __ldg(p.offsets + g + 1) - row_begin;
+    }
+    const int f = t - gstart * p.f_tiles;
+    SwapTile ti;
+    ti.row0 = row_begin;
+    ti.n_valid = min(64, count);
+    ti.b_row = row_begin;
+    ti.a_row = g * p.a_rows_per_group + f * p.a_tile_rows;
+    ti.a_part_stride = p.a_part_stride;
+    ti.f0 = f * p.f_step;
+    ti.kb0 = 0;
+    ti.nkb = p.nkb;
+    ti.split = 0;
+    return ti;
+  }
+};
+
+// gate_up: accumulator part 0 = gate rows f0..f0+127, part 1 = the up rows of the same features.
+struct SwigluStreamEpi {
+  struct Params {
+    __nv_bfloat16* out;   // [rows, ld_out] intermediate
+    int ld_out;
+  };
+  template <int NB>
+  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
+    __nv_bfloat16* col = p.out + ti.f0 + r;
+#pragma unroll 1
+    for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(taddr + c0, g);
+      tmem_ld_32x32b_x32(taddr + NB + c0, u);
+      tmem_ld_wait();
+      const int n = min(32, ti.n_valid - c0);
+      __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < n)
+          dst[static_cast<long long>(i) * p.ld_out] =
+              __float2bfloat16_rn(silu_f(__uint_as_float(g[i])) * __uint_as_float(u[i]));
+    }
+  }
+};
+
+// down: accumulator parts 0 and 1 = output features f0..f0+127 and f0+128..f0+255, each token row scaled
+// by its routing weight (1 when row_scale is null).
+struct ScaleStreamEpi {
+  struct Params {
+    __nv_bfloat16* out;       // [rows, ld_out]
+    const float* row_scale;   // [rows] or null
+    int ld_out;
+    int n_total;              // valid output features
+  };
+  template <int NB>
+  __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
+#pragma unroll 1
+    for (int a = 0; a < 2; ++a) {
+      const int feat = ti.f0 + a * 128 + r;
+      const bool ok = feat < p.n_total;
+      __nv_bfloat16* col = p.out + feat;
+#pragma unroll 1
+      for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + a * NB + c0, v);
+        tmem_ld_wait();
+        const int n = min(32, ti.n_valid - c0);
+        if (!ok) continue;
+        __nv_bfloat16* dst = col + static_cast<long long>(ti.row0 + c0) * p.ld_out;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (i < n) {
+            const float sc = p.row_scale ? __ldg(p.row_scale + ti.row0 + c0 + i) : 1.0f;
+            dst[static_cast<long long>(i) * p.ld_out] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
+          }
+        }
+      }
+    }
+  }
+};
+
 template <class Kern>
 static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
   int dev = 0;
@@ -201,15 +318,18 @@ static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
   return KDB_OK;
 }
 
-// Wide staging (tiles up to 512 tokens) keeps 4 stages of 48 KB; narrow staging (at most 64 tokens per
-// group, as in decode) keeps 9 stages of 20 KB.
 template <class Epi, int ABOXES>
 static int launch_grouped_pair(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
-                               int max_group_tokens, const GroupedPairSched::Params& sp,
-                               const typename Epi::Params& ep, cudaStream_t s) {
+                               const GroupedPairSched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
+  constexpr int kStages = 4;   // 48 KB per stage: 128 weight rows + two 128-row token groups
+  using L = GpLayout<ABOXES, kStages, 2 * Epi::kSmemBytes>;
+  auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, kStages>;
+  static bool done[64] = {false};
+  int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
+  if (rc) return rc;
   CUtensorMap ta;
   TokenMaps tb;
-  int rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, 128 / ABOXES);
+  rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, L::kABoxRows);
   if (rc) return rc;
   rc = make_token_maps(&tb, tokens, a_rows, K);
   if (rc) return rc;
@@ -221,6 +341,7 @@ static int launch_grouped_pair(const void* tokens, int a_rows, const void* weigh
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kGpThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -229,27 +350,51 @@ static int launch_grouped_pair(const void* tokens, int a_rows, const void* weigh
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (max_group_tokens <= 64) {
-    using L = GpLayout<ABOXES, 32, 9, 2 * Epi::kSmemBytes>;
-    auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, 32, 9>;
-    static bool done[64] = {false};
-    rc = ensure_smem_attr(kern, L::kSmemBytes, done);
-    if (rc) return rc;
-    cfg.dynamicSmemBytes = L::kSmemBytes;
-    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
-  }
-  using L = GpLayout<ABOXES, 128, 4, 2 * Epi::kSmemBytes>;
-  auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, 128, 4>;
-  static bool done[64] = {false};
-  rc = ensure_smem_attr(kern, L::kSmemBytes, done);
-  if (rc) return rc;
-  cfg.dynamicSmemBytes = L::kSmemBytes;
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, sp, ep));
+}
+
+template <class Epi>
+static int launch_stream(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
+                         const StreamSched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
+  constexpr int MA = 2, NB = 64, STAGES = 5;
+  using L = SwapLayout<MA, NB, STAGES>;
+  auto kern = gemm_swap_kernel<StreamSched, Epi, MA, NB, STAGES>;
+  static bool done[64] = {false};
+  int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
+  if (rc) return rc;
+  CUtensorMap ta;
+  TokenMaps tb;
+  rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, 128);
+  if (rc) return rc;
+  rc = make_token_maps(&tb, tokens, a_rows, K);
+  if (rc) return rc;
+  int grid = num_sms();
+  if (!sp.tile_start) grid = sp.f_tiles < grid ? sp.f_tiles : grid;
+  kern<<<grid, kGemmThreads, L::kSmemBytes, s>>>(ta, tb, sp, ep);
+  return cuda_status(cudaGetLastError());
 }
 
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
                      const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens) {
   if (a_rows <= 0) return KDB_OK;
+  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
+  if (bound <= 64) {
+    StreamSched::Params sp;
+    sp.offsets = offsets;
+    sp.tile_start = mtile_start;
+    sp.groups = groups;
+    sp.rows = a_rows;
+    sp.f_tiles = I / 128;      // 128 intermediate features (one packed block) per tile
+    sp.nkb = (H + kBK - 1) / kBK;
+    sp.a_rows_per_group = 2 * I;
+    sp.a_tile_rows = 256;
+    sp.a_part_stride = 128;
+    sp.f_step = 128;
+    SwigluStreamEpi::Params ep;
+    ep.out = static_cast<__nv_bfloat16*>(out);
+    ep.ld_out = I;
+    return launch_stream<SwigluStreamEpi>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp, ep, s);
+  }
   GroupedPairSched::Params sp;
   sp.offsets = offsets;
   sp.tile_start = mtile_start;
@@ -267,14 +412,33 @@ int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups
   ep.ld_out = I;
   ep.n_feat = I;
   ep.vec_ok = aligned16(out) && I % 8 == 0;
-  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
-  return launch_grouped_pair<SwigluGpEpi, 2>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, bound, sp,
-                                             ep, s);
+  return launch_grouped_pair<SwigluGpEpi, 2>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp, ep,
+                                             s);
 }
 
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
                   const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens) {
   if (a_rows <= 0) return KDB_OK;
+  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
+  if (bound <= 64) {
+    StreamSched::Params sp;
+    sp.offsets = offsets;
+    sp.tile_start = mtile_start;
+    sp.groups = groups;
+    sp.rows = a_rows;
+    sp.f_tiles = (H + 255) / 256;   // 256 output features (two 128-row parts) per tile
+    sp.nkb = (I + kBK - 1) / kBK;
+    sp.a_rows_per_group = H;
+    sp.a_tile_rows = 256;
+    sp.a_part_stride = 128;
+    sp.f_step = 256;
+    ScaleStreamEpi::Params ep;
+    ep.out = static_cast<__nv_bfloat16*>(out);
+    ep.row_scale = row_scale;
+    ep.ld_out = H;
+    ep.n_total = H;
+    return launch_stream<ScaleStreamEpi>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep, s);
+  }
   GroupedPairSched::Params sp;
   sp.offsets = offsets;
   sp.tile_start = mtile_start;
@@ -293,8 +457,7 @@ int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int
   ep.ld_out = H;
   ep.n_total = H;
   ep.vec_ok = aligned16(out) && H % 8 == 0;
-  const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
-  return launch_grouped_pair<ScaleGpEpi, 1>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, bound, sp, ep, s);
+  return launch_grouped_pair<ScaleGpEpi, 1>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep, s);
 }
 
 }  // namespace kdb
