@@ -76,6 +76,20 @@ size_t kdb_proj_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int kdb_proj_bf16_ws(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Projection with fp32 weights and fp32 output, for the reference's router layer ("fp32 weights and
+ * output (BF16 hi+lo pair with FP32 accumulation allowed)", src/kdev/adapters/okc_problems/
+ * muse_bf16_proj.toml:371; probe rows exact to 0.1%, :376).  Prepare once with kdb_proj_split_f32:
+ * w fp32 [n, k] -> w_split bf16 [n, 2k] = [bf16(W) | bf16(W - bf16(W))] per row (each weight kept to
+ * 2^-16 relative).  Then Y fp32 [m, n] (contiguous) = X · W_hiᵀ + X · W_midᵀ with fp32 accumulation;
+ * k % 64 == 0, x and w_split 16-byte aligned.  m <= 128 uses a K-split workspace like kdb_proj_bf16_ws
+ * (kdb_proj_f32w_workspace_bytes; NULL runs without the split).
+ */
+int kdb_proj_split_f32(const float* w, void* w_split, int64_t n, int64_t k, void* stream);
+size_t kdb_proj_f32w_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int kdb_proj_f32w(const void* x, const void* w_split, float* y, int64_t m, int64_t n, int64_t k, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* The output tile kdb_proj_bf16 picks for an m x n output on the current device: out[0] = tile width,
  * out[1] = 1 for 256-row tiles on CTA pairs, 0 for 128-row single-CTA tiles.  Host-only. */
 int kdb_proj_tile_shape(int64_t m, int64_t n, int32_t out[2]);

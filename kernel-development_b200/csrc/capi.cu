@@ -62,6 +62,18 @@ int kdb_proj_bf16_ws(const void* x, const void* w, void* y, int64_t m, int64_t n
   return kdb::proj_bf16(x, w, y, m, n, k, ldy, 0, 0, static_cast<cudaStream_t>(stream), workspace, workspace_bytes);
 }
 
+int kdb_proj_split_f32(const float* w, void* w_split, int64_t n, int64_t k, void* stream) {
+  return kdb::proj_split_f32(w, w_split, n, k, static_cast<cudaStream_t>(stream));
+}
+
+size_t kdb_proj_f32w_workspace_bytes(int64_t m, int64_t n, int64_t k) { return kdb::proj_f32w_workspace_bytes(m, n, k); }
+
+int kdb_proj_f32w(const void* x, const void* w_split, float* y, int64_t m, int64_t n, int64_t k, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 15) != 0) return KDB_ERR_INVALID_ARG;
+  return kdb::proj_f32w(x, w_split, y, m, n, k, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
 int kdb_proj_tile_shape(int64_t m, int64_t n, int32_t out[2]) {
   if (!out || m <= 0 || n <= 0) return KDB_ERR_INVALID_ARG;
   int bn = 0, pair = 0;

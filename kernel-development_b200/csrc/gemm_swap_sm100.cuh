@@ -24,9 +24,12 @@ namespace kdb {
 
 // One tile of a swapped-operand GEMM: weight rows [a_row, a_row + 128*MA) (parts a_part_stride apart),
 // token rows [b_row, b_row + n_valid), k slices [kb0, kb0 + nkb); f0 / row0 / split locate the output.
+// b_kwrap > 0: the token operand's k chunk index wraps at b_kwrap (the weights hold [W_hi | W_mid] side by
+// side along K, both multiplied by the same token row).
 struct SwapTile {
   int a_row, a_part_stride, b_row, kb0, nkb, n_valid;
   int f0, row0, split;
+  int b_kwrap = 0;
 };
 
 
@@ -134,7 +137,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int c = 0; c < KC; ++c)
             if (c < nc)
               tma_load_2d(sB + stage * L::kBBytesMax + c * L::kBChunk, &tmB.m[bi], &full[stage],
-                          (ti.kb0 + kb + c) * kBK, ti.b_row, pol_t);
+                          (ti.b_kwrap > 0 ? (ti.kb0 + kb + c) % ti.b_kwrap : ti.kb0 + kb + c) * kBK, ti.b_row,
+                          pol_t);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(256)
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if (lane == 0) norms[e] = __double2float_ru(sqrt(ss) * (1.0 + 1e-12));
+  if (lane == 0 && norms) norms[e] = __double2float_ru(sqrt(ss) * (1.0 + 1e-12));
 }
 
 // fp32 output tile of the approx-logit GEMM: out[row, col] = accumulator (row < M, col < N).

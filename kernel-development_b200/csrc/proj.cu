@@ -8,6 +8,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_swap_sm100.cuh"
 #include "host_util.h"
+#include "moe.h"
 #include "proj.h"
 
 namespace kdb {
@@ -209,6 +210,7 @@ static int launch_proj_pair(const void* x, const void* w, void* y, int M, int N,
 struct ProjSwapSched {
   struct Params {
     int M, N, f_tiles, t_tiles, splits, nkb_total, nkb_per, nb;   // nb: token rows per tile
+    int b_kwrap;                                                  // 0, or the token k chunks (wrap)
   };
   Params p;
   __device__ explicit ProjSwapSched(const Params& pp) : p(pp) {}
@@ -229,13 +231,15 @@ struct ProjSwapSched {
     ti.nkb = min(p.nkb_per, p.nkb_total - ti.kb0);
     ti.f0 = f * 128;
     ti.split = sp;
+    ti.b_kwrap = p.b_kwrap;
     return ti;
   }
 };
 
 struct ProjSwapEpi {
   struct Params {
-    __nv_bfloat16* y;   // used when partial is null
+    __nv_bfloat16* y;   // used when partial and y32 are null
+    float* y32;         // fp32 output instead of y (when partial is null), or null
     float* partial;     // [splits, M, N] fp32, or null
     long long ldy;
     int M, N;
@@ -256,6 +260,11 @@ struct ProjSwapEpi {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           if (i < n) dst[static_cast<long long>(i) * p.N] = __uint_as_float(v[i]);
+      } else if (p.y32) {
+        float* dst = p.y32 + static_cast<long long>(ti.row0 + c0) * p.ldy + feat;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < n) dst[static_cast<long long>(i) * p.ldy] = __uint_as_float(v[i]);
       } else {
         __nv_bfloat16* dst = p.y + static_cast<long long>(ti.row0 + c0) * p.ldy + feat;
 #pragma unroll
@@ -266,17 +275,18 @@ struct ProjSwapEpi {
   }
 };
 
-// y[m, n] = bf16(sum_s partial[s, m, n]), s ascending.
+// y[m, n] = bf16(sum_s partial[s, m, n]) (or the fp32 sum into y32), s ascending.
 __global__ void __launch_bounds__(256)
-    proj_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ y, long long ldy, int M, int N,
-                       int splits) {
+    proj_reduce_kernel(const float* __restrict__ partial, __nv_bfloat16* __restrict__ y, float* __restrict__ y32,
+                       long long ldy, int M, int N, int splits) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(M) * N;
   if (idx >= total) return;
   const long long m = idx / N, n = idx % N;
   float acc = 0.f;
   for (int s = 0; s < splits; ++s) acc += partial[static_cast<long long>(s) * total + idx];
-  y[m * ldy + n] = __float2bfloat16_rn(acc);
+  if (y32) y32[m * ldy + n] = acc;
+  else y[m * ldy + n] = __float2bfloat16_rn(acc);
 }
 
 // K split of the small-M path: minimises (W bytes + partial traffic) / wave efficiency.
@@ -309,9 +319,12 @@ size_t proj_workspace_bytes(long long M, long long N, long long K) {
   return s > 1 ? static_cast<size_t>(s) * M * N * sizeof(float) : 0;
 }
 
+// y32 (fp32 output) replaces y when not null.  kx: the token operand's width when the weights are
+// [W_hi | W_mid] (K = 2 kx, token k chunks wrap at kx); 0 otherwise.
 template <int NB, int STAGES, int KC>
 static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
-                               void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                               void* workspace, size_t ws_bytes, cudaStream_t stream, float* y32 = nullptr,
+                               int kx = 0) {
   constexpr int MA = 1;
   using L = SwapLayout<MA, NB, STAGES, KC>;
   auto kern = gemm_swap_kernel<ProjSwapSched, ProjSwapEpi, MA, NB, STAGES, KC>;
@@ -330,9 +343,10 @@ static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int
   TokenMaps tb;
   int rc = make_tmap_bf16_2d(&ta, w, K, N, K, kBK, 128);
   if (rc) return rc;
-  rc = make_token_maps(&tb, x, M, K);
+  rc = make_token_maps(&tb, x, M, kx > 0 ? kx : K);
   if (rc) return rc;
   ProjSwapSched::Params sp;
+  sp.b_kwrap = kx > 0 ? kx / kBK : 0;
   sp.M = M;
   sp.N = N;
   sp.f_tiles = (N + 127) / 128;
@@ -343,6 +357,7 @@ static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int
   sp.nkb_per = (sp.nkb_total + splits - 1) / splits;
   ProjSwapEpi::Params ep;
   ep.y = static_cast<__nv_bfloat16*>(y);
+  ep.y32 = y32;
   ep.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   ep.ldy = ldy;
   ep.M = M;
@@ -354,7 +369,7 @@ static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int
   if (rc || splits == 1) return rc;
   const long long total = static_cast<long long>(M) * N;
   proj_reduce_kernel<<<static_cast<unsigned int>((total + 255) / 256), 256, 0, stream>>>(
-      static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(y), ldy, M, N, splits);
+      static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(y), y32, ldy, M, N, splits);
   return cuda_status(cudaGetLastError());
 }
 
@@ -433,6 +448,46 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
     case 64: return launch_proj_cfg<64, 8>(x, w, y, (int)M, (int)N, (int)K, ldy, stream);
     default: return KDB_ERR_INVALID_ARG;
   }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// Projection with fp32 weights and fp32 output: the reference's router layer, whose precision rule is
+// "fp32 weights and output (BF16 hi+lo pair with FP32 accumulation allowed)"
+// (src/kdev/adapters/okc_problems/muse_bf16_proj.toml:371).  proj_split_f32 stores, once,
+// w_split[n] = [bf16(W[n]) | bf16(W[n] - bf16(W[n]))] (n x 2k, lossless to 2^-16 of each weight: the
+// probe-row rule's 0.1% holds), and Y = X · W_hiᵀ + X · W_midᵀ is one bf16 GEMM over K = 2k whose token
+// operand repeats along K: the small-M swapped path wraps the token k chunk at k, the tiled path
+// (router_approx) wraps A's k coordinate.
+int proj_split_f32(const float* w, void* w_split, long long N, long long K, cudaStream_t stream) {
+  if (N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
+  if (N == 0 || K == 0) return KDB_OK;
+  if (!w || !w_split) return KDB_ERR_INVALID_ARG;
+  if (N > (1ll << 24) || K > (1ll << 30) || N * K > (1ll << 40)) return KDB_ERR_UNSUPPORTED;
+  return router_prepare(w, w_split, nullptr, static_cast<int>(N), static_cast<int>(K), stream);
+}
+
+size_t proj_f32w_workspace_bytes(long long M, long long N, long long K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > 128) return 0;
+  const int s = proj_small_m_splits(M, N, 2 * K, num_sms());
+  return s > 1 ? static_cast<size_t>(s) * M * N * sizeof(float) : 0;
+}
+
+int proj_f32w(const void* x, const void* w_split, float* y, long long M, long long N, long long K, void* workspace,
+              size_t ws_bytes, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return KDB_ERR_INVALID_ARG;
+  if (M == 0 || N == 0) return KDB_OK;
+  if (!y) return KDB_ERR_INVALID_ARG;
+  if (M > (1ll << 30) || N > (1ll << 30) || K > (1ll << 29) || M * N > (1ll << 31) / 4) return KDB_ERR_UNSUPPORTED;
+  if (K == 0) return cuda_status(cudaMemsetAsync(y, 0, static_cast<size_t>(M) * N * sizeof(float), stream));
+  if (!x || !w_split) return KDB_ERR_INVALID_ARG;
+  if (K % kBK != 0) return KDB_ERR_UNSUPPORTED;   // the token operand wraps on whole 64-wide k chunks
+  if (!aligned16(x) || !aligned16(w_split)) return KDB_ERR_INVALID_ARG;
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k2 = static_cast<int>(2 * K);
+  if (M <= 32)
+    return launch_proj_small_m<32, 5, 2>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
+  if (M <= 128)
+    return launch_proj_small_m<128, 6, 1>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
+  return router_approx(x, w_split, y, m, static_cast<int>(K), n, stream);
 }
 
 }  // namespace kdb

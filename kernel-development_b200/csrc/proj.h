@@ -13,4 +13,11 @@ void pick_tile(long long M, long long N, long long sms, int* bn, int* pair);
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
               int force_bn, int cta_pair, cudaStream_t stream, void* workspace = nullptr, size_t ws_bytes = 0);
 size_t proj_workspace_bytes(long long M, long long N, long long K);
+
+// fp32-weight projection (router layer): w_split = [bf16(W) | bf16(W - bf16(W))] (N x 2K) from
+// proj_split_f32; Y fp32 [M, N] contiguous.  K % 64 == 0.
+int proj_split_f32(const float* w, void* w_split, long long N, long long K, cudaStream_t stream);
+size_t proj_f32w_workspace_bytes(long long M, long long N, long long K);
+int proj_f32w(const void* x, const void* w_split, float* y, long long M, long long N, long long K, void* workspace,
+              size_t ws_bytes, cudaStream_t stream);
 }  // namespace kdb

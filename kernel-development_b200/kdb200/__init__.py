@@ -6,6 +6,6 @@ Host-side layer over libkdb200.so (include/kdb200.h).  Public surface:
   submissions/*.py                            kdev submission files: prepare(weights), kernel_fn(data, state)
 """
 from . import _lib
-from .proj import proj, proj_into
+from .proj import proj, proj_f32w, proj_into, split_f32
 
-__all__ = ["proj", "proj_into", "_lib"]
+__all__ = ["proj", "proj_into", "proj_f32w", "split_f32", "_lib"]

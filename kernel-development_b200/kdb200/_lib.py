@@ -35,6 +35,9 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_proj_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "kdb_proj_bf16_ws": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "kdb_proj_tile_shape": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(ctypes.c_int32)]),
+    "kdb_proj_split_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
+    "kdb_proj_f32w_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "kdb_proj_f32w": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "kdb_proj_bf16_cfg": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp]),
     "kdb_moe_workspace_bytes": (_c_size, [_c_i64] * 7),
     "kdb_moe_pack_gate_up": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),

@@ -68,3 +68,45 @@ def proj(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 @proj.register_fake
 def _proj_fake(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return x.new_empty((x.shape[0], w.shape[0]))
+
+
+# ------------------------------------------------------------------------- fp32 weights (router layer)
+def split_f32(w: torch.Tensor) -> torch.Tensor:
+    """w fp32 [N, K] -> w_split bf16 [N, 2K] = [bf16(W) | bf16(W - bf16(W))] per row (prepare step of the
+    router layer: "fp32 weights and output (BF16 hi+lo pair with FP32 accumulation allowed)",
+    src/kdev/adapters/okc_problems/muse_bf16_proj.toml:371).  The caller's w is not modified."""
+    if not w.is_cuda or w.dtype != torch.float32 or w.dim() != 2:
+        raise TypeError("w must be a 2-D fp32 CUDA tensor")
+    w = w.contiguous()
+    n, k = w.shape
+    out = torch.empty((n, 2 * k), dtype=torch.bfloat16, device=w.device)
+    with torch.cuda.device(w.device):
+        rc = _lib.lib().kdb_proj_split_f32(w.data_ptr(), out.data_ptr(), n, k,
+                                           torch.cuda.current_stream(w.device).cuda_stream)
+    _lib.check("kdb_proj_split_f32", rc)
+    return out
+
+
+@torch.library.custom_op("kdb200::proj_f32w", mutates_args=())
+def proj_f32w(x: torch.Tensor, w_split: torch.Tensor) -> torch.Tensor:
+    """Y fp32 [M, N] = X[M, K] · (W_hi + W_mid)ᵀ, w_split = split_f32(W) ([N, 2K] bf16), fp32 accumulation."""
+    _check_operand("x", x)
+    _check_operand("w_split", w_split)
+    m, k = x.shape
+    n, k2 = w_split.shape
+    if k2 != 2 * k:
+        raise ValueError(f"x is [{m}, {k}] but w_split is [{n}, {k2}]: expected [{n}, {2 * k}]")
+    y = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        nbytes = int(_lib.lib().kdb_proj_f32w_workspace_bytes(m, n, k)) if m > 0 and n > 0 and k > 0 else 0
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device) if nbytes else None
+        rc = _lib.lib().kdb_proj_f32w(x.data_ptr(), w_split.data_ptr(), y.data_ptr(), m, n, k,
+                                      None if ws is None else ws.data_ptr(), nbytes,
+                                      torch.cuda.current_stream(x.device).cuda_stream)
+    _lib.check("kdb_proj_f32w", rc)
+    return y
+
+
+@proj_f32w.register_fake
+def _proj_f32w_fake(x: torch.Tensor, w_split: torch.Tensor) -> torch.Tensor:
+    return x.new_empty((x.shape[0], w_split.shape[0]), dtype=torch.float32)

@@ -89,9 +89,22 @@ def proj_weight(k: int, n: int, seed: int = 0, device="cpu") -> torch.Tensor:
     return _randn((n, k), seed * 1000 + _TID_W, device, 1.0 / math.sqrt(k))
 
 
-def proj_input(m: int, k: int, seed: int = 0, device="cpu") -> torch.Tensor:
-    """X[m, k] bf16 ~ N(0, 1)."""
-    return _randn((m, k), seed * 1000 + _TID_X, device)
+def proj_input(m: int, k: int, seed: int = 0, device="cpu", dist: str = "normal") -> torch.Tensor:
+    """X[m, k] bf16 ~ N(0, 1).  dist="outliers": additionally 1 in 64 elements (seeded positions) scaled
+    by 64, the heavy-tailed activation case of the reference's test lists (`dist = "outliers"`)."""
+    x = _randn((m, k), seed * 1000 + _TID_X, device)
+    if dist == "outliers":
+        g = torch.Generator().manual_seed(seed * 1000 + _TID_X + 500)
+        mask = (torch.rand((m, k), generator=g) < 1.0 / 64).to(x.device)
+        x = torch.where(mask, (x.float() * 64).to(torch.bfloat16), x)
+    elif dist != "normal":
+        raise ValueError(f"unknown input distribution {dist!r}")
+    return x
+
+
+def proj_weight_f32(k: int, n: int, seed: int = 0, device="cpu") -> torch.Tensor:
+    """W[n, k] fp32 ~ N(0, 1/k): the router layer's fp32 weights."""
+    return _randn((n, k), seed * 1000 + _TID_ROUTER, device, 1.0 / math.sqrt(k), torch.float32)
 
 
 # ---------------------------------------------------------------------------------------------- MoE

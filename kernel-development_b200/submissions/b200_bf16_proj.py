@@ -9,13 +9,27 @@ _PKG = str(Path(__file__).resolve().parent.parent)
 if _PKG not in sys.path:
     sys.path.insert(0, _PKG)
 
+import torch  # noqa: E402
+
 from kdb200 import proj as _proj  # noqa: E402
+from kdb200 import proj_f32w as _proj_f32w  # noqa: E402
+from kdb200 import split_f32 as _split_f32  # noqa: E402
 
 
 def prepare(weights):
-    """Weights are kept as given (bf16, bit-exact); one contiguous [N, K] tensor per layer."""
-    return {layer: w.contiguous() for layer, w in weights.items()}
+    """bf16 layers are kept as given (bit-exact, one contiguous [N, K] tensor each); an fp32 layer (the
+    router) is stored as its lossless-to-2^-16 bf16 hi+mid pair [N, 2K] next to the untouched original."""
+    state = {}
+    for layer, w in weights.items():
+        if w.dtype == torch.float32:
+            state[layer] = ("f32", _split_f32(w))
+        else:
+            state[layer] = ("bf16", w.contiguous())
+    return state
 
 
 def kernel_fn(data, state):
-    return _proj(data["x"], state[data["config"]["layer"]])
+    kind, w = state[data["config"]["layer"]]
+    if kind == "f32":
+        return _proj_f32w(data["x"], w)
+    return _proj(data["x"], w)

@@ -3,7 +3,9 @@ OKC adapter imports: src/kdev/adapters/okc.py:476-575); the product never import
 
 API (the one kdev's OkcAdapter calls): generate_weights(seed), generate_input(m, layer, seed),
 check_implementation(data, out, weights) -> (ok, msg), speed_of_light_ns(m, layer, hw).
-Weights: one bf16 W[N, K] per layer; input {"x": bf16[m, K], "config": {"m", "layer"}}.
+Weights: one bf16 W[N, K] per layer, and fp32 W for the "router" layer (the reference's precision rule:
+fp32 weights and output, BF16 hi+lo pair with FP32 accumulation allowed, muse_bf16_proj.toml:371);
+input {"x": bf16[m, K], "config": {"m", "layer"[, "dist"]}}.
 """
 import sys
 from pathlib import Path
@@ -20,7 +22,8 @@ from oracle import proj as op  # noqa: E402
 
 WEIGHTS_SEED = 0
 REL_L2_TOL = op.REL_FRO_TOL
-LAYERS = {"k2048_n2048": (2048, 2048), "k7168_n7168": (7168, 7168)}
+LAYERS = {"k2048_n2048": (2048, 2048), "k7168_n7168": (7168, 7168), "router": (7168, 256)}
+FP32_LAYERS = {"router"}
 
 
 def _dev(device):
@@ -28,18 +31,28 @@ def _dev(device):
 
 
 def generate_weights(seed, device="cuda"):
-    return {name: W.proj_weight(k, n, seed * 10 + i, _dev(device)) for i, (name, (k, n)) in enumerate(LAYERS.items())}
+    out = {}
+    for i, (name, (k, n)) in enumerate(LAYERS.items()):
+        gen = W.proj_weight_f32 if name in FP32_LAYERS else W.proj_weight
+        out[name] = gen(k, n, seed * 10 + i, _dev(device))
+    return out
 
 
-def generate_input(m, layer, seed, device="cuda", **_):
+def generate_input(m, layer, seed, device="cuda", dist="normal", **_):
     k, _n = LAYERS[layer]
-    return {"x": W.proj_input(int(m), k, int(seed), _dev(device)), "config": {"m": int(m), "layer": layer}}
+    cfg = {"m": int(m), "layer": layer}
+    if dist != "normal":
+        cfg["dist"] = dist
+    return {"x": W.proj_input(int(m), k, int(seed), _dev(device), dist), "config": cfg}
 
 
 def check_implementation(data, output, weights):
-    w = weights[data["config"]["layer"]]
+    layer = data["config"]["layer"]
+    w = weights[layer]
     if not isinstance(output, torch.Tensor):
         return False, "expected a tensor"
+    if layer in FP32_LAYERS:
+        return op.check_f32w(output.detach().cpu(), op.proj_ref_f32w(data["x"], w))
     return op.check(output.detach().cpu(), op.proj_ref(data["x"], w))
 
 

@@ -18,6 +18,29 @@ def proj_ref(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return x.detach().cpu().float() @ w.detach().cpu().float().T
 
 
+# fp32-weight (router) layer: the hi+mid split keeps each weight to 2^-16 and accumulation is fp32, so
+# the output is checked far tighter than the bf16 layers.
+ROUTER_REL_FRO_TOL = 1e-4
+ROUTER_MAX_ABS_TOL = 1e-3
+PROBE_REL_TOL = 1e-3   # probe rows (one nonzero power-of-two input) exact to 0.1% (muse_bf16_proj.toml:376)
+
+
+def proj_ref_f32w(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """fp32 [M, N] = x · wᵀ with fp32 weights, accumulated in fp64 on the CPU (the router layer)."""
+    return (x.detach().cpu().double() @ w.detach().cpu().double().T).float()
+
+
+def check_f32w(out: torch.Tensor, ref: torch.Tensor) -> tuple[bool, str]:
+    """(ok, message) for the fp32-output router layer."""
+    if tuple(out.shape) != tuple(ref.shape) or out.dtype != torch.float32:
+        return False, f"expected fp32 {tuple(ref.shape)}, got {out.dtype} {tuple(out.shape)}"
+    c = compare(out, ref)
+    ok = c["nonfinite"] == 0 and c["max_abs"] <= ROUTER_MAX_ABS_TOL and c["rel_fro"] <= ROUTER_REL_FRO_TOL
+    msg = (f"relative L2 error {c['rel_fro']:.3e} (worst row {c['worst_row']:.3e}) max-abs {c['max_abs']:.3e} "
+           f"[bound {ROUTER_REL_FRO_TOL}: max-abs <= {ROUTER_MAX_ABS_TOL}]")
+    return ok, msg
+
+
 def compare(out: torch.Tensor, ref: torch.Tensor) -> dict:
     """max-abs, relative Frobenius and worst-row relative L2 error of `out` against fp32 `ref`."""
     o = out.detach().cpu().float()

@@ -177,3 +177,85 @@ def test_deterministic_and_row_independent():
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
     assert torch.equal(y3, y1[perm])
+
+
+# ------------------------------------------------------------------------- fp32 weights (router layer)
+# Tolerance (the oracle's router-layer bound): relative Frobenius <= 1e-4 and max-abs <= 1e-3 against the
+# fp64-accumulated product with the fp32 weights; probe rows exact to 0.1% (muse_bf16_proj.toml:376).
+@pytest.mark.parametrize("m,k,n,dist", [
+    (1, 7168, 256, "normal"), (8, 7168, 256, "normal"), (9, 7168, 256, "outliers"), (32, 7168, 256, "normal"),
+    (33, 7168, 256, "normal"), (128, 7168, 256, "normal"), (129, 7168, 256, "normal"), (300, 7168, 256, "normal"),
+    (1000, 512, 100, "outliers"), (24, 640, 130, "normal"),
+])
+def test_f32w_matches_oracle(m, k, n, dist):
+    from kdb200 import proj_f32w, split_f32
+    x = W.proj_input(m, k, m + 3, dist=dist)
+    w = W.proj_weight_f32(k, n, n + 1)
+    gw = w.cuda()
+    split = split_f32(gw)
+    assert torch.equal(gw.cpu(), w)   # the caller's weights are untouched
+    y = proj_f32w(x.cuda(), split)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32
+    ok, msg = op.check_f32w(y.cpu(), op.proj_ref_f32w(x, w))
+    assert ok, msg
+    # a bf16 rounding of the weights would not pass the router bound: the hi+mid pair is doing its job
+    rough = op.proj_ref_f32w(x, w.to(torch.bfloat16).float())
+    assert not op.check_f32w(rough, op.proj_ref_f32w(x, w))[0]
+
+
+@pytest.mark.parametrize("m", [1, 16, 200])
+def test_f32w_probe_rows_exact(m):
+    """One nonzero power-of-two input per row returns that weight column scaled, to 0.1% per element."""
+    from kdb200 import proj_f32w, split_f32
+    k, n = 7168, 256
+    w = W.proj_weight_f32(k, n, 11)
+    g = torch.Generator().manual_seed(m)
+    cols = torch.randint(0, k, (m,), generator=g)
+    pw = torch.randint(-6, 7, (m,), generator=g).float()
+    x = torch.zeros((m, k), dtype=torch.float32)
+    x[torch.arange(m), cols] = torch.pow(2.0, pw)
+    y = proj_f32w(x.to(torch.bfloat16).cuda(), split_f32(w.cuda())).cpu()
+    torch.cuda.synchronize()
+    want = w[:, cols].T * torch.pow(2.0, pw)[:, None]
+    rel = ((y - want).abs() / want.abs().clamp_min(1e-30)).max().item()
+    assert rel <= op.PROBE_REL_TOL, rel
+
+
+def test_f32w_through_submission_and_graph():
+    """The submission's prepare/kernel_fn route the fp32 router layer to kdb_proj_f32w; graph replay equals eager."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "b200_bf16_proj_sub", Path(__file__).resolve().parent.parent / "kernel-development_b200" / "submissions" /
+        "b200_bf16_proj.py")
+    sub = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sub)
+    w = W.proj_weight_f32(7168, 256, 5)
+    state = sub.prepare({"router": w.cuda()})
+    x = W.proj_input(16, 7168, 2, device="cuda")
+    data = {"x": x, "config": {"m": 16, "layer": "router"}}
+    y = sub.kernel_fn(data, state)
+    torch.cuda.synchronize()
+    assert op.check_f32w(y.cpu(), op.proj_ref_f32w(x, w))[0]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        sub.kernel_fn(data, state)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        yg = sub.kernel_fn(data, state)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(yg, y)
+
+
+def test_f32w_rejects_bad_shapes():
+    from kdb200 import _lib as L
+    from kdb200 import proj_f32w, split_f32
+    with pytest.raises(ValueError):
+        proj_f32w(torch.zeros((4, 64), dtype=torch.bfloat16, device="cuda"),
+                  torch.zeros((8, 64), dtype=torch.bfloat16, device="cuda"))     # w_split not [n, 2k]
+    with pytest.raises(L.KdbError):                                               # k % 64 != 0
+        proj_f32w(torch.zeros((4, 72), dtype=torch.bfloat16, device="cuda"),
+                  split_f32(torch.zeros((8, 72), dtype=torch.float32, device="cuda")))
