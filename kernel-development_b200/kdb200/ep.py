@@ -13,6 +13,11 @@ shared expert are replicated.  One layer call on rank r:
   7. owner: regroup back to source-major, all-to-all the rows home
   8. combine: y[t] = sum_j w[t, j] * row(t, j) (+ shared expert on local tokens)   kdb_moe_combine
 
+The all-to-alls are issued asynchronously (NCCL runs them on its own stream): the shared expert runs
+while the dispatched rows cross NVLink, and when every local expert still sees >= 512 tokens per slice
+the call is split into two micro-batches, so that while one slice's rows are in flight the tensor cores
+work on the other's.
+
 The reference simulates a single expert-parallel rank and computes only its local routes
 (src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:31,136); this is the real exchange.
 """
@@ -77,12 +82,6 @@ class ExpertParallelMoE:
         _, w, ids = self.ops.route(x, self.router, self.router_bias, self.k)
         return w, ids
 
-    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
-        if self.P == 1:
-            out.copy_(inp)
-            return
-        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
-
     # Phases of one call (forward composes them around the two all-to-alls; tests on one GPU emulate
     # the exchange between several instances).
     def dispatch(self, x: torch.Tensor) -> dict:
@@ -104,34 +103,83 @@ class ExpertParallelMoE:
         back, _, _ = ops.ep_regroup(recv_counts, yg, to_expert_major=False)
         return back
 
-    def finish(self, st: dict, ret: torch.Tensor):
-        """Weighted combine of the returned rows (+ shared expert on the local tokens)."""
+    def shared_rows(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+        """The shared expert's output rows for local tokens x (None without a shared expert)."""
+        if self.shared_gate_up_packed is None:
+            return None
+        hs = self.ops.expert_gate_up(x, self.shared_gate_up_packed[0:1])
+        return self.ops.expert_down(hs, self.shared_down[0:1])
+
+    def finish(self, st: dict, ret: torch.Tensor, shared: Optional[torch.Tensor] = None):
+        """Weighted combine of the returned rows (+ shared expert on the local tokens; computed here
+        unless the caller passes its rows)."""
         x = st["x"]
         T = x.shape[0]
-        shared = None
-        if self.shared_gate_up_packed is not None:
-            hs = self.ops.expert_gate_up(x, self.shared_gate_up_packed[0:1])
-            shared = self.ops.expert_down(hs, self.shared_down[0:1])
+        if shared is None and self.shared_gate_up_packed is not None:
+            shared = self.shared_rows(x)
         y = self.ops.combine(ret, st["slot_pos"], T, self.k, slot_w=st["w"], shared_rows=shared)
         return y, st["w"], st["ids"]
 
-    def forward(self, x: torch.Tensor):
-        """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32)."""
+    def _exchange(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits):
+        """Row all-to-all; asynchronous when P > 1 (returns the work handle to wait on, else None)."""
+        if self.P == 1:
+            out.copy_(inp)
+            return None
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=True)
+
+    def forward(self, x: torch.Tensor, micro_batches: Optional[int] = None):
+        """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32).
+
+        micro_batches: token slices whose exchanges overlap each other's expert GEMMs.  Default: 2 when
+        P > 1 and a local expert still sees >= 512 tokens per slice on average (T_r k P / E >= 1024), else 1
+        (below that, slicing would stream every expert's weights once per slice).  Every rank must use the
+        same count (each slice is one round of all-to-alls)."""
         T, H = x.shape
-        st = self.dispatch(x)
-        send_counts = st["send_counts"]
+        if micro_batches is None:
+            micro_batches = 2 if self.P > 1 and T * self.k * self.P >= 1024 * self.E else 1
+        nb = micro_batches
+        nb = max(1, min(int(nb), max(T, 1)))
+        bounds = [T * i // nb for i in range(nb + 1)]
+        sts = [self.dispatch(x[bounds[i]:bounds[i + 1]]) for i in range(nb)]
+        # the counts of every micro-batch in one exchange, then the one host read-back of the split sizes
+        send_counts = torch.stack([st["send_counts"] for st in sts])          # [nb, P, Er]
         recv_counts = torch.empty_like(send_counts)
         if self.P > 1:
-            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+            self._count_exchange(recv_counts, send_counts)
         else:
             recv_counts.copy_(send_counts)
-        both = torch.stack([send_counts.sum(1), recv_counts.sum(1)]).cpu()    # the one host read-back
-        send_rows, recv_rows = both[0].tolist(), both[1].tolist()
-        recv = torch.empty((int(sum(recv_rows)), H), dtype=st["send"].dtype, device=x.device)
-        self._all_to_all(recv, st["send"], recv_rows, send_rows)
-        back = self.owner_compute(recv, recv_counts)
-        ret = torch.empty((T * self.k, H), dtype=back.dtype, device=x.device)
-        self._all_to_all(ret, back, send_rows, recv_rows)
-        return self.finish(st, ret)
+        both = torch.stack([send_counts.sum(2), recv_counts.sum(2)]).cpu()    # [2, nb, P]
+        recvs, works = [], []
+        for i, st in enumerate(sts):
+            send_rows, recv_rows = both[0, i].tolist(), both[1, i].tolist()
+            recv = torch.empty((int(sum(recv_rows)), H), dtype=st["send"].dtype, device=x.device)
+            works.append(self._exchange(recv, st["send"], recv_rows, send_rows))
+            recvs.append((recv, send_rows, recv_rows))
+        shared = [self.shared_rows(st["x"]) for st in sts]   # the shared expert runs while rows are in flight
+        rets = []
+        for i in range(nb):
+            if works[i] is not None:
+                works[i].wait()                      # the compute stream waits for this slice's rows only
+            recv, send_rows, recv_rows = recvs[i]
+            back = self.owner_compute(recv, recv_counts[i])
+            ret = torch.empty(((bounds[i + 1] - bounds[i]) * self.k, H), dtype=back.dtype, device=x.device)
+            rets.append((ret, self._exchange(ret, back, send_rows, recv_rows), back))
+        outs = []
+        for i, st in enumerate(sts):
+            ret, work, _back = rets[i]                       # _back stays referenced until its send is done
+            if work is not None:
+                work.wait()
+            outs.append(self.finish(st, ret, shared[i]))
+        if nb == 1:
+            return outs[0]
+        return tuple(torch.cat([o[j] for o in outs]) for j in range(3))
+
+    def _count_exchange(self, recv_counts: torch.Tensor, send_counts: torch.Tensor) -> None:
+        """recv_counts[b, s] = what rank s sent here in micro-batch b (send_counts[b, p] went to rank p)."""
+        nb = send_counts.shape[0]
+        snd = send_counts.transpose(0, 1).contiguous()            # [P, nb, Er]: destination-major
+        rcv = torch.empty_like(snd)                               # [P, nb, Er]: source-major
+        dist.all_to_all_single(rcv.view(self.P, -1), snd.view(self.P, -1), group=self.group)
+        recv_counts.copy_(rcv.transpose(0, 1))
 
     __call__ = forward

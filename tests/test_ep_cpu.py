@@ -24,7 +24,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cfg_args, queue):
+def _worker(rank, world, port, cfg_args, queue, micro_batches=None):
     import datetime
     for p in (str(ROOT), str(ROOT / "kernel-development_b200"), str(ROOT / "tests")):
         if p not in sys.path:
@@ -41,7 +41,7 @@ def _worker(rank, world, port, cfg_args, queue):
         wts = W.moe_weights(cfg, seed=3)                  # same full layer on every rank
         x = W.moe_input(cfg.t, cfg.h, seed=10 + rank)     # each rank its own tokens
         layer = EP.ExpertParallelMoE(wts, cfg.k, ops=ep_cpu_ops)
-        y, w, ids = layer(x)
+        y, w, ids = layer(x, micro_batches=micro_batches)
         ref = om.moe_ref(x, wts, cfg.k)
         ok_ids = bool(torch.equal(ids, ref["ids"]))
         c = om.compare(y, ref["y32"])
@@ -51,15 +51,17 @@ def _worker(rank, world, port, cfg_args, queue):
         queue.put((rank, False, 1e9, 1e9, repr(e)))
 
 
-@pytest.mark.parametrize("cfg_args", [
-    ("ep_small", 48, 64, 8, 128, 2),
-    ("ep_shared_skew", 40, 64, 16, 128, 4, 1, 128, 1.2),
+@pytest.mark.parametrize("cfg_args,micro_batches", [
+    (("ep_small", 48, 64, 8, 128, 2), None),
+    (("ep_shared_skew", 40, 64, 16, 128, 4, 1, 128, 1.2), None),
+    # three micro-batches: asynchronous exchanges of one slice overlap another slice's expert compute
+    (("ep_micro", 50, 64, 8, 128, 2, 1, 128), 3),
 ])
-def test_expert_parallel_host_logic_gloo(cfg_args):
+def test_expert_parallel_host_logic_gloo(cfg_args, micro_batches):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfg_args, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfg_args, q, micro_batches)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=180) for _ in procs]
