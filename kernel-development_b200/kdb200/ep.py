@@ -13,10 +13,10 @@ shared expert are replicated.  One layer call on rank r:
   7. owner: regroup back to source-major, all-to-all the rows home
   8. combine: y[t] = sum_j w[t, j] * row(t, j) (+ shared expert on local tokens)   kdb_moe_combine
 
-The all-to-alls are issued asynchronously (NCCL runs them on its own stream): the shared expert runs
-while the dispatched rows cross NVLink, and when every local expert still sees >= 512 tokens per slice
-the call is split into two micro-batches, so that while one slice's rows are in flight the tensor cores
-work on the other's.
+The all-to-alls are issued asynchronously (NCCL runs them on its own stream) and a call may be split into
+micro-batches, so that while one slice's rows are in flight the tensor cores work on another's.  That
+overlap is off by default: on 8 B200s it was not faster, since the persistent expert GEMMs occupy every
+SM and NCCL's kernels then wait for SMs (giving NCCL reserved SMs is the next step).
 
 The reference simulates a single expert-parallel rank and computes only its local routes
 (src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:31,136); this is the real exchange.
@@ -130,14 +130,12 @@ class ExpertParallelMoE:
     def forward(self, x: torch.Tensor, micro_batches: Optional[int] = None):
         """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32).
 
-        micro_batches: token slices whose exchanges overlap each other's expert GEMMs.  Default: 2 when
-        P > 1 and a local expert still sees >= 512 tokens per slice on average (T_r k P / E >= 1024), else 1
-        (below that, slicing would stream every expert's weights once per slice).  Every rank must use the
-        same count (each slice is one round of all-to-alls)."""
+        micro_batches: token slices whose exchanges overlap each other's expert GEMMs (default 1: measured
+        on 8 B200s, two slices were not faster, because the persistent expert GEMMs, which hold every SM,
+        and NCCL's all-to-all kernels then compete for SMs).  Every rank must use the same count (each
+        slice is one round of all-to-alls)."""
         T, H = x.shape
-        if micro_batches is None:
-            micro_batches = 2 if self.P > 1 and T * self.k * self.P >= 1024 * self.E else 1
-        nb = micro_batches
+        nb = 1 if micro_batches is None else micro_batches
         nb = max(1, min(int(nb), max(T, 1)))
         bounds = [T * i // nb for i in range(nb + 1)]
         sts = [self.dispatch(x[bounds[i]:bounds[i + 1]]) for i in range(nb)]
@@ -155,7 +153,6 @@ class ExpertParallelMoE:
             recv = torch.empty((int(sum(recv_rows)), H), dtype=st["send"].dtype, device=x.device)
             works.append(self._exchange(recv, st["send"], recv_rows, send_rows))
             recvs.append((recv, send_rows, recv_rows))
-        shared = [self.shared_rows(st["x"]) for st in sts]   # the shared expert runs while rows are in flight
         rets = []
         for i in range(nb):
             if works[i] is not None:
@@ -169,7 +166,7 @@ class ExpertParallelMoE:
             ret, work, _back = rets[i]                       # _back stays referenced until its send is done
             if work is not None:
                 work.wait()
-            outs.append(self.finish(st, ret, shared[i]))
+            outs.append(self.finish(st, ret))
         if nb == 1:
             return outs[0]
         return tuple(torch.cat([o[j] for o in outs]) for j in range(3))
