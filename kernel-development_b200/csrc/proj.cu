@@ -211,6 +211,7 @@ struct ProjSwapSched {
   struct Params {
     int M, N, f_tiles, t_tiles, splits, nkb_total, nkb_per, nb;   // nb: token rows per tile
     int b_kwrap;                                                  // 0, or the token k chunks (wrap)
+    int a_tile_rows;                                              // weight rows per tile: 128 or 256 (2 parts)
   };
   Params p;
   __device__ explicit ProjSwapSched(const Params& pp) : p(pp) {}
@@ -222,14 +223,14 @@ struct ProjSwapSched {
     const int sp = rest % p.splits;
     const int f = rest / p.splits;
     SwapTile ti;
-    ti.a_row = f * 128;
+    ti.a_row = f * p.a_tile_rows;
     ti.a_part_stride = 128;
     ti.b_row = tt * p.nb;
     ti.row0 = ti.b_row;
     ti.n_valid = min(p.nb, p.M - ti.row0);
     ti.kb0 = sp * p.nkb_per;
     ti.nkb = min(p.nkb_per, p.nkb_total - ti.kb0);
-    ti.f0 = f * 128;
+    ti.f0 = f * p.a_tile_rows;
     ti.split = sp;
     ti.b_kwrap = p.b_kwrap;
     return ti;
@@ -243,10 +244,15 @@ struct ProjSwapEpi {
     float* partial;     // [splits, M, N] fp32, or null
     long long ldy;
     int M, N;
+    int parts;          // 128-row weight parts per tile (accumulators NB columns apart)
   };
   template <int NB>
   __device__ static void run(const Params& p, const SwapTile& ti, int r, uint32_t taddr) {
-    const int feat = ti.f0 + r;
+#pragma unroll 1
+    for (int a = 0; a < p.parts; ++a) run_part<NB>(p, ti, ti.f0 + a * 128 + r, taddr + a * NB);
+  }
+  template <int NB>
+  __device__ static void run_part(const Params& p, const SwapTile& ti, int feat, uint32_t taddr) {
     const bool ok = feat < p.N;
 #pragma unroll 1
     for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
@@ -289,28 +295,82 @@ __global__ void __launch_bounds__(256)
   else y[m * ldy + n] = __float2bfloat16_rn(acc);
 }
 
-// K split of the small-M path: minimises (W bytes + partial traffic) / wave efficiency.
-int proj_small_m_splits(long long M, long long N, long long K, long long sms) {
-  const long long base = ((N + 127) / 128) * ((M + 127) / 128);
+// The same with four consecutive columns per thread (N % 4 == 0, ldy % 4 == 0, y 8-byte aligned): 16-byte
+// partial loads, the slices' loads issued together, summed in slice order as above.
+__global__ void __launch_bounds__(256)
+    proj_reduce4_kernel(const float4* __restrict__ partial, __nv_bfloat16* __restrict__ y, float* __restrict__ y32,
+                        long long ldy, int M, int N, int splits) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long n4 = N / 4, total4 = static_cast<long long>(M) * n4;
+  if (idx >= total4) return;
+  const long long m = idx / n4, n = (idx % n4) * 4;
+  float4 acc = partial[idx];
+  for (int s0 = 1; s0 < splits; s0 += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (s0 + j < splits) v[j] = partial[static_cast<long long>(s0 + j) * total4 + idx];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (s0 + j < splits) {
+        acc.x += v[j].x;
+        acc.y += v[j].y;
+        acc.z += v[j].z;
+        acc.w += v[j].w;
+      }
+    }
+  }
+  if (y32) {
+    y32[m * ldy + n] = acc.x;
+    y32[m * ldy + n + 1] = acc.y;
+    y32[m * ldy + n + 2] = acc.z;
+    y32[m * ldy + n + 3] = acc.w;
+  } else {
+    uint2 packed;
+    packed.x = pack_bf16x2(acc.x, acc.y);
+    packed.y = pack_bf16x2(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(y + m * ldy + n) = packed;
+  }
+}
+
+// Small-M plan: weight rows per tile (128, or 256 as two parts when M > 32) and the K split.  Cost model
+// (bytes staged or moved, over the wave efficiency of the persistent grid): the weights once, the token
+// rows once per weight tile (so 256-row tiles halve that term), and the fp32 partials written and read
+// back when K is split.
+struct SmallMPlan {
+  int parts, splits;
+};
+
+static SmallMPlan small_m_plan(long long M, long long N, long long K, long long sms) {
   const long long nkb = (K + 63) / 64;
-  int best = 1;
-  double best_cost = 1e30;
+  const long long m_pad = M <= 32 ? 32 : 128;
   const long long max_s = M <= 32 ? 32 : 16;
-  for (long long s = 1; s <= max_s && s <= nkb; ++s) {
-    const long long per = (nkb + s - 1) / s;
-    const long long used = (nkb + per - 1) / per;   // slices actually non-empty
-    if (used != s) continue;
-    const long long tiles = base * s;
-    const long long rounds = (tiles + sms - 1) / sms;
-    const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * sms);
-    const double traffic = 1.0 + (s > 1 ? 4.0 * s * static_cast<double>(M) / static_cast<double>(K) : 0.0);
-    const double cost = traffic / wave;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = static_cast<int>(s);
+  SmallMPlan best{1, 1};
+  double best_cost = 1e30;
+  for (int parts = 1; parts <= (M > 32 ? 2 : 1); ++parts) {
+    const long long rows = 128 * parts;
+    const long long f_tiles = (N + rows - 1) / rows;
+    const double w_bytes = 2.0 * N * K, x_bytes = 2.0 * f_tiles * m_pad * K;
+    for (long long s = 1; s <= max_s && s <= nkb; ++s) {
+      const long long per = (nkb + s - 1) / s;
+      const long long used = (nkb + per - 1) / per;   // slices actually non-empty
+      if (used != s) continue;
+      const long long tiles = f_tiles * ((M + 127) / 128) * s;
+      const long long rounds = (tiles + sms - 1) / sms;
+      const double wave = static_cast<double>(tiles) / static_cast<double>(rounds * sms);
+      const double partial = s > 1 ? 2.0 * 4.0 * s * M * N : 0.0;
+      const double cost = (w_bytes + x_bytes + partial) / wave;
+      if (cost < best_cost * (1.0 - 1e-9)) {
+        best_cost = cost;
+        best = SmallMPlan{parts, static_cast<int>(s)};
+      }
     }
   }
   return best;
+}
+
+int proj_small_m_splits(long long M, long long N, long long K, long long sms) {
+  return small_m_plan(M, N, K, sms).splits;
 }
 
 size_t proj_workspace_bytes(long long M, long long N, long long K) {
@@ -321,11 +381,10 @@ size_t proj_workspace_bytes(long long M, long long N, long long K) {
 
 // y32 (fp32 output) replaces y when not null.  kx: the token operand's width when the weights are
 // [W_hi | W_mid] (K = 2 kx, token k chunks wrap at kx); 0 otherwise.
-template <int NB, int STAGES, int KC>
+template <int MA, int NB, int STAGES, int KC>
 static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int N, int K, long long ldy,
                                void* workspace, size_t ws_bytes, cudaStream_t stream, float* y32 = nullptr,
                                int kx = 0) {
-  constexpr int MA = 1;
   using L = SwapLayout<MA, NB, STAGES, KC>;
   auto kern = gemm_swap_kernel<ProjSwapSched, ProjSwapEpi, MA, NB, STAGES, KC>;
   static bool attr_done[64] = {false};
@@ -349,7 +408,8 @@ static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int
   sp.b_kwrap = kx > 0 ? kx / kBK : 0;
   sp.M = M;
   sp.N = N;
-  sp.f_tiles = (N + 127) / 128;
+  sp.a_tile_rows = 128 * MA;
+  sp.f_tiles = (N + sp.a_tile_rows - 1) / sp.a_tile_rows;
   sp.t_tiles = (M + NB - 1) / NB;
   sp.nb = NB;
   sp.splits = splits;
@@ -362,14 +422,20 @@ static int launch_proj_small_m(const void* x, const void* w, void* y, int M, int
   ep.ldy = ldy;
   ep.M = M;
   ep.N = N;
+  ep.parts = MA;
   const int tiles = sp.f_tiles * sp.t_tiles * splits;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, kGemmThreads, L::kSmemBytes, stream>>>(ta, tb, sp, ep);
   rc = cuda_status(cudaGetLastError());
   if (rc || splits == 1) return rc;
   const long long total = static_cast<long long>(M) * N;
-  proj_reduce_kernel<<<static_cast<unsigned int>((total + 255) / 256), 256, 0, stream>>>(
-      static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(y), y32, ldy, M, N, splits);
+  const bool vec4 = N % 4 == 0 && ldy % 4 == 0 && (y32 ? aligned16(y32) : (reinterpret_cast<uintptr_t>(y) & 7) == 0);
+  if (vec4)
+    proj_reduce4_kernel<<<static_cast<unsigned int>((total / 4 + 255) / 256), 256, 0, stream>>>(
+        static_cast<const float4*>(workspace), static_cast<__nv_bfloat16*>(y), y32, ldy, M, N, splits);
+  else
+    proj_reduce_kernel<<<static_cast<unsigned int>((total + 255) / 256), 256, 0, stream>>>(
+        static_cast<const float*>(workspace), static_cast<__nv_bfloat16*>(y), y32, ldy, M, N, splits);
   return cuda_status(cudaGetLastError());
 }
 
@@ -427,8 +493,12 @@ int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, l
     // room for 11 pipeline stages (more weight bytes in flight per SM)
     // two 64-wide k chunks per stage: 256 contiguous bytes of every weight row per request (7% faster
     // than one chunk at 16 x 7168 x 7168)
-    if (M <= 32) return launch_proj_small_m<32, 5, 2>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
-    if (M <= 128) return launch_proj_small_m<128, 6, 1>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    if (M <= 32) return launch_proj_small_m<1, 32, 5, 2>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    if (M <= 128) {
+      if (small_m_plan(M, N, K, num_sms()).parts == 2)
+        return launch_proj_small_m<2, 128, 4, 1>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+      return launch_proj_small_m<1, 128, 6, 1>(x, w, y, (int)M, (int)N, (int)K, ldy, workspace, ws_bytes, stream);
+    }
     pick_tile(M, N, num_sms(), &bn, &cta_pair);
   }
   if (cta_pair > 0) {
@@ -484,9 +554,11 @@ int proj_f32w(const void* x, const void* w_split, float* y, long long M, long lo
   if (!aligned16(x) || !aligned16(w_split)) return KDB_ERR_INVALID_ARG;
   const int m = static_cast<int>(M), n = static_cast<int>(N), k2 = static_cast<int>(2 * K);
   if (M <= 32)
-    return launch_proj_small_m<32, 5, 2>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
+    return launch_proj_small_m<1, 32, 5, 2>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
   if (M <= 128)
-    return launch_proj_small_m<128, 6, 1>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
+    return small_m_plan(M, N, 2 * K, num_sms()).parts == 2
+               ? launch_proj_small_m<2, 128, 4, 1>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K)
+               : launch_proj_small_m<1, 128, 6, 1>(x, w_split, nullptr, m, n, k2, n, workspace, ws_bytes, stream, y, (int)K);
   return router_approx(x, w_split, y, m, static_cast<int>(K), n, stream);
 }
 
