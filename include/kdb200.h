@@ -36,6 +36,14 @@ extern "C" {
 /* ABI version (KDB200_ABI_VERSION). */
 int kdb_abi_version(void);
 
+/*
+ * Process-wide cap on the SMs the persistent kernels launched after this call size their grids for
+ * (0 = all SMs; values below 2 act as 2).  Returns the previous cap.  Use: leave SMs free for a
+ * collective (NCCL all-to-all) that runs alongside the expert GEMMs; results do not depend on it.
+ */
+int kdb_set_sm_budget(int32_t sms);
+int kdb_sm_budget(void);
+
 /* Static string for a KDB_* status code. */
 const char* kdb_strerror(int code);
 

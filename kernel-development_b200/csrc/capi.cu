@@ -16,6 +16,10 @@ extern "C" {
 
 int kdb_abi_version(void) { return KDB200_ABI_VERSION; }
 
+int kdb_set_sm_budget(int32_t sms) { return kdb::set_sm_budget(sms < 0 ? 0 : sms); }
+
+int kdb_sm_budget(void) { return kdb::sm_budget(); }
+
 const char* kdb_strerror(int code) {
   switch (code) {
     case KDB_OK: return "ok";

@@ -1,6 +1,7 @@
 // host_util.cu — see host_util.h.
 #include "host_util.h"
 
+#include <atomic>
 #include <mutex>
 
 namespace kdb {
@@ -16,16 +17,25 @@ int cuda_status(cudaError_t e) {
   return KDB_ERR_CUDA;
 }
 
+static std::atomic<int> g_sm_budget{0};
+
+int set_sm_budget(int sms) { return g_sm_budget.exchange(sms > 0 ? sms : 0); }
+int sm_budget() { return g_sm_budget.load(); }
+
 int num_sms() {
   static int cache[64] = {0};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cache[dev] = n;
+  int n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+    if (cache[dev] == 0) {
+      int v = 0;
+      if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+      cache[dev] = v;
+    }
+    n = cache[dev];
   }
-  return cache[dev];
+  const int b = g_sm_budget.load(std::memory_order_relaxed);
+  return (b > 0 && b < n) ? (b < 2 ? 2 : b) : n;
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

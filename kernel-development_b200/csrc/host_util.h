@@ -15,7 +15,11 @@ void set_cuda_error(cudaError_t e);
 int cuda_status(cudaError_t e);   // KDB_OK or KDB_ERR_CUDA (and records e)
 
 // Number of SMs of the current device (cached per device).
+// SMs the persistent kernels size their grids for: the device's count, or the process-wide budget when
+// one is set (set_sm_budget; 0 = no budget), e.g. to leave SMs to a collective running alongside.
 int num_sms();
+int set_sm_budget(int sms);   // returns the previous budget
+int sm_budget();
 
 // Encodes a 2-D bf16 tensor map over a row-major [rows, inner] matrix with row stride `ld`
 // elements, box = [box_rows, box_inner] with the 128-byte swizzle.  Returns KDB_OK or an error.

@@ -13,16 +13,18 @@ shared expert are replicated.  One layer call on rank r:
   7. owner: regroup back to source-major, all-to-all the rows home
   8. combine: y[t] = sum_j w[t, j] * row(t, j) (+ shared expert on local tokens)   kdb_moe_combine
 
-The all-to-alls are issued asynchronously (NCCL runs them on its own stream) and a call may be split into
-micro-batches, so that while one slice's rows are in flight the tensor cores work on another's.  That
-overlap is off by default: on 8 B200s it was not faster, since the persistent expert GEMMs occupy every
-SM and NCCL's kernels then wait for SMs (giving NCCL reserved SMs is the next step).
+The all-to-alls are issued asynchronously (NCCL runs them on its own stream).  The shared expert runs
+while the dispatched rows are in flight, and with P >= 4 (enough tokens per local expert) the call is split
+into two micro-batches, so that while one slice's rows cross NVLink the tensor cores work on the other's.
+The kernels that overlap an exchange are launched on all but `comm_sms` SMs (kdb_set_sm_budget): the
+persistent GEMMs would otherwise hold every SM and NCCL's kernels would wait for them.
 
 The reference simulates a single expert-parallel rank and computes only its local routes
 (src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:31,136); this is the real exchange.
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Optional
 
 import torch
@@ -127,16 +129,19 @@ class ExpertParallelMoE:
             return None
         return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=True)
 
-    def forward(self, x: torch.Tensor, micro_batches: Optional[int] = None):
+    def forward(self, x: torch.Tensor, micro_batches: Optional[int] = None, comm_sms: int = 16):
         """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32).
 
-        micro_batches: token slices whose exchanges overlap each other's expert GEMMs (default 1: measured
-        on 8 B200s, two slices were not faster, because the persistent expert GEMMs, which hold every SM,
-        and NCCL's all-to-all kernels then compete for SMs).  Every rank must use the same count (each
-        slice is one round of all-to-alls)."""
+        micro_batches: token slices whose exchanges overlap each other's expert GEMMs.  Default: 2 when
+        P >= 4 and a local expert still sees >= 512 tokens per slice on average (T_r k P / E >= 1024),
+        else 1 (with fewer tokens per expert, slicing would stream every expert's weights once per slice).
+        Every rank must use the same count (each slice is one round of all-to-alls).
+        comm_sms: SMs the kernels that run while an exchange is in flight leave to NCCL (the persistent
+        GEMMs otherwise hold every SM and NCCL's kernels wait for them); 0 = no reservation."""
         T, H = x.shape
-        nb = 1 if micro_batches is None else micro_batches
-        nb = max(1, min(int(nb), max(T, 1)))
+        if micro_batches is None:
+            micro_batches = 2 if self.P >= 4 and T * self.k * self.P >= 1024 * self.E else 1
+        nb = max(1, min(int(micro_batches), max(T, 1)))
         bounds = [T * i // nb for i in range(nb + 1)]
         sts = [self.dispatch(x[bounds[i]:bounds[i + 1]]) for i in range(nb)]
         # the counts of every micro-batch in one exchange, then the one host read-back of the split sizes
@@ -153,12 +158,18 @@ class ExpertParallelMoE:
             recv = torch.empty((int(sum(recv_rows)), H), dtype=st["send"].dtype, device=x.device)
             works.append(self._exchange(recv, st["send"], recv_rows, send_rows))
             recvs.append((recv, send_rows, recv_rows))
+        leave = comm_sms if self.P > 1 else 0
+        with self._sm_budget(leave):
+            # the shared expert needs no exchange: it runs while the first rows are in flight
+            shared = [self.shared_rows(st["x"]) for st in sts]
         rets = []
         for i in range(nb):
             if works[i] is not None:
                 works[i].wait()                      # the compute stream waits for this slice's rows only
             recv, send_rows, recv_rows = recvs[i]
-            back = self.owner_compute(recv, recv_counts[i])
+            # with several slices another slice's exchange is in flight during this compute
+            with self._sm_budget(leave if nb > 1 else 0):
+                back = self.owner_compute(recv, recv_counts[i])
             ret = torch.empty(((bounds[i + 1] - bounds[i]) * self.k, H), dtype=back.dtype, device=x.device)
             rets.append((ret, self._exchange(ret, back, send_rows, recv_rows), back))
         outs = []
@@ -166,10 +177,24 @@ class ExpertParallelMoE:
             ret, work, _back = rets[i]                       # _back stays referenced until its send is done
             if work is not None:
                 work.wait()
-            outs.append(self.finish(st, ret))
+            outs.append(self.finish(st, ret, shared[i]))
         if nb == 1:
             return outs[0]
         return tuple(torch.cat([o[j] for o in outs]) for j in range(3))
+
+    @contextlib.contextmanager
+    def _sm_budget(self, leave: int):
+        """Caps the persistent kernels' grids at (SMs - leave) for the launches inside the block."""
+        if leave <= 0 or self.ops is not M:
+            yield
+            return
+        lib = M._lib.lib()
+        total = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        prev = lib.kdb_set_sm_budget(max(2, total - int(leave)))
+        try:
+            yield
+        finally:
+            lib.kdb_set_sm_budget(prev)
 
     def _count_exchange(self, recv_counts: torch.Tensor, send_counts: torch.Tensor) -> None:
         """recv_counts[b, s] = what rank s sent here in micro-batch b (send_counts[b, p] went to rank p)."""

@@ -280,3 +280,21 @@ def test_prefill_fast_and_exact_paths_agree():
     w1, i1 = M.route_fast(x, router, None, split, norms, cfg.k)
     torch.cuda.synchronize()
     assert torch.equal(i1, i0) and torch.equal(w1, w0)
+
+
+def test_sm_budget_leaves_results_unchanged():
+    """kdb_set_sm_budget only resizes the persistent grids: the layer's output is bitwise the same."""
+    from kdb200 import _lib as L
+    cfg = W.MoeConfig("budget", 700, 512, 16, 256, 4, shared=1, shared_i=256)
+    x = W.moe_input(cfg.t, cfg.h, 9, device="cuda")
+    state = M.prepare(W.moe_weights(cfg, 9, device="cuda"), cfg.k)
+    y0, w0, i0 = M.forward(x, state)
+    prev = L.lib().kdb_set_sm_budget(37)
+    try:
+        assert L.lib().kdb_sm_budget() == 37
+        y1, w1, i1 = M.forward(x, state)
+    finally:
+        L.lib().kdb_set_sm_budget(prev)
+    torch.cuda.synchronize()
+    assert L.lib().kdb_sm_budget() == prev
+    assert torch.equal(y0, y1) and torch.equal(w0, w1) and torch.equal(i0, i1)
