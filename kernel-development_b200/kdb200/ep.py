@@ -13,11 +13,11 @@ shared expert are replicated.  One layer call on rank r:
   7. owner: regroup back to source-major, all-to-all the rows home
   8. combine: y[t] = sum_j w[t, j] * row(t, j) (+ shared expert on local tokens)   kdb_moe_combine
 
-The all-to-alls are issued asynchronously (NCCL runs them on its own stream).  The shared expert runs
-while the dispatched rows are in flight, and with P >= 4 (enough tokens per local expert) the call is split
-into two micro-batches, so that while one slice's rows cross NVLink the tensor cores work on the other's.
-The kernels that overlap an exchange are launched on all but `comm_sms` SMs (kdb_set_sm_budget): the
-persistent GEMMs would otherwise hold every SM and NCCL's kernels would wait for them.
+The all-to-alls are issued asynchronously (NCCL runs them on its own stream) and the shared expert runs
+while the dispatched rows are in flight, on all but `comm_sms` SMs (kdb_set_sm_budget): the persistent
+GEMMs would otherwise hold every SM and NCCL's kernels would wait for them.  A call can also be split into
+micro-batches so that one slice's exchange overlaps another slice's expert GEMMs; measured on 8 B200s that
+was not faster, so it is off by default.
 
 The reference simulates a single expert-parallel rank and computes only its local routes
 (src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:31,136); this is the real exchange.
@@ -132,16 +132,14 @@ class ExpertParallelMoE:
     def forward(self, x: torch.Tensor, micro_batches: Optional[int] = None, comm_sms: int = 16):
         """x bf16 [T_r, H] (this rank's tokens) -> (y bf16 [T_r, H], topk_w fp32 [T_r, k], topk_ids int32).
 
-        micro_batches: token slices whose exchanges overlap each other's expert GEMMs.  Default: 2 when
-        P >= 4 and a local expert still sees >= 512 tokens per slice on average (T_r k P / E >= 1024),
-        else 1 (with fewer tokens per expert, slicing would stream every expert's weights once per slice).
-        Every rank must use the same count (each slice is one round of all-to-alls).
+        micro_batches: token slices whose exchanges overlap each other's expert GEMMs (default 1).  Measured
+        on 8 B200s (prefill layer, ms per call): one slice 9.70, one slice with the shared expert on 132 SMs
+        beside the dispatch 9.58, two slices 10.39 / 10.45 / 9.72 with 0 / 16 / 32 SMs left to NCCL, so the
+        default is one slice.  Every rank must use the same count (each slice is one round of all-to-alls).
         comm_sms: SMs the kernels that run while an exchange is in flight leave to NCCL (the persistent
         GEMMs otherwise hold every SM and NCCL's kernels wait for them); 0 = no reservation."""
         T, H = x.shape
-        if micro_batches is None:
-            micro_batches = 2 if self.P >= 4 and T * self.k * self.P >= 1024 * self.E else 1
-        nb = max(1, min(int(micro_batches), max(T, 1)))
+        nb = max(1, min(int(1 if micro_batches is None else micro_batches), max(T, 1)))
         bounds = [T * i // nb for i in range(nb + 1)]
         sts = [self.dispatch(x[bounds[i]:bounds[i + 1]]) for i in range(nb)]
         # the counts of every micro-batch in one exchange, then the one host read-back of the split sizes
