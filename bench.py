@@ -226,6 +226,12 @@ def _proj_cfg(name):
     return W.PROJ_CONFIGS[name]
 
 
+def _lib_ws(cfg) -> int:
+    """Workspace bytes of the small-M K split for this shape (0: one launch, no split)."""
+    from kdb200 import _lib
+    return int(_lib.lib().kdb_proj_workspace_bytes(cfg.m, cfg.n, cfg.k))
+
+
 def bench_proj(args, dist: Dist) -> dict | None:
     from kdb200 import proj_into
     from kdb200 import workloads as W
@@ -284,8 +290,13 @@ def bench_proj(args, dist: Dist) -> dict | None:
     roof["peak_source"] = f"{peaks['source']} (burst)"
     from kdb200.proj import tile_shape
     bn, pair = tile_shape(cfg.m, cfg.n)
-    roof["kernel"] = (f"gemm_tn_pair_kernel<ProjSched<256,{bn}>> (256 x {bn} tiles on 2-CTA clusters)" if pair else
-                      f"gemm_tn_kernel<ProjSched<128,{bn}>> (128 x {bn} tiles)") + ", one launch per step"
+    if cfg.m <= 128:
+        split = int(_lib_ws(cfg)) > 0
+        roof["kernel"] = ("gemm_swap_kernel<ProjSwapSched> (weights as the M operand"
+                          + (", K split + proj_reduce4_kernel: two launches per step)" if split else "), one launch per step"))
+    else:
+        roof["kernel"] = (f"gemm_tn_pair_kernel<ProjSched<256,{bn}>> (256 x {bn} tiles on 2-CTA clusters)" if pair else
+                          f"gemm_tn_kernel<ProjSched<128,{bn}>> (128 x {bn} tiles)") + ", one launch per step"
     line = {
         "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in roofline.frac)",
         "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
@@ -300,7 +311,7 @@ def bench_proj(args, dist: Dist) -> dict | None:
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "path": "submissions/b200_bf16_proj.py kernel_fn (kdev adapter API) -> kdb_proj_bf16",
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if cfg.m <= 128 and _lib_ws(cfg) > 0 else 1),
         "roofline": roof,
         "clocks": sampler.summary() if sampler else None,
         "timed_region_ms": round(region_ms, 2),
