@@ -262,6 +262,24 @@ int kdb_moe_forward(const void* x, const float* router_w, const float* router_bi
                     float* topk_w, int32_t* topk_ids, int64_t t, int64_t h, int64_t e, int64_t i, int64_t k,
                     int64_t shared, int64_t shared_i, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * NVFP4 w4a16 MoE layer of one expert-parallel rank (the reference's muse_moe_w4a16 problem,
+ * src/kdev/adapters/okc_problems/muse_moe_w4a16.toml; engines okc-challenge/engines/sc_h.cu:189-467).
+ * x bf16 [t, h]; topk_ids int32 / topk_w fp32 [t, k] over e_total experts, of which ids 0..local-1 live
+ * here (routes to other ids are skipped); y bf16 [t, h] = sum over local routes j of
+ * topk_w * rms_norm(y_j), y_j = (bf16(silu(x.W1^T gs13) * (x.W3^T gs13)) . W2^T) gs2, rms_norm(v) =
+ * v * rsqrt(mean(v^2) + 1e-8).  Weights NVFP4 (E2M1 codes, E4M3 scale per 16 elements, fp32 global scale
+ * per expert tensor), tiled: w13_codes [local][2i/128][h/64][128 rows][32 B], w13_scales
+ * [local][2i/128][h/64][128][4 B], rows 0..i-1 gate and i..2i-1 up; w2_codes [local][h/128][i/64][128][32 B],
+ * w2_scales [local][h/128][i/64][128][4 B]; gscales fp32 [local].  h % 256 == 0, h <= 8192, i % 128 == 0.
+ * workspace >= kdb_moe_w4a16_workspace_bytes, 256-byte aligned.
+ */
+size_t kdb_moe_w4a16_workspace_bytes(int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k);
+int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_codes,
+                          const void* w13_scales, const float* w13_gscale, const void* w2_codes, const void* w2_scales,
+                          const float* w2_gscale, void* y, int64_t t, int64_t h, int64_t i, int64_t local,
+                          int64_t e_total, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

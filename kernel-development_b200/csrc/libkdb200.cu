@@ -8,4 +8,5 @@
 #include "moe.cu"
 #include "moe_ep.cu"
 #include "moe_noalloc.cu"
+#include "moe_w4a16.cu"
 #include "capi.cu"

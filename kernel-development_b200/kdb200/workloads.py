@@ -199,3 +199,109 @@ def moe_bytes(cfg: MoeConfig, distinct_experts: int) -> float:
     w = distinct_experts * 3.0 * cfg.h * cfg.i * 2
     ws = cfg.shared * 3.0 * cfg.h * cfg.shared_i * 2
     return w + ws + 4.0 * cfg.h * cfg.e + 2.0 * (2.0 * cfg.t * cfg.h) + 8.0 * cfg.t * cfg.k
+
+
+# ------------------------------------------------------------------------------------ NVFP4 w4a16 MoE
+# NVFP4 weights: E2M1 codes (two per byte, element 2j in the low nibble), one E4M3 scale per 16 consecutive
+# elements of a row, one fp32 global scale per expert tensor; value = e2m1(code) * e4m3(scale) * global.
+# e2m1(code) * e4m3(scale) has at most 6 significant bits, so it is exact in bf16: a kernel may dequantise
+# to bf16 without rounding and apply the global scale to the fp32 accumulator.
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+@dataclass(frozen=True)
+class W4A16Config:
+    """One expert-parallel rank of an NVFP4 MoE layer: `local` experts of `e_total` live here (ids
+    0..local-1), every token carries k routes over all e_total experts and only the local ones are
+    computed (the reference's ep8 slice, src/kdev/adapters/okc_problems/muse_moe_w4a16.toml:136)."""
+    name: str
+    t: int
+    h: int
+    i: int
+    local: int
+    e_total: int
+    k: int
+    skew: bool = False
+
+
+W4A16_CONFIGS = {
+    "w4a16_bs1": W4A16Config("w4a16_bs1", 1, 4096, 4096, 32, 256, 8),
+    "w4a16_bs16": W4A16Config("w4a16_bs16", 16, 4096, 4096, 32, 256, 8),
+    "w4a16_bs256": W4A16Config("w4a16_bs256", 256, 4096, 4096, 32, 256, 8),
+    "w4a16_bs32_skewed": W4A16Config("w4a16_bs32_skewed", 32, 4096, 4096, 32, 256, 8, skew=True),
+}
+
+
+def e2m1_encode(v: torch.Tensor) -> torch.Tensor:
+    """Nearest E2M1 code (4 bits: sign, 2 exponent, 1 mantissa; ties to the even mantissa) of fp32 v,
+    saturating at +-6.  Returns uint8 codes 0..15."""
+    mag = v.abs().clamp(max=6.0)
+    grid = torch.tensor(E2M1_VALUES, dtype=torch.float32)
+    d = (mag.unsqueeze(-1) - grid).abs()
+    best = d.min(dim=-1, keepdim=True).values
+    # ties: prefer the even code (mantissa 0), i.e. the lowest index among equals with even index
+    tie_even = (d == best) & (torch.arange(8) % 2 == 0)
+    idx = torch.where(tie_even.any(-1), tie_even.float().argmax(-1), (d == best).float().argmax(-1))
+    sign = ((v < 0) & (idx > 0)).to(torch.uint8)
+    return (sign << 3) | idx.to(torch.uint8)
+
+
+def e2m1_decode(codes: torch.Tensor) -> torch.Tensor:
+    """fp32 values of uint8 E2M1 codes 0..15."""
+    grid = torch.tensor(E2M1_VALUES + tuple(-x for x in E2M1_VALUES), dtype=torch.float32)
+    return grid[codes.long()]
+
+
+def nvfp4_quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """fp32 w [rows, cols] (cols % 16 == 0) -> (codes uint8 [rows, cols/2], scales float8_e4m3fn
+    [rows, cols/16], global fp32 scalar): per-16 amax / 6 scaled into E4M3's range by the global scale."""
+    rows, cols = w.shape
+    blocks = w.reshape(rows, cols // 16, 16)
+    amax = blocks.abs().amax(-1)
+    g = float(amax.max()) / (6.0 * 448.0) if float(amax.max()) > 0 else 1.0
+    scale = (amax / 6.0 / g).to(torch.float8_e4m3fn)
+    s = scale.float().clamp(min=2.0 ** -9)
+    codes = e2m1_encode(blocks / (s.unsqueeze(-1) * g)).reshape(rows, cols)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
+    return packed.contiguous(), scale.contiguous(), torch.tensor(g, dtype=torch.float32)
+
+
+def nvfp4_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """e2m1(code) * e4m3(scale) as fp32 [rows, cols] (exactly representable in bf16); the global scale
+    is not applied."""
+    rows = codes.shape[0]
+    lo = e2m1_decode(codes & 0xF)
+    hi = e2m1_decode(codes >> 4)
+    vals = torch.stack([lo, hi], dim=-1).reshape(rows, -1)
+    return (vals.reshape(rows, -1, 16) * scales.float().unsqueeze(-1)).reshape(rows, -1)
+
+
+def w4a16_weights(cfg: W4A16Config, seed: int = 0) -> dict:
+    """NVFP4 weights of the local experts (CPU): w13 [L, 2I, H/2] uint8 (rows 0..I-1 gate, I..2I-1 up),
+    w13_scale [L, 2I, H/16] e4m3, w13_gscale [L] fp32, w2 [L, H, I/2], w2_scale [L, H, I/16], w2_gscale [L]."""
+    L, H, I = cfg.local, cfg.h, cfg.i
+    out = {k: [] for k in ("w13", "w13_scale", "w13_gscale", "w2", "w2_scale", "w2_gscale")}
+    for e in range(L):
+        w13 = _randn((2 * I, H), (seed * 1000 + _TID_GU) * 4096 + e, "cpu", 1.0 / math.sqrt(H), torch.float32)
+        w2 = _randn((H, I), (seed * 1000 + _TID_DOWN) * 4096 + e, "cpu", 1.0 / math.sqrt(I), torch.float32)
+        for name, w in (("w13", w13), ("w2", w2)):
+            c, s, g = nvfp4_quantize(w)
+            out[name].append(c)
+            out[name + "_scale"].append(s)
+            out[name + "_gscale"].append(g)
+    return {k: torch.stack(v) for k, v in out.items()}
+
+
+def w4a16_routing(cfg: W4A16Config, seed: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """(topk_ids int32 [T, k] over e_total experts, topk_w fp32 [T, k] renormalised): distinct experts per
+    token drawn with extra weight on the local ones (this rank is the busiest, as in the reference's
+    rank='busiest' routing); skew concentrates the local routes on a few experts."""
+    g = torch.Generator().manual_seed(seed * 1000 + _TID_ROUTER)
+    pref = torch.ones(cfg.e_total)
+    pref[: cfg.local] = 4.0
+    if cfg.skew:
+        pref[: cfg.local] = 4.0 * torch.pow(torch.arange(1, cfg.local + 1, dtype=torch.float32), -1.2) * 4
+    ids = torch.stack([torch.multinomial(pref, cfg.k, replacement=False, generator=g) for _ in range(cfg.t)])
+    logits = torch.randn((cfg.t, cfg.k), generator=g)
+    w = torch.softmax(logits, dim=-1)
+    return ids.to(torch.int32), w.to(torch.float32)

@@ -204,3 +204,46 @@ def test_golden_layer_reproduces():
         f = np.load(GOLDEN / f"{case['name']}.npz")
         x, w = mg.proj_inputs(case)
         assert np.allclose(op.proj_ref(x, w).numpy(), f["y32"], rtol=1e-5, atol=1e-5)
+
+
+# ------------------------------------------------------------------------------ NVFP4 (w4a16) oracle
+def test_nvfp4_codes_and_dequant_are_exact():
+    from kdb200 import workloads as W
+    vals = torch.tensor(W.E2M1_VALUES + tuple(-v for v in W.E2M1_VALUES[1:]))
+    assert torch.equal(W.e2m1_decode(W.e2m1_encode(vals)), vals)          # every representable value round-trips
+    w = torch.randn(256, 512) / 20
+    q, s, g = W.nvfp4_quantize(w)
+    dq = W.nvfp4_dequantize(q, s)
+    assert torch.equal(dq, dq.to(torch.bfloat16).float())                  # e2m1 * e4m3 is exact in bf16
+    assert torch.equal(dq, dq.to(torch.float16).float())                   # and in f16 (the kernel's operand)
+    rel = float(((dq * g) - w).norm() / w.norm())
+    assert rel < 0.12                                                      # 4-bit quantisation error
+
+
+def test_w4a16_oracle_skips_remote_routes_and_normalises():
+    from kdb200 import workloads as W
+    from oracle import moe_w4a16 as ow
+    cfg = W.W4A16Config("t", 6, 128, 128, 2, 16, 3)
+    wts = W.w4a16_weights(cfg, 4)
+    x = W.moe_input(cfg.t, cfg.h, 4)
+    ids = torch.tensor([[0, 5, 9], [1, 0, 7], [8, 9, 10], [1, 2, 3], [0, 1, 15], [4, 4, 4]], dtype=torch.int32)
+    tw = torch.full((6, 3), 1.0 / 3)
+    out = ow.w4a16_ref(x, ids, tw, wts, cfg.local)
+    assert float(out[2].abs().max()) == 0.0 and float(out[5].abs().max()) == 0.0   # no local routes
+    # one local route: the output row is tw * y / rms(y), whose RMS is tw (up to the 1e-8 and bf16 of y)
+    rms = float((out[0] ** 2).mean().sqrt())
+    assert abs(rms - 1.0 / 3) < 1e-3
+
+
+def test_w4a16_tiling_is_a_permutation():
+    from kdb200 import workloads as W
+    import importlib
+    W4 = importlib.import_module("kdb200.moe_w4a16")
+    cfg = W.W4A16Config("t", 2, 256, 128, 2, 16, 2)
+    wts = W.w4a16_weights(cfg, 1)
+    c, s = W4._tile(wts["w13"], wts["w13_scale"])
+    L, rows, half = wts["w13"].shape
+    # block (l, rt, kc) row r = original row rt*128 + r, bytes kc*32 .. kc*32+31
+    assert torch.equal(c[1, 1, 2, 5], wts["w13"][1, 128 + 5, 64:96])
+    assert torch.equal(s[0, 1, 3, 7], wts["w13_scale"][0, 128 + 7, 12:16].view(torch.uint8))
+    assert sorted(c.flatten().tolist()) == sorted(wts["w13"].flatten().tolist())
