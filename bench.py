@@ -531,6 +531,70 @@ def cpu_baseline_moe(workload: str, steps: int = 3) -> dict:
 
 
 # ------------------------------------------------------------------------------------------------ main
+def bench_w4a16(args, dist: Dist) -> dict | None:
+    """NVFP4 w4a16 MoE layer of one ep8 rank (1 GPU; the layer is one rank's slice by definition)."""
+    from kdb200 import moe_w4a16 as W4
+    from kdb200 import workloads as W
+    if dist.world > 1:
+        raise SystemExit("w4a16 workloads are one expert-parallel rank's layer: run them with --gpus 1")
+    cfg = W.W4A16_CONFIGS[args.workload]
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    state = W4.prepare(W.w4a16_weights(cfg, 1), dev)
+    ids, tw = W.w4a16_routing(cfg, 1)
+    x = W.moe_input(cfg.t, cfg.h, 1, device=dev)
+    gi, gw = ids.to(dev), tw.to(dev)
+    flush = _flusher(dev)
+    holder = {}
+    sampler = ClockSampler(_physical_index(dist.local))
+
+    def step():
+        holder["y"] = W4.forward(x, gi, gw, state, cfg.e_total)
+
+    run_step = _capture(step).replay
+    per_step, region_ms = timed_steps(run_step, args.steps, args.warmup, flush, dist, sampler)
+    ms = statistics.mean(per_step)
+    hit = sorted({int(e) for e in ids.flatten().tolist() if int(e) < cfg.local})
+    per_expert = 3 * cfg.h * cfg.i * (0.5 + 1.0 / 16)        # E2M1 codes + E4M3 scales
+    nbytes = len(hit) * per_expert + cfg.t * cfg.h * 4 + cfg.t * cfg.k * 8
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((cfg.t, cfg.h), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y_host.copy_(W4.forward(x_dev, gi, gw, state, cfg.e_total), non_blocking=True)
+
+    e2e_steps, _ = timed_steps(e2e_step, max(3, args.steps // 4), 2, flush, dist, None)
+    e2e_ms = statistics.mean(e2e_steps)
+    peaks = _peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "MoE layer tokens/s", "value": round(cfg.t / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights x bf16 activations (f16 operands), fp32 acc",
+        "data": "synthetic (seeded; x~N(0,1) bf16, experts N(0,1/fan_in) quantised to NVFP4, routing with this "
+                "rank the busiest)",
+        "config": {"workload": args.workload, "t": cfg.t, "h": cfg.h, "i": cfg.i, "local_experts": cfg.local,
+                   "e_total": cfg.e_total, "k": cfg.k, "local_experts_hit": len(hit),
+                   "parallelism": "one ep8 rank's slice on 1 GPU",
+                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
+                   "graph": "CUDA graph replay per step"},
+        "e2e": {"value": round(cfg.t / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": cfg.t * cfg.h * 2,
+                "d2h_bytes_per_step": cfg.t * cfg.h * 2, "path": "kdb200.moe_w4a16.forward -> kdb_moe_w4a16_forward",
+                "ms_per_step": round(e2e_ms, 4)},
+        # plan (3), tile prefix, gather, gate_up, down, combine
+        "gpu_launches": 8 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": f"{peaks['source']} (burst)",
+                     "kernel": "whole layer (plan, gather, NVFP4 gate_up, NVFP4 down, RMS-norm combine); "
+                               "bytes = NVFP4 weights of the local experts hit + activations"},
+        "clocks": sampler.summary(),
+        "timed_region_ms": round(region_ms, 3),
+    }
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -556,6 +620,8 @@ def main() -> int:
             line = bench_proj(args, dist)
         elif args.workload.startswith("moe"):
             line = bench_moe(args, dist)
+        elif args.workload.startswith("w4a16"):
+            line = bench_w4a16(args, dist)
         else:
             raise SystemExit(f"unknown workload {args.workload}")
         if line is not None and dist.rank == 0:

@@ -7,9 +7,13 @@
 //   converter (warps 6-9): e2m1 x e4m3 -> f16 (cvt.rn.f16x2.e2m1x2, then one f16x2 multiply: both exact,
 //       the product has at most 6 significant bits) into the 128-byte-swizzled K-major layout the MMA
 //       reads; thread 0 also loads the stage's token rows (f16) with TMA;
-//   MMA issuer (warp 1, one thread): 128 x N x 16 f16 MMAs into TMEM (two weight parts, N = tokens
-//       rounded up to 16), double-buffered accumulators;
-//   epilogue (warps 2-5): per-group global scale and the layer's output conversion (Epi).
+//   MMA issuer (warp 1, one thread): M = 128 token rows (<= 64 real; the rest of the A tile is whatever
+//       follows in shared memory and lands in TMEM lanes nobody reads) x N = 256 weight rows (both parts)
+//       x K = 16 f16 MMAs into TMEM, double-buffered accumulators;
+//   epilogue (warps 2-3 hold the token lanes): per-group global scale and the layer's output conversion
+//       (Epi), one token row per thread, contiguous feature stores.
+// Tokens as M and weights as N: 256 weight rows per instruction, half the MMA instructions per weight byte
+// of a 128-row weight operand, and contiguous output rows in the epilogue.
 // Tokens are f16 because a kind::f16 MMA takes both operands in one type: the bf16 activations convert to
 // f16 exactly within f16's range (their 8 significant bits fit in 11), so the products are those of the
 // bf16 computation.  Why not tcgen05's block-scaled MMA: it scales fp4/fp6/fp8 operands only, and w4a16
@@ -42,15 +46,17 @@ struct Fp4Tile {
 
 template <int RSTAGES, int CSTAGES>
 struct Fp4Layout {
-  static constexpr int kAPart = 128 * kBK * 2;                 // one 128 x 64 f16 weight part (16 KB)
-  static constexpr int kBBytes = kFp4NB * kBK * 2;             // 64 token rows (8 KB)
-  static constexpr int kConvStage = 2 * kAPart + kBBytes;      // 40 KB, 1024-aligned
+  // conv stage: token rows (A, 64 rows = 8 KB; the MMA reads 128 rows, the upper 64 from the weight part
+  // that follows) then the two 128-row weight parts (B, 256 rows x 64 f16 = 32 KB)
+  static constexpr int kTokBytes = kFp4NB * kBK * 2;
+  static constexpr int kWPart = 128 * kBK * 2;
+  static constexpr int kConvStage = kTokBytes + 2 * kWPart;    // 40 KB, 1024-aligned
   static constexpr int kRawStage = 2 * kFp4Block + 2 * kFp4ScaleBlock;
   static constexpr int kRawOffset = CSTAGES * kConvStage;
   static constexpr int kBarOffset = kRawOffset + RSTAGES * kRawStage;
   static constexpr int kBarBytes = (2 * RSTAGES + 2 * CSTAGES + 5) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
-  static constexpr uint32_t kTmemCols = 256;                   // 2 accumulators x 2 parts x 64 columns
+  static constexpr uint32_t kTmemCols = 512;                   // 2 accumulators x 256 weight columns
 };
 
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
@@ -209,27 +215,23 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       int it = 0;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
         const Fp4Tile ti = sched.tile(t);
-        const uint32_t idesc = idesc_f16_f32(128, (ti.n_valid + 15) & ~15);
+        constexpr uint32_t idesc = idesc_f16_f32(128, 256);
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, kSiteMmaTmemEmpty)) break;
         tc_fence_after();
-        const uint32_t d_base = tmem_base + acc * 2 * kFp4NB;
+        const uint32_t d_base = tmem_base + acc * 256;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&conv_full[stage], phase, abort_flag, kSiteMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * L::kConvStage);
-          const uint32_t b_addr = a_addr + 2 * L::kAPart;
+          const uint32_t a_addr = smem_u32(smem + stage * L::kConvStage);   // token rows
+          const uint32_t b_addr = a_addr + L::kTokBytes;                      // 256 weight rows
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-            const uint64_t bdesc = sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2);
-#pragma unroll
-            for (int a = 0; a < 2; ++a)
-              mma_bf16(d_base + a * kFp4NB, sdesc_sw128_kmajor(a_addr + a * L::kAPart + kk * kUmmaK * 2), bdesc, idesc,
-                       (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            mma_bf16(d_base, sdesc_sw128_kmajor(a_addr + kk * kUmmaK * 2), sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2),
+                     idesc, (kb | kk) != 0);
           mma_commit(&conv_empty[stage]);
           issued = true;
           if (++stage == CSTAGES) {
@@ -263,8 +265,7 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
         uint8_t* cst = smem + cstage * L::kConvStage;
         if (ct == 0) {
           mbar_arrive_expect_tx(&conv_full[cstage], (16u << bi) * kBK * 2);
-          tma_load_2d(cst + 2 * L::kAPart, &tmB.m[bi], &conv_full[cstage], kb * kBK, ti.b_row,
-                      l2_policy_evict_normal());
+          tma_load_2d(cst, &tmB.m[bi], &conv_full[cstage], kb * kBK, ti.b_row, l2_policy_evict_normal());
           armed = true;
           armed_stage = cstage;
           armed_ph = cphase;
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
           const uint4 c0 = crow[0], c1 = crow[1];
           const uint32_t sc = *reinterpret_cast<const uint32_t*>(rst + 2 * kFp4Block + a * kFp4ScaleBlock + ct * 4);
           const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          uint8_t* drow = cst + a * L::kAPart + ct * 128;
+          uint8_t* drow = cst + L::kTokBytes + a * L::kWPart + ct * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {   // 16-byte chunk j = elements 8j..8j+7, scale j / 2
             const uint32_t s2 = e4m3_to_f16x2((sc >> (8 * (j >> 1))) & 0xffu);
@@ -304,7 +305,7 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     if (ct == 0 && armed) mbar_wait_drain(&conv_full[armed_stage], armed_ph, kSiteDrainTma);
   } else {
     // -------------------------------------------------------------------- epilogue (128 threads)
-    const int quad = warp & 3;
+    const int quad = warp & 3;   // TMEM lanes = token rows 32 * quad .. + 31 (only quads 0, 1 hold tokens)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
@@ -312,8 +313,10 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const Fp4Tile ti = sched.tile(t);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * 2 * kFp4NB;
-      Epi::run(ep, ti, quad * 32 + static_cast<int>(lane), taddr);
+      if (quad * 32 < ti.n_valid) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * 256;
+        Epi::run(ep, ti, quad * 32 + static_cast<int>(lane), taddr);
+      }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
