@@ -268,17 +268,19 @@ int kdb_moe_forward(const void* x, const float* router_w, const float* router_bi
  * x bf16 [t, h]; topk_ids int32 / topk_w fp32 [t, k] over e_total experts, of which ids 0..local-1 live
  * here (routes to other ids are skipped); y bf16 [t, h] = sum over local routes j of
  * topk_w * rms_norm(y_j), y_j = (bf16(silu(x.W1^T gs13) * (x.W3^T gs13)) . W2^T) gs2, rms_norm(v) =
- * v * rsqrt(mean(v^2) + 1e-8).  Weights NVFP4 (E2M1 codes, E4M3 scale per 16 elements, fp32 global scale
- * per expert tensor), tiled: w13_codes [local][2i/128][h/64][128 rows][32 B], w13_scales
- * [local][2i/128][h/64][128][4 B], rows 0..i-1 gate and i..2i-1 up; w2_codes [local][h/128][i/64][128][32 B],
- * w2_scales [local][h/128][i/64][128][4 B]; gscales fp32 [local].  h % 256 == 0, h <= 8192, i % 128 == 0.
- * workspace >= kdb_moe_w4a16_workspace_bytes, 256-byte aligned.
+ * v * rsqrt(mean(v^2) + 1e-8).  Weights NVFP4 (E2M1 codes two per byte, low nibble first; E4M3 scale per
+ * 16 elements; fp32 global scale per expert tensor), as 9216-byte blocks, one per (expert, weight tile,
+ * 64-element k chunk), tiles and chunks in order: [part 0 codes 128 x 32 B | part 1 codes | part 0 scales
+ * 128 x 4 B | part 1 scales].  w13_blocks [local][i/128][h/64]: tile f's part 0 = gate rows 128f.., part 1
+ * = up rows i + 128f..; w2_blocks [local][h/256][i/64]: parts = output rows 256f.. and 256f + 128..;
+ * gscales fp32 [local].  h % 256 == 0, h <= 8192, i % 128 == 0.  workspace >= kdb_moe_w4a16_workspace_bytes,
+ * 256-byte aligned.
  */
 size_t kdb_moe_w4a16_workspace_bytes(int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k);
-int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_codes,
-                          const void* w13_scales, const float* w13_gscale, const void* w2_codes, const void* w2_scales,
-                          const float* w2_gscale, void* y, int64_t t, int64_t h, int64_t i, int64_t local,
-                          int64_t e_total, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_blocks,
+                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, void* y, int64_t t,
+                          int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

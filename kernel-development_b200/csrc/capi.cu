@@ -258,13 +258,12 @@ size_t kdb_moe_w4a16_workspace_bytes(int64_t t, int64_t h, int64_t i, int64_t lo
   return kdb::moe_w4a16_workspace_bytes(t, h, i, local, e_total, k);
 }
 
-int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_codes,
-                          const void* w13_scales, const float* w13_gscale, const void* w2_codes, const void* w2_scales,
-                          const float* w2_gscale, void* y, int64_t t, int64_t h, int64_t i, int64_t local,
-                          int64_t e_total, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
-  return kdb::moe_w4a16_forward(x, topk_ids, topk_w, w13_codes, w13_scales, w13_gscale, w2_codes, w2_scales, w2_gscale,
-                                y, t, h, i, local, e_total, k, workspace, workspace_bytes,
-                                static_cast<cudaStream_t>(stream));
+int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_blocks,
+                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, void* y, int64_t t,
+                          int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  return kdb::moe_w4a16_forward(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, y, t, h, i, local,
+                                e_total, k, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -2,8 +2,10 @@
 //
 // The weights stream from HBM as NVFP4 (E2M1 codes, one E4M3 scale per 16 elements; 4.5 bits per weight)
 // and become tcgen05 operands only in shared memory:
-//   producer (warp 0, one thread): bulk copies of each 128-row x 64-element weight block's codes (4 KB) and
-//       scales (512 B) into a deep raw ring (prepare() stores every such block contiguously);
+//   producer (warp 0, one thread): one bulk copy per raw stage of two k chunks; prepare() stores, for each
+//       weight tile (two 128-row parts) and 64-element k chunk, both parts' codes (2 x 4 KB) and scales
+//       (2 x 512 B) contiguously and the chunks of a tile one after another, because each TMA operation
+//       carries a fixed cost that dominated when a chunk took four small copies;
 //   converter (warps 6-9): e2m1 x e4m3 -> f16 (cvt.rn.f16x2.e2m1x2, then one f16x2 multiply: both exact,
 //       the product has at most 6 significant bits) into the 128-byte-swizzled K-major layout the MMA
 //       reads; thread 0 also loads the stage's token rows (f16) with TMA;
@@ -34,14 +36,16 @@
 namespace kdb {
 
 constexpr int kFp4Threads = 320;       // warp 0 producer, 1 MMA, 2-5 epilogue, 6-9 converter
-constexpr int kFp4Block = 4096;        // codes of one 128-row x 64-element weight block
+constexpr int kFp4Block = 4096;        // codes of one 128-row x 64-element weight part
 constexpr int kFp4ScaleBlock = 512;    // its E4M3 scales (4 per row)
+constexpr int kFp4Chunk = 2 * kFp4Block + 2 * kFp4ScaleBlock;   // one k chunk of a weight tile: 9 KB
+constexpr int kFp4RawChunks = 2;       // k chunks per raw stage (one bulk copy)
 constexpr int kFp4NB = 64;             // tokens per tile at most
 constexpr unsigned int kSiteFp4Conv = 0x120;
 
-// One tile: weight parts at row tiles rt0 / rt1 of expert `group` times <= 64 token rows.
+// One tile: weight tile f (two 128-row parts) of expert `group` times <= 64 token rows.
 struct Fp4Tile {
-  int group, rt0, rt1, b_row, n_valid, f0;
+  int group, f, b_row, n_valid, f0;
 };
 
 template <int RSTAGES, int CSTAGES>
@@ -51,7 +55,7 @@ struct Fp4Layout {
   static constexpr int kTokBytes = kFp4NB * kBK * 2;
   static constexpr int kWPart = 128 * kBK * 2;
   static constexpr int kConvStage = kTokBytes + 2 * kWPart;    // 40 KB, 1024-aligned
-  static constexpr int kRawStage = 2 * kFp4Block + 2 * kFp4ScaleBlock;
+  static constexpr int kRawStage = kFp4RawChunks * kFp4Chunk;
   static constexpr int kRawOffset = CSTAGES * kConvStage;
   static constexpr int kBarOffset = kRawOffset + RSTAGES * kRawStage;
   static constexpr int kBarBytes = (2 * RSTAGES + 2 * CSTAGES + 5) * 8 + 16;
@@ -123,9 +127,8 @@ __device__ __forceinline__ uint32_t e4m3_to_f16x2(uint32_t byte) {
 
 template <class Sched, class Epi, int RSTAGES, int CSTAGES>
 __global__ void __launch_bounds__(kFp4Threads, 1)
-    gemm_fp4w_kernel(const __grid_constant__ TokenMaps tmB, const uint8_t* __restrict__ codes,
-                     const uint8_t* __restrict__ scales, const typename Sched::Params sp,
-                     const typename Epi::Params ep) {
+    gemm_fp4w_kernel(const __grid_constant__ TokenMaps tmB, const uint8_t* __restrict__ blocks,
+                     const typename Sched::Params sp, const typename Epi::Params ep) {
   using L = Fp4Layout<RSTAGES, CSTAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -182,20 +185,16 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       bool ok = true;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
         const Fp4Tile ti = sched.tile(t);
-        const long long blk0 = (static_cast<long long>(ti.group) * sp.row_tiles + ti.rt0) * nkb;
-        const long long blk1 = (static_cast<long long>(ti.group) * sp.row_tiles + ti.rt1) * nkb;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const uint8_t* tile_src = blocks + (static_cast<long long>(ti.group) * sp.f_tiles + ti.f) * nkb * kFp4Chunk;
+        for (int kb = 0; kb < nkb; kb += kFp4RawChunks) {
+          const int nc = min(kFp4RawChunks, nkb - kb);
           if (!mbar_wait(&raw_empty[stage], phase ^ 1u, abort_flag, kSiteProdEmpty)) {
             ok = false;
             break;
           }
           uint8_t* st = raw + stage * L::kRawStage;
-          mbar_arrive_expect_tx(&raw_full[stage], L::kRawStage);
-          bulk_load(st, codes + (blk0 + kb) * kFp4Block, kFp4Block, &raw_full[stage]);
-          bulk_load(st + kFp4Block, codes + (blk1 + kb) * kFp4Block, kFp4Block, &raw_full[stage]);
-          bulk_load(st + 2 * kFp4Block, scales + (blk0 + kb) * kFp4ScaleBlock, kFp4ScaleBlock, &raw_full[stage]);
-          bulk_load(st + 2 * kFp4Block + kFp4ScaleBlock, scales + (blk1 + kb) * kFp4ScaleBlock, kFp4ScaleBlock,
-                    &raw_full[stage]);
+          mbar_arrive_expect_tx(&raw_full[stage], nc * kFp4Chunk);
+          bulk_load(st, tile_src + static_cast<long long>(kb) * kFp4Chunk, nc * kFp4Chunk, &raw_full[stage]);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == RSTAGES) {
@@ -255,48 +254,51 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     for (int t = blockIdx.x; live && t < ntiles; t += gridDim.x) {
       const Fp4Tile ti = sched.tile(t);
       const int bi = box_index(ti.n_valid);
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; live && kb < nkb; kb += kFp4RawChunks) {
+        const int nc = min(kFp4RawChunks, nkb - kb);
         bool ok = mbar_wait(&raw_full[rstage], rphase, abort_flag, kSiteFp4Conv);
-        ok = ok && mbar_wait(&conv_empty[cstage], cphase ^ 1u, abort_flag, kSiteFp4Conv);
-        if (!conv_vote_all(ok)) {
-          live = false;
-          break;
-        }
-        uint8_t* cst = smem + cstage * L::kConvStage;
-        if (ct == 0) {
-          mbar_arrive_expect_tx(&conv_full[cstage], (16u << bi) * kBK * 2);
-          tma_load_2d(cst, &tmB.m[bi], &conv_full[cstage], kb * kBK, ti.b_row, l2_policy_evict_normal());
-          armed = true;
-          armed_stage = cstage;
-          armed_ph = cphase;
-        }
         const uint8_t* rst = raw + rstage * L::kRawStage;
+        for (int c = 0; c < nc; ++c) {
+          ok = ok && mbar_wait(&conv_empty[cstage], cphase ^ 1u, abort_flag, kSiteFp4Conv);
+          if (!conv_vote_all(ok)) {
+            live = false;
+            break;
+          }
+          uint8_t* cst = smem + cstage * L::kConvStage;
+          if (ct == 0) {
+            mbar_arrive_expect_tx(&conv_full[cstage], (16u << bi) * kBK * 2);
+            tma_load_2d(cst, &tmB.m[bi], &conv_full[cstage], (kb + c) * kBK, ti.b_row, l2_policy_evict_normal());
+            armed = true;
+            armed_stage = cstage;
+            armed_ph = cphase;
+          }
+          const uint8_t* rch = rst + c * kFp4Chunk;
 #pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          const uint4* crow = reinterpret_cast<const uint4*>(rst + a * kFp4Block + ct * 32);
-          const uint4 c0 = crow[0], c1 = crow[1];
-          const uint32_t sc = *reinterpret_cast<const uint32_t*>(rst + 2 * kFp4Block + a * kFp4ScaleBlock + ct * 4);
-          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          uint8_t* drow = cst + L::kTokBytes + a * L::kWPart + ct * 128;
+          for (int a = 0; a < 2; ++a) {
+            const uint4* crow = reinterpret_cast<const uint4*>(rch + a * kFp4Block + ct * 32);
+            const uint4 c0 = crow[0], c1 = crow[1];
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(rch + 2 * kFp4Block + a * kFp4ScaleBlock + ct * 4);
+            const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            uint8_t* drow = cst + L::kTokBytes + a * L::kWPart + ct * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {   // 16-byte chunk j = elements 8j..8j+7, scale j / 2
-            const uint32_t s2 = e4m3_to_f16x2((sc >> (8 * (j >> 1))) & 0xffu);
-            *reinterpret_cast<uint4*>(drow + ((j ^ (ct & 7)) << 4)) = dequant8(words[j], s2);
+            for (int j = 0; j < 8; ++j) {   // 16-byte chunk j = elements 8j..8j+7, scale j / 2
+              const uint32_t s2 = e4m3_to_f16x2((sc >> (8 * (j >> 1))) & 0xffu);
+              *reinterpret_cast<uint4*>(drow + ((j ^ (ct & 7)) << 4)) = dequant8(words[j], s2);
+            }
+          }
+          fence_proxy_async_smem();
+          conv_bar_sync();
+          if (ct == 0) mbar_arrive(&conv_full[cstage]);
+          if (++cstage == CSTAGES) {
+            cstage = 0;
+            cphase ^= 1u;
           }
         }
-        fence_proxy_async_smem();
-        conv_bar_sync();
-        if (ct == 0) {
-          mbar_arrive(&raw_empty[rstage]);
-          mbar_arrive(&conv_full[cstage]);
-        }
+        if (!live) break;
+        if (ct == 0) mbar_arrive(&raw_empty[rstage]);
         if (++rstage == RSTAGES) {
           rstage = 0;
           rphase ^= 1u;
-        }
-        if (++cstage == CSTAGES) {
-          cstage = 0;
-          cphase ^= 1u;
         }
       }
     }

@@ -32,8 +32,8 @@ int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int
 
 // NVFP4 w4a16 layer of one expert-parallel rank (moe_w4a16.cu).
 size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long long L, long long E, long long k);
-int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_codes, const void* w13_scales,
-                      const float* w13_gscale, const void* w2_codes, const void* w2_scales, const float* w2_gscale,
+int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_blocks, const float* w13_gscale,
+                      const void* w2_blocks, const float* w2_gscale,
                       void* y, long long T, long long H, long long I, long long L, long long E, long long k,
                       void* workspace, size_t workspace_bytes, cudaStream_t s);
 

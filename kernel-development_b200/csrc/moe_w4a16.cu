@@ -10,8 +10,10 @@
 //   down       y = bf16((h.W2^T) * gs2)
 //   combine    out[t] = sum over t's local routes j (in route order) of tw[t, j] * y * rsqrt(mean(y^2) + 1e-8)
 //
-// Weights arrive already tiled by prepare(): every 128-row x 64-element block of an expert tensor keeps its
-// 4 KB of E2M1 codes and 512 B of E4M3 scales contiguous (a lossless reordering of NVFP4).
+// Weights arrive already tiled by prepare() (a lossless reordering of NVFP4): for each expert, weight tile f
+// (gate_up: the gate rows of 128 features and their up rows; down: 256 output features as two 128-row
+// parts) and 64-element k chunk, one 9 KB block [part 0 codes | part 1 codes | part 0 scales | part 1
+// scales], the chunks of a tile consecutive: blocks [local][f_tiles][K / 64][9216 B].
 #include "gemm_fp4w_sm100.cuh"
 #include "host_util.h"
 #include "moe.h"
@@ -27,9 +29,7 @@ struct Fp4Sched {
   struct Params {
     const int* offsets;      // [groups + 1] token-row offsets of the local experts
     const int* tile_start;   // [groups + 1] exclusive prefix of ceil(count / 64)
-    int groups, f_tiles, nkb, row_tiles;
-    int rt_part1;            // row-tile offset of part 1 from part 0 (gate_up: I / 128, the up rows)
-    int rt_step;             // row tiles per weight tile (gate_up 1, down 2)
+    int groups, f_tiles, nkb;
     int f_step;              // output features per weight tile (gate_up 128, down 256)
   };
   Params p;
@@ -50,8 +50,7 @@ struct Fp4Sched {
     const int f = local / tcount, tt = local - f * tcount;
     Fp4Tile ti;
     ti.group = g;
-    ti.rt0 = f * p.rt_step;
-    ti.rt1 = ti.rt0 + p.rt_part1;
+    ti.f = f;
     ti.b_row = row_begin + tt * kW4Tokens;
     ti.n_valid = min(kW4Tokens, count - tt * kW4Tokens);
     ti.f0 = f * p.f_step;
@@ -256,9 +255,9 @@ size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long lon
 }
 
 template <class Epi>
-static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* codes, const uint8_t* scales,
-                       const Fp4Sched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
-  constexpr int RS = 10, CS = 3;   // 92 KB of NVFP4 in flight, 3 x 40 KB converted stages
+static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* blocks, const Fp4Sched::Params& sp,
+                       const typename Epi::Params& ep, cudaStream_t s) {
+  constexpr int RS = 4, CS = 3;   // 72 KB of NVFP4 in flight, 3 x 40 KB converted stages
   using L = Fp4Layout<RS, CS>;
   auto kern = gemm_fp4w_kernel<Fp4Sched, Epi, RS, CS>;
   static bool done[64] = {false};
@@ -273,22 +272,19 @@ static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* codes
   TokenMaps tb;
   int rc = make_token_maps(&tb, tokens, rows, K);
   if (rc) return rc;
-  kern<<<num_sms(), kFp4Threads, L::kSmemBytes, s>>>(tb, codes, scales, sp, ep);
+  kern<<<num_sms(), kFp4Threads, L::kSmemBytes, s>>>(tb, blocks, sp, ep);
   return cuda_status(cudaGetLastError());
 }
 
-int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_codes, const void* w13_scales,
-                      const float* w13_gscale, const void* w2_codes, const void* w2_scales, const float* w2_gscale,
+int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_blocks, const float* w13_gscale,
+                      const void* w2_blocks, const float* w2_gscale,
                       void* y, long long T, long long H, long long I, long long L, long long E, long long k,
                       void* workspace, size_t workspace_bytes, cudaStream_t s) {
   int rc = w4_check(T, H, I, L, E, k);
   if (rc) return rc;
   if (T == 0) return KDB_OK;
-  if (!x || !ids || !tw || !w13_codes || !w13_scales || !w13_gscale || !w2_codes || !w2_scales || !w2_gscale || !y)
-    return KDB_ERR_INVALID_ARG;
-  if (!aligned16(x) || !aligned16(w13_codes) || !aligned16(w13_scales) || !aligned16(w2_codes) ||
-      !aligned16(w2_scales) || !aligned16(y))
-    return KDB_ERR_INVALID_ARG;
+  if (!x || !ids || !tw || !w13_blocks || !w13_gscale || !w2_blocks || !w2_gscale || !y) return KDB_ERR_INVALID_ARG;
+  if (!aligned16(x) || !aligned16(w13_blocks) || !aligned16(w2_blocks) || !aligned16(y)) return KDB_ERR_INVALID_ARG;
   const W4Carve c = w4_carve(T, H, I, L, E, k);
   if (!workspace || workspace_bytes < c.total) return KDB_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return KDB_ERR_INVALID_ARG;
@@ -317,16 +313,12 @@ int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void
     sp.groups = Li;
     sp.f_tiles = Ii / 128;
     sp.nkb = Hi / kBK;
-    sp.row_tiles = 2 * Ii / 128;
-    sp.rt_part1 = Ii / 128;
-    sp.rt_step = 1;
     sp.f_step = 128;
     SwigluFp4Epi::Params ep;
     ep.out = reinterpret_cast<__half*>(ws + c.hbuf);
     ep.gscale = w13_gscale;
     ep.ld_out = Ii;
-    rc = launch_fp4w<SwigluFp4Epi>(ws + c.xf16, R, Hi, static_cast<const uint8_t*>(w13_codes),
-                                   static_cast<const uint8_t*>(w13_scales), sp, ep, s);
+    rc = launch_fp4w<SwigluFp4Epi>(ws + c.xf16, R, Hi, static_cast<const uint8_t*>(w13_blocks), sp, ep, s);
     if (rc) return rc;
   }
   {
@@ -336,16 +328,12 @@ int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void
     sp.groups = Li;
     sp.f_tiles = Hi / 256;
     sp.nkb = Ii / kBK;
-    sp.row_tiles = Hi / 128;
-    sp.rt_part1 = 1;
-    sp.rt_step = 2;
     sp.f_step = 256;
     ScaleFp4Epi::Params ep;
     ep.out = reinterpret_cast<__nv_bfloat16*>(ws + c.yrows);
     ep.gscale = w2_gscale;
     ep.ld_out = Hi;
-    rc = launch_fp4w<ScaleFp4Epi>(ws + c.hbuf, R, Ii, static_cast<const uint8_t*>(w2_codes),
-                                  static_cast<const uint8_t*>(w2_scales), sp, ep, s);
+    rc = launch_fp4w<ScaleFp4Epi>(ws + c.hbuf, R, Ii, static_cast<const uint8_t*>(w2_blocks), sp, ep, s);
     if (rc) return rc;
   }
   w4_combine_kernel<<<Ti, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(ws + c.yrows), ids, tw, Ip(c.slot_pos),

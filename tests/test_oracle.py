@@ -235,15 +235,23 @@ def test_w4a16_oracle_skips_remote_routes_and_normalises():
     assert abs(rms - 1.0 / 3) < 1e-3
 
 
-def test_w4a16_tiling_is_a_permutation():
+def test_w4a16_blocks_are_a_permutation():
     from kdb200 import workloads as W
     import importlib
     W4 = importlib.import_module("kdb200.moe_w4a16")
-    cfg = W.W4A16Config("t", 2, 256, 128, 2, 16, 2)
+    cfg = W.W4A16Config("t", 2, 256, 256, 2, 16, 2)
     wts = W.w4a16_weights(cfg, 1)
-    c, s = W4._tile(wts["w13"], wts["w13_scale"])
-    L, rows, half = wts["w13"].shape
-    # block (l, rt, kc) row r = original row rt*128 + r, bytes kc*32 .. kc*32+31
-    assert torch.equal(c[1, 1, 2, 5], wts["w13"][1, 128 + 5, 64:96])
-    assert torch.equal(s[0, 1, 3, 7], wts["w13_scale"][0, 128 + 7, 12:16].view(torch.uint8))
-    assert sorted(c.flatten().tolist()) == sorted(wts["w13"].flatten().tolist())
+    I = cfg.i
+    b13 = W4._blocks(wts["w13"], wts["w13_scale"], gate_up=True)            # [L, I/128, H/64, 9216]
+    assert tuple(b13.shape) == (2, I // 128, cfg.h // 64, 9216)
+    # tile f=1, chunk 2: part 0 row 5 = gate row 128 + 5, part 1 row 5 = up row I + 128 + 5
+    blk = b13[1, 1, 2]
+    assert torch.equal(blk[5 * 32:6 * 32], wts["w13"][1, 128 + 5, 64:96])
+    assert torch.equal(blk[4096 + 5 * 32:4096 + 6 * 32], wts["w13"][1, I + 128 + 5, 64:96])
+    assert torch.equal(blk[8192 + 512 + 7 * 4:8192 + 512 + 8 * 4], wts["w13_scale"][1, I + 128 + 7, 8:12].view(torch.uint8))
+    b2 = W4._blocks(wts["w2"], wts["w2_scale"], gate_up=False)               # [L, H/256, I/64, 9216]
+    blk2 = b2[0, 0, 1]
+    assert torch.equal(blk2[4096 + 3 * 32:4096 + 4 * 32], wts["w2"][0, 128 + 3, 32:64])
+    n = wts["w13"].numel() + wts["w13_scale"].numel()
+    assert b13.numel() == n and sorted(b13.flatten().tolist()) == sorted(
+        torch.cat([wts["w13"].flatten(), wts["w13_scale"].view(torch.uint8).flatten()]).tolist())
