@@ -1,28 +1,29 @@
-// gemm_fp4w_sm100.cuh — grouped expert GEMM with NVFP4 weights dequantised in shared memory (w4a16).
+// gemm_fp4w_sm100.cuh — grouped expert GEMM with NVFP4 weights dequantised on chip into TMEM (w4a16).
 //
 // The weights stream from HBM as NVFP4 (E2M1 codes, one E4M3 scale per 16 elements; 4.5 bits per weight)
-// and become tcgen05 operands only in shared memory:
+// and become f16 tcgen05 operands only on chip:
 //   producer (warp 0, one thread): one bulk copy per raw stage of two k chunks; prepare() stores, for each
 //       weight tile (two 128-row parts) and 64-element k chunk, both parts' codes (2 x 4 KB) and scales
 //       (2 x 512 B) contiguously and the chunks of a tile one after another, because each TMA operation
 //       carries a fixed cost that dominated when a chunk took four small copies;
 //   converter (warps 6-9): e2m1 x e4m3 -> f16 (cvt.rn.f16x2.e2m1x2, then one f16x2 multiply: both exact,
-//       the product has at most 6 significant bits) into the 128-byte-swizzled K-major layout the MMA
-//       reads; thread 0 also loads the stage's token rows (f16) with TMA;
-//   MMA issuer (warp 1, one thread): M = 128 token rows (<= 64 real; the rest of the A tile is whatever
-//       follows in shared memory and lands in TMEM lanes nobody reads) x N = 256 weight rows (both parts)
-//       x K = 16 f16 MMAs into TMEM, double-buffered accumulators;
-//   epilogue (warps 2-3 hold the token lanes): per-group global scale and the layer's output conversion
-//       (Epi), one token row per thread, contiguous feature stores.
-// Tokens as M and weights as N: 256 weight rows per instruction, half the MMA instructions per weight byte
-// of a 128-row weight operand, and contiguous output rows in the epilogue.
+//       the product has at most 6 significant bits) written straight into TMEM with tcgen05.st (lane =
+//       weight row, two k elements per 32-bit column), where the MMA takes its A operand; thread 0 also
+//       loads the stage's token rows (f16) into shared memory with TMA.  Staging the f16 weights in TMEM
+//       keeps them out of shared memory, whose bandwidth (32 KB of f16 written and read per 9 KB of NVFP4)
+//       bounded the version that converted into a swizzled shared-memory tile;
+//   MMA issuer (warp 1, one thread): A = 128 weight rows of each part from TMEM, B = the tile's tokens
+//       (N = tokens rounded up to 16) from shared memory, K = 16 per instruction, double-buffered
+//       accumulators (2 parts x 64 token columns each);
+//   epilogue (warps 2-5): per-group global scale and the layer's output conversion (Epi), TMEM lane =
+//       output feature, one token per column.
 // Tokens are f16 because a kind::f16 MMA takes both operands in one type: the bf16 activations convert to
 // f16 exactly within f16's range (their 8 significant bits fit in 11), so the products are those of the
 // bf16 computation.  Why not tcgen05's block-scaled MMA: it scales fp4/fp6/fp8 operands only, and w4a16
 // keeps the activations in 16 bits.
 //
 // Signalling (all waits bounded): raw_full (TMA tx), raw_empty (converter), conv_full (converter's
-// expect-tx for the tokens + its arrival after the weights are written and fenced for the async proxy),
+// expect-tx for the tokens + its arrival after its tcgen05.st of the weights completed and was fenced),
 // conv_empty (MMA commit), tfull / tempty (accumulators).  The converter warps vote after each wait so
 // their named barrier is reached by all four or none.
 #pragma once
@@ -50,17 +51,18 @@ struct Fp4Tile {
 
 template <int RSTAGES, int CSTAGES>
 struct Fp4Layout {
-  // conv stage: token rows (A, 64 rows = 8 KB; the MMA reads 128 rows, the upper 64 from the weight part
-  // that follows) then the two 128-row weight parts (B, 256 rows x 64 f16 = 32 KB)
-  static constexpr int kTokBytes = kFp4NB * kBK * 2;
-  static constexpr int kWPart = 128 * kBK * 2;
-  static constexpr int kConvStage = kTokBytes + 2 * kWPart;    // 40 KB, 1024-aligned
+  static constexpr int kTokBytes = kFp4NB * kBK * 2;           // one stage's token rows (B, 64 x 64 f16 = 8 KB)
   static constexpr int kRawStage = kFp4RawChunks * kFp4Chunk;
-  static constexpr int kRawOffset = CSTAGES * kConvStage;
+  static constexpr int kRawOffset = CSTAGES * kTokBytes;
   static constexpr int kBarOffset = kRawOffset + RSTAGES * kRawStage;
   static constexpr int kBarBytes = (2 * RSTAGES + 2 * CSTAGES + 5) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
-  static constexpr uint32_t kTmemCols = 512;                   // 2 accumulators x 256 weight columns
+  // TMEM: accumulators [0, 256) = 2 buffers x 2 weight parts x 64 token columns; then CSTAGES stages of the
+  // dequantised weights, 2 parts x 32 columns (64 f16 of K packed two per 32-bit column) each
+  static constexpr uint32_t kAccCols = 2 * kFp4NB;
+  static constexpr uint32_t kACol0 = 2 * kAccCols;
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(kACol0 + CSTAGES * 64 <= kTmemCols, "TMEM holds the accumulators and the weight stages");
 };
 
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
@@ -115,6 +117,32 @@ __device__ __forceinline__ uint4 dequant8(uint32_t word, uint32_t scale2) {
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(out.z) : "r"(h2), "r"(scale2));
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(out.w) : "r"(h3), "r"(scale2));
   return out;
+}
+
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes (lane i: v[0..31] of lane i).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem]: A is M = 128 lanes x K = 16 (eight 32-bit columns of packed f16 pairs).
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 
 // E4M3 byte -> {s, s} as f16x2.
@@ -214,23 +242,26 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       int it = 0;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
         const Fp4Tile ti = sched.tile(t);
-        constexpr uint32_t idesc = idesc_f16_f32(128, 256);
+        const uint32_t idesc = idesc_f16_f32(128, (ti.n_valid + 15) & ~15);
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, kSiteMmaTmemEmpty)) break;
         tc_fence_after();
-        const uint32_t d_base = tmem_base + acc * 256;
+        const uint32_t d_base = tmem_base + acc * L::kAccCols;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&conv_full[stage], phase, abort_flag, kSiteMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * L::kConvStage);   // token rows
-          const uint32_t b_addr = a_addr + L::kTokBytes;                      // 256 weight rows
+          const uint32_t b_addr = smem_u32(smem + stage * L::kTokBytes);            // token rows
+          const uint32_t a_col = tmem_base + L::kACol0 + stage * 64;                  // weight parts
 #pragma unroll
-          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-            mma_bf16(d_base, sdesc_sw128_kmajor(a_addr + kk * kUmmaK * 2), sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2),
-                     idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            const uint64_t bdesc = sdesc_sw128_kmajor(b_addr + kk * kUmmaK * 2);
+#pragma unroll
+            for (int a = 0; a < 2; ++a)
+              mma_f16_tmem_a(d_base + a * kFp4NB, a_col + a * 32 + kk * 8, bdesc, idesc, (kb | kk) != 0);
+          }
           mma_commit(&conv_empty[stage]);
           issued = true;
           if (++stage == CSTAGES) {
@@ -247,7 +278,9 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     }
   } else if (warp >= 6) {
     // -------------------------------------------------------------------- converter (128 threads)
-    const int ct = threadIdx.x - 192;   // weight row of both parts this thread converts
+    const int ct = threadIdx.x - 192;
+    const int wrow = (warp & 3) * 32 + static_cast<int>(lane);   // weight row (= TMEM lane) this thread converts
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t rstage = 0, rphase = 0, cstage = 0, cphase = 0;
     bool live = true, armed = false;
     uint32_t armed_stage = 0, armed_ph = 0;
@@ -264,7 +297,8 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
             live = false;
             break;
           }
-          uint8_t* cst = smem + cstage * L::kConvStage;
+          tc_fence_after();   // the MMAs that read this TMEM stage completed (conv_empty) before it is rewritten
+          uint8_t* cst = smem + cstage * L::kTokBytes;
           if (ct == 0) {
             mbar_arrive_expect_tx(&conv_full[cstage], (16u << bi) * kBK * 2);
             tma_load_2d(cst, &tmB.m[bi], &conv_full[cstage], (kb + c) * kBK, ti.b_row, l2_policy_evict_normal());
@@ -275,18 +309,23 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
           const uint8_t* rch = rst + c * kFp4Chunk;
 #pragma unroll
           for (int a = 0; a < 2; ++a) {
-            const uint4* crow = reinterpret_cast<const uint4*>(rch + a * kFp4Block + ct * 32);
+            const uint4* crow = reinterpret_cast<const uint4*>(rch + a * kFp4Block + wrow * 32);
             const uint4 c0 = crow[0], c1 = crow[1];
-            const uint32_t sc = *reinterpret_cast<const uint32_t*>(rch + 2 * kFp4Block + a * kFp4ScaleBlock + ct * 4);
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(rch + 2 * kFp4Block + a * kFp4ScaleBlock + wrow * 4);
             const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            uint8_t* drow = cst + L::kTokBytes + a * L::kWPart + ct * 128;
+            uint32_t v[32];   // 64 f16 of this row's chunk, k pairs packed per 32-bit column
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {   // 16-byte chunk j = elements 8j..8j+7, scale j / 2
-              const uint32_t s2 = e4m3_to_f16x2((sc >> (8 * (j >> 1))) & 0xffu);
-              *reinterpret_cast<uint4*>(drow + ((j ^ (ct & 7)) << 4)) = dequant8(words[j], s2);
+            for (int j = 0; j < 8; ++j) {   // elements 8j..8j+7, scale j / 2
+              const uint4 q = dequant8(words[j], e4m3_to_f16x2((sc >> (8 * (j >> 1))) & 0xffu));
+              v[4 * j] = q.x;
+              v[4 * j + 1] = q.y;
+              v[4 * j + 2] = q.z;
+              v[4 * j + 3] = q.w;
             }
+            tmem_st_32x32b_x32(tmem_base + lane_off + L::kACol0 + cstage * 64 + a * 32, v);
           }
-          fence_proxy_async_smem();
+          tmem_st_wait();
+          tc_fence_before();
           conv_bar_sync();
           if (ct == 0) mbar_arrive(&conv_full[cstage]);
           if (++cstage == CSTAGES) {
@@ -307,7 +346,7 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     if (ct == 0 && armed) mbar_wait_drain(&conv_full[armed_stage], armed_ph, kSiteDrainTma);
   } else {
     // -------------------------------------------------------------------- epilogue (128 threads)
-    const int quad = warp & 3;   // TMEM lanes = token rows 32 * quad .. + 31 (only quads 0, 1 hold tokens)
+    const int quad = warp & 3;   // TMEM lanes = weight rows 32 * quad .. + 31 of both parts
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
@@ -315,10 +354,8 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const Fp4Tile ti = sched.tile(t);
-      if (quad * 32 < ti.n_valid) {
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * 256;
-        Epi::run(ep, ti, quad * 32 + static_cast<int>(lane), taddr);
-      }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * L::kAccCols;
+      Epi::run(ep, ti, quad * 32 + static_cast<int>(lane), taddr);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

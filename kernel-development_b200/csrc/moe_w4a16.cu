@@ -60,9 +60,9 @@ struct Fp4Sched {
 
 __device__ __forceinline__ float silu_w4(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-// gate_up: accumulator lane = token row r of the tile, columns 0..127 = gate features f0..f0+127, 128..255
-// = their up rows.  h is rounded to bf16 (the layer's intermediate precision) and stored as the f16 of that
-// value (the down GEMM's token operand), 32 contiguous features per 64-byte store group.
+// gate_up: accumulator lane r = gate feature f0 + r (part 0) and its up row (part 1); columns = the tile's
+// tokens.  h is rounded to bf16 (the layer's intermediate precision) and stored as the f16 of that value
+// (the down GEMM's token operand); for each token the warp's 32 lanes store 32 consecutive features.
 struct SwigluFp4Epi {
   struct Params {
     __half* out;            // [rows, ld_out]
@@ -71,37 +71,28 @@ struct SwigluFp4Epi {
   };
   __device__ static void run(const Params& p, const Fp4Tile& ti, int r, uint32_t taddr) {
     const float gs = __ldg(p.gscale + ti.group);
-    const bool ok = r < ti.n_valid;
-    __half* row = p.out + static_cast<long long>(ti.b_row + r) * p.ld_out + ti.f0;
+    __half* col = p.out + ti.f0 + r;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
       uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(taddr + c * 32, g);
-      tmem_ld_32x32b_x32(taddr + 128 + c * 32, u);
+      tmem_ld_32x32b_x32(taddr + c0, g);
+      tmem_ld_32x32b_x32(taddr + kFp4NB + c0, u);
       tmem_ld_wait();
-      if (!ok) continue;
-      uint32_t packed[16];
+      const int n = min(32, ti.n_valid - c0);
+      __half* dst = col + static_cast<long long>(ti.b_row + c0) * p.ld_out;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float h[2];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const float v = silu_w4(__uint_as_float(g[2 * i + q]) * gs) * (__uint_as_float(u[2 * i + q]) * gs);
-          h[q] = __bfloat162float(__float2bfloat16_rn(v));
+      for (int i = 0; i < 32; ++i) {
+        if (i < n) {
+          const float h = silu_w4(__uint_as_float(g[i]) * gs) * (__uint_as_float(u[i]) * gs);
+          dst[static_cast<long long>(i) * p.ld_out] = __float2half_rn(__bfloat162float(__float2bfloat16_rn(h)));
         }
-        const __half2 hh = __floats2half2_rn(h[0], h[1]);
-        packed[i] = *reinterpret_cast<const uint32_t*>(&hh);
       }
-      uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
     }
   }
 };
 
-// down: accumulator lane = token row r, columns 0..255 = output features f0..f0+255, times gs2 of the
-// expert -> bf16, 32 contiguous features per 64-byte store group.
+// down: accumulator lane r of part a = output feature f0 + 128 a + r; columns = the tile's tokens; times gs2
+// of the expert -> bf16.
 struct ScaleFp4Epi {
   struct Params {
     __nv_bfloat16* out;     // [rows, ld_out]
@@ -110,22 +101,20 @@ struct ScaleFp4Epi {
   };
   __device__ static void run(const Params& p, const Fp4Tile& ti, int r, uint32_t taddr) {
     const float gs = __ldg(p.gscale + ti.group);
-    const bool ok = r < ti.n_valid;
-    __nv_bfloat16* row = p.out + static_cast<long long>(ti.b_row + r) * p.ld_out + ti.f0;
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(taddr + c * 32, v);
-      tmem_ld_wait();
-      if (!ok) continue;
-      uint32_t packed[16];
+    for (int a = 0; a < 2; ++a) {
+      __nv_bfloat16* col = p.out + ti.f0 + a * 128 + r;
+#pragma unroll 1
+      for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + a * kFp4NB + c0, v);
+        tmem_ld_wait();
+        const int n = min(32, ti.n_valid - c0);
+        __nv_bfloat16* dst = col + static_cast<long long>(ti.b_row + c0) * p.ld_out;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]) * gs, __uint_as_float(v[2 * i + 1]) * gs);
-      uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        for (int i = 0; i < 32; ++i)
+          if (i < n) dst[static_cast<long long>(i) * p.ld_out] = __float2bfloat16_rn(__uint_as_float(v[i]) * gs);
+      }
     }
   }
 };
@@ -257,7 +246,7 @@ size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long lon
 template <class Epi>
 static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* blocks, const Fp4Sched::Params& sp,
                        const typename Epi::Params& ep, cudaStream_t s) {
-  constexpr int RS = 4, CS = 3;   // 72 KB of NVFP4 in flight, 3 x 40 KB converted stages
+  constexpr int RS = 8, CS = 3;   // 144 KB of NVFP4 in flight, 3 x 8 KB token stages
   using L = Fp4Layout<RS, CS>;
   auto kern = gemm_fp4w_kernel<Fp4Sched, Epi, RS, CS>;
   static bool done[64] = {false};
