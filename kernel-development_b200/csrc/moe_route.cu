@@ -233,40 +233,56 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// One warp per chunk: walks the chunk's slots in (token, j) order and hands out rows in that order
-// within each expert.  Writes perm_slot, slot_pos, perm_token and perm_w.
-__global__ void __launch_bounds__(32)
+// One CTA per chunk.  The chunk's expert ids and routing weights are staged in shared memory by all 256
+// threads (coalesced loads, pieces of kScatterPiece slots); warp 0 then walks the slots in (token, j) order
+// and hands out rows in that order within each expert, so the serial walk reads only shared memory.
+// Writes perm_slot, slot_pos, perm_token and perm_w.
+constexpr int kScatterPiece = 2048;
+
+__global__ void __launch_bounds__(256)
     moe_plan_scatter_kernel(const int* __restrict__ ids, const float* __restrict__ topk_w, int T, int E, int k,
                             const int* __restrict__ chunk_base, int* __restrict__ perm_slot,
                             int* __restrict__ slot_pos, int* __restrict__ perm_token, float* __restrict__ perm_w) {
   extern __shared__ int cursor[];
-  const int lane = threadIdx.x;
+  __shared__ int s_id[kScatterPiece];
+  __shared__ float s_w[kScatterPiece];
   const int c = blockIdx.x;
-  for (int e = lane; e < E; e += 32) cursor[e] = chunk_base[static_cast<long long>(c) * E + e];
-  __syncwarp();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = chunk_base[static_cast<long long>(c) * E + e];
   const long long s0 = static_cast<long long>(c) * kPlanChunk * k;
   const long long s1 = min(static_cast<long long>(T) * k, s0 + static_cast<long long>(kPlanChunk) * k);
-  for (long long base = s0; base < s1; base += 32) {
-    const long long s = base + lane;
-    const bool valid = s < s1;
-    int e = valid ? ids[s] : -1;
-    if (valid && (e < 0 || e >= E)) e = -1;   // counted as a bounds error by the count kernel
-    const unsigned int peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    const int cur = (e >= 0) ? cursor[e] : 0;
-    __syncwarp();
-    if (e >= 0) {
-      const int pos = cur + rank;
-      perm_slot[pos] = static_cast<int>(s);
-      slot_pos[s] = pos;
-      perm_token[pos] = static_cast<int>(s / k);
-      perm_w[pos] = topk_w[s];
-      const int leader = 31 - __clz(peers);   // highest lane of the group advances the cursor
-      if (lane == leader) cursor[e] = cur + __popc(peers);
-    } else if (valid) {
-      slot_pos[s] = -1;
+  for (long long p0 = s0; p0 < s1; p0 += kScatterPiece) {
+    const int n = static_cast<int>(min(static_cast<long long>(kScatterPiece), s1 - p0));
+    __syncthreads();   // cursors written; the previous piece consumed
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      s_id[i] = ids[p0 + i];
+      s_w[i] = topk_w[p0 + i];
     }
-    __syncwarp();
+    __syncthreads();
+    if (threadIdx.x >= 32) continue;
+    const int lane = threadIdx.x;
+    for (int base = 0; base < n; base += 32) {
+      const int i = base + lane;
+      const long long s = p0 + i;
+      const bool valid = i < n;
+      int e = valid ? s_id[i] : -1;
+      if (valid && (e < 0 || e >= E)) e = -1;   // counted as a bounds error by the count kernel
+      const unsigned int peers = __match_any_sync(0xffffffffu, e);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int cur = (e >= 0) ? cursor[e] : 0;
+      __syncwarp();
+      if (e >= 0) {
+        const int pos = cur + rank;
+        perm_slot[pos] = static_cast<int>(s);
+        slot_pos[s] = pos;
+        perm_token[pos] = static_cast<int>(s / k);
+        perm_w[pos] = s_w[i];
+        const int leader = 31 - __clz(peers);   // highest lane of the group advances the cursor
+        if (lane == leader) cursor[e] = cur + __popc(peers);
+      } else if (valid) {
+        slot_pos[s] = -1;
+      }
+      __syncwarp();
+    }
   }
 }
 
@@ -395,8 +411,8 @@ int moe_plan(const int* ids, const float* topk_w, int T, int E, int k, int* chun
   moe_plan_scan_kernel<<<1, ((E + 31) / 32) * 32, 0, s>>>(chunk_counts, C, E, chunk_base, counts, offsets, mtile_start);
   rc = cuda_status(cudaGetLastError());
   if (rc) return rc;
-  moe_plan_scatter_kernel<<<C, 32, sizeof(int) * E, s>>>(ids, topk_w, T, E, k, chunk_base, perm_slot, slot_pos,
-                                                         perm_token, perm_w);
+  moe_plan_scatter_kernel<<<C, 256, sizeof(int) * E, s>>>(ids, topk_w, T, E, k, chunk_base, perm_slot, slot_pos,
+                                                          perm_token, perm_w);
   return cuda_status(cudaGetLastError());
 }
 
