@@ -75,6 +75,49 @@ def test_moe_workspace_and_shape_checks(lib):
     assert lib.kdb_moe_plan_workspace_bytes(100, 16, 4) > 0
 
 
+def test_w4a16_host_checks(lib):
+    # one ep8 rank of the NVFP4 layer: 32 local of 256 experts, H = I = 4096, top-8
+    assert lib.kdb_moe_w4a16_workspace_bytes(256, 4096, 4096, 32, 256, 8) > 0
+    assert lib.kdb_moe_w4a16_workspace_bytes(256, 4000, 4096, 32, 256, 8) == 0   # H % 256 != 0
+    assert lib.kdb_moe_w4a16_workspace_bytes(256, 4096, 4000, 32, 256, 8) == 0   # I % 128 != 0
+    assert lib.kdb_moe_w4a16_workspace_bytes(256, 4096, 4096, 300, 256, 8) == 0  # local > total experts
+    vp = ctypes.c_void_p
+    ptrs = [vp(256)] * 8
+    shape = (16, 4096, 4096, 32, 256, 8)
+    need = lib.kdb_moe_w4a16_workspace_bytes(*shape)
+    # no tokens: nothing to do, whatever the pointers
+    assert lib.kdb_moe_w4a16_forward(*([None] * 8), 0, 4096, 4096, 32, 256, 8, None, 0, None) == 0
+    # null, misaligned, too small a workspace: rejected before any launch
+    assert lib.kdb_moe_w4a16_forward(*([None] + ptrs[1:]), *shape, vp(256), need, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_moe_w4a16_forward(*([vp(264)] + ptrs[1:]), *shape, vp(256), need, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_moe_w4a16_forward(*ptrs, *shape, vp(256), need - 1, None) == _lib.KDB_ERR_WORKSPACE
+    assert lib.kdb_moe_w4a16_forward(*ptrs, *shape, vp(384), need, None) == _lib.KDB_ERR_INVALID_ARG  # 256-B alignment
+    assert lib.kdb_moe_w4a16_forward(*ptrs, 16, 4096, 4000, 32, 256, 8, vp(256), need, None) == _lib.KDB_ERR_UNSUPPORTED
+
+
+def test_f32w_projection_host_checks(lib):
+    vp = ctypes.c_void_p
+    assert lib.kdb_proj_split_f32(None, None, 0, 7168, None) == 0
+    assert lib.kdb_proj_split_f32(None, vp(16), 256, 7168, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_f32w(None, None, None, 0, 256, 7168, None, 0, None) == 0
+    assert lib.kdb_proj_f32w(vp(16), vp(16), None, 4, 256, 7168, None, 0, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_f32w(vp(16), vp(16), vp(16), 4, 256, 7100, None, 0, None) == _lib.KDB_ERR_UNSUPPORTED
+    assert lib.kdb_proj_f32w(vp(17), vp(16), vp(16), 4, 256, 7168, None, 0, None) == _lib.KDB_ERR_INVALID_ARG
+    assert lib.kdb_proj_f32w_workspace_bytes(200, 256, 7168) == 0     # above 128 rows: no K split
+    assert lib.kdb_proj_f32w_workspace_bytes(0, 256, 7168) == 0
+
+
+def test_sm_budget_round_trip(lib):
+    old = lib.kdb_set_sm_budget(16)
+    try:
+        assert lib.kdb_sm_budget() == 16
+        assert lib.kdb_set_sm_budget(-5) == 16    # negative clears the budget
+        assert lib.kdb_sm_budget() == 0
+    finally:
+        lib.kdb_set_sm_budget(old)
+    assert lib.kdb_sm_budget() == old
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "nope.so")
