@@ -1,6 +1,6 @@
 """Seeded synthetic workloads for the projection and the MoE layer.
 
-Shapes and value distributions follow the benchmark configurations of this build:
+Shapes and value distributions of the benchmark workloads:
 
   projection   Y[M, N] = X[M, K] · W[N, K]ᵀ;  X ~ N(0, 1), W ~ N(0, 1/K), both rounded to bf16
                proj_2048:        M=128, K=N=2048

@@ -1,7 +1,7 @@
 """oracle — CPU restatement of the two hot paths.  TEST INFRASTRUCTURE, NOT PRODUCT CODE.
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this package, and only
-as the checker (or as the timed CPU baseline).  The product path (kernel-development_b200/kdb200 and
+to verify GPU results (or as the timed CPU baseline).  The product path (kernel-development_b200/kdb200 and
 libkdb200.so) never imports, links or executes anything here.
 
 What it restates:
@@ -11,7 +11,7 @@ What it restates:
               SwiGLU experts (gate_up, silu(g)*u rounded to bf16, down); weighted combine; shared
               expert.  Structure follows the reference engine's plan/expert/combine stages
               (okc-challenge/engines/x3_h.cu:346-385 plan, sc_h.cu:322-340 SwiGLU epilogue,
-              sc_h.cu:374-381 weighted combine), with the math of this build's bf16 layer.
+              sc_h.cu:374-381 weighted combine), with the math of the bf16 layer.
   routing.c   the integer/bit-exact part of routing in C: fixed-order fp64 router logits, top-k,
               the stable (expert, token) permutation.  Built by oracle/build.py.
   problems/   kdev problem dirs (TASK.md + reference.py) and TOMLs so kdev's OKC adapter, `kdev check`

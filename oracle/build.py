@@ -1,6 +1,6 @@
 """Compile the oracle's C restatement (routing.c) into oracle/_build/liboracle_routing.so.
 
-TEST INFRASTRUCTURE: the library is the checker for the GPU routing kernels and is loaded only by
+TEST INFRASTRUCTURE: the library verifies the GPU routing kernels and is loaded only by
 tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg.
 
     python oracle/build.py [--force]

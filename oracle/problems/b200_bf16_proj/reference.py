@@ -1,4 +1,4 @@
-"""kdev problem reference for the B200 bf16 projection.  TEST INFRASTRUCTURE (the checker kdev's
+"""kdev problem reference for the B200 bf16 projection.  TEST INFRASTRUCTURE (the reference module kdev's
 OKC adapter imports: src/kdev/adapters/okc.py:476-575); the product never imports it.
 
 API (the one kdev's OkcAdapter calls): generate_weights(seed), generate_input(m, layer, seed),

@@ -1,5 +1,5 @@
 """kdev problem reference for the fused MoE layer, moe_decode configuration.  TEST INFRASTRUCTURE:
-the checker kdev imports; body in oracle/problems/moe_problem.py."""
+the reference module kdev imports; body in oracle/problems/moe_problem.py."""
 import sys
 from pathlib import Path
 

@@ -1,5 +1,5 @@
 """Shared body of the kdev MoE problem references (decode / prefill / skewed configurations).
-TEST INFRASTRUCTURE: imported only by oracle/problems/b200_moe_*/reference.py, the checkers kdev's
+TEST INFRASTRUCTURE: imported only by oracle/problems/b200_moe_*/reference.py, the reference modules kdev's
 OKC adapter loads (src/kdev/adapters/okc.py:476-575)."""
 import sys
 from pathlib import Path

@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import torch
 
-# Tolerances of the build's projection check: max-abs and relative Frobenius error against this
+# Tolerances of the projection check: max-abs and relative Frobenius error against this
 # fp32 reference (the bf16 rounding of Y alone gives a relative error near 2^-9 / sqrt(3)).
 MAX_ABS_TOL = 2e-2
 REL_FRO_TOL = 1e-2

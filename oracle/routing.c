@@ -1,11 +1,11 @@
 /*
- * oracle/routing.c — CPU restatement of the MoE routing plan.  TEST INFRASTRUCTURE ONLY: the checker
- * for the GPU router/permute kernels, never linked into libkdb200 and never on the product path.
+ * oracle/routing.c — CPU restatement of the MoE routing plan.  TEST INFRASTRUCTURE ONLY: it verifies
+ * the GPU router/permute kernels, is never linked into libkdb200 and is never on the product path.
  *
  * The reference's routing plan is the `up_moe` plan stage (okc-challenge/engines/x3_h.cu:346-385):
  * per-expert token masks, popcount counts, an exclusive scan giving each expert's base row, and the
- * list of routed (token, expert) pairs grouped by expert in token order.  The layer this build
- * implements routes with an fp32 router inside the layer (softmax over logits, top-k, renormalised
+ * list of routed (token, expert) pairs grouped by expert in token order.  The bf16 layer
+ * routes with an fp32 router inside the layer (softmax over logits, top-k, renormalised
  * weights), so the plan here starts from router logits:
  *
  *   1. logits[t, e] = fl32( dot(x[t, :], w[e, :]) ) (+ bias[e] as one fp32 add), where the dot

@@ -1,6 +1,6 @@
 """The drop-in boundary, exercised through kdev's own OKC adapter (CPU only).
 
-kdev's OkcAdapter (src/kdev/adapters/okc.py:318-577) loads this build's problem dirs and TOMLs
+kdev's OkcAdapter (src/kdev/adapters/okc.py:318-577) loads the problem dirs and TOMLs
 (oracle/problems/) and a submission file, and calls prepare / make_inputs / call / check exactly as
 `kdev check` does (src/kdev/checks/check.py:362-448).  The real submissions need a GPU, so the call
 path uses a CPU stand-in with the same two entry points; the real submission files are loaded (not
