@@ -232,18 +232,22 @@ W4A16_CONFIGS = {
 }
 
 
+# Decision boundaries between consecutive E2M1 magnitudes (midpoints of E2M1_VALUES), each with the side a
+# value exactly on it goes to: the even code of the two (mantissa 0), i.e. down at 0.25, 1.25, 2.5 and 5,
+# up at 0.75, 1.75 and 3.5.
+_E2M1_BOUNDS = ((0.25, False), (0.75, True), (1.25, False), (1.75, True), (2.5, False), (3.5, True), (5.0, False))
+
+
 def e2m1_encode(v: torch.Tensor) -> torch.Tensor:
     """Nearest E2M1 code (4 bits: sign, 2 exponent, 1 mantissa; ties to the even mantissa) of fp32 v,
-    saturating at +-6.  Returns uint8 codes 0..15."""
+    saturating at +-6.  Returns uint8 codes 0..15.  The magnitude code is the number of decision
+    boundaries the magnitude passes."""
     mag = v.abs().clamp(max=6.0)
-    grid = torch.tensor(E2M1_VALUES, dtype=torch.float32)
-    d = (mag.unsqueeze(-1) - grid).abs()
-    best = d.min(dim=-1, keepdim=True).values
-    # ties: prefer the even code (mantissa 0), i.e. the lowest index among equals with even index
-    tie_even = (d == best) & (torch.arange(8) % 2 == 0)
-    idx = torch.where(tie_even.any(-1), tie_even.float().argmax(-1), (d == best).float().argmax(-1))
-    sign = ((v < 0) & (idx > 0)).to(torch.uint8)
-    return (sign << 3) | idx.to(torch.uint8)
+    idx = torch.zeros(v.shape, dtype=torch.uint8, device=v.device)
+    for bound, tie_up in _E2M1_BOUNDS:
+        idx += (mag >= bound) if tie_up else (mag > bound)
+    idx |= ((v < 0) & (idx > 0)).to(torch.uint8) << 3
+    return idx
 
 
 def e2m1_decode(codes: torch.Tensor) -> torch.Tensor:

@@ -220,6 +220,23 @@ def test_nvfp4_codes_and_dequant_are_exact():
     assert rel < 0.12                                                      # 4-bit quantisation error
 
 
+def test_e2m1_encoder_is_nearest_with_ties_to_even():
+    from kdb200 import workloads as W
+    grid = torch.tensor(W.E2M1_VALUES)
+    mids = (grid[1:] + grid[:-1]) / 2
+    v = torch.cat([torch.randn(20000) * 3, mids, -mids, grid, -grid, torch.tensor([7.0, -7.0, 1e-30, -1e-30])])
+    codes = W.e2m1_encode(v)
+    # brute force: nearest magnitude, exact ties to the even index (mantissa bit 0), saturation at 6
+    mag = v.abs().clamp(max=6.0)
+    d = (mag.unsqueeze(-1) - grid).abs()
+    best = d.min(-1, keepdim=True).values
+    cand = d == best
+    even = cand & (torch.arange(8) % 2 == 0)
+    idx = torch.where(even.any(-1), even.float().argmax(-1), cand.float().argmax(-1))
+    want = (((v < 0) & (idx > 0)).to(torch.uint8) << 3) | idx.to(torch.uint8)
+    assert torch.equal(codes, want)
+
+
 def test_w4a16_oracle_skips_remote_routes_and_normalises():
     from kdb200 import workloads as W
     from oracle import moe_w4a16 as ow
