@@ -37,6 +37,12 @@ def _need(name: str, t: torch.Tensor, dtype: torch.dtype, dim: int) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+def _same_device(dev: torch.device, **tensors: Optional[torch.Tensor]) -> None:
+    for name, t in tensors.items():
+        if t is not None and t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, expected {dev} (the kernels read every operand there)")
+
+
 def pack_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
     """[E, 2I, H] (gate rows then up rows) -> the packed layout the gate_up GEMM reads."""
     _need("w_gate_up", w_gate_up, torch.bfloat16, 3)
@@ -53,8 +59,13 @@ def route(x: torch.Tensor, router: torch.Tensor, bias: Optional[torch.Tensor], k
     """(logits fp32 [T, E], topk_w fp32 [T, k], topk_ids int32 [T, k]) of the router stage."""
     _need("x", x, torch.bfloat16, 2)
     _need("router", router, torch.float32, 2)
+    if bias is not None:
+        _need("bias", bias, torch.float32, 1)
+    _same_device(x.device, router=router, bias=bias)
     t, h = x.shape
     e = router.shape[0]
+    if router.shape[1] != h or (bias is not None and tuple(bias.shape) != (e,)):
+        raise ValueError(f"router must be [E, {h}] and bias [E]")
     logits = torch.empty((t, e), dtype=torch.float32, device=x.device)
     w = torch.empty((t, k), dtype=torch.float32, device=x.device)
     ids = torch.empty((t, k), dtype=torch.int32, device=x.device)
@@ -68,8 +79,12 @@ def route(x: torch.Tensor, router: torch.Tensor, bias: Optional[torch.Tensor], k
 def plan(ids: torch.Tensor, topk_w: torch.Tensor, e: int) -> dict:
     """Permutation plan: counts [E], offsets [E+1], perm_slot [T*k], slot_pos [T*k] (int32)."""
     _need("topk_ids", ids, torch.int32, 2)
+    _need("topk_w", topk_w, torch.float32, 2)
+    if topk_w.shape != ids.shape:
+        raise ValueError("topk_ids and topk_w must have the same shape")
     t, k = ids.shape
     dev = ids.device
+    _same_device(dev, topk_w=topk_w)
     counts = torch.empty(e, dtype=torch.int32, device=dev)
     offsets = torch.empty(e + 1, dtype=torch.int32, device=dev)
     perm_slot = torch.empty(t * k, dtype=torch.int32, device=dev)
@@ -99,8 +114,13 @@ def prepare_router(router: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 def router_approx(x: torch.Tensor, split: torch.Tensor) -> torch.Tensor:
     """fp32 [T, E] tensor-core pre-pass logits x · [W_hi | W_mid]ᵀ (without bias)."""
+    _need("x", x, torch.bfloat16, 2)
+    _need("split", split, torch.bfloat16, 2)
+    _same_device(x.device, split=split)
     t, h = x.shape
     e = split.shape[0]
+    if split.shape[1] != 2 * h:
+        raise ValueError(f"split must be [E, {2 * h}] (prepare_router)")
     out = torch.empty((t, e), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
         rc = _lib.lib().kdb_moe_router_approx(x.data_ptr(), split.data_ptr(), out.data_ptr(), t, h, e,
@@ -112,8 +132,18 @@ def router_approx(x: torch.Tensor, split: torch.Tensor) -> torch.Tensor:
 def route_fast(x: torch.Tensor, router: torch.Tensor, bias: Optional[torch.Tensor], split: torch.Tensor,
                norms: torch.Tensor, k: int):
     """(topk_w, topk_ids) of the tensor-core routing path (identical to route()'s)."""
+    _need("x", x, torch.bfloat16, 2)
+    _need("router", router, torch.float32, 2)
+    _need("split", split, torch.bfloat16, 2)
+    _need("norms", norms, torch.float32, 1)
+    if bias is not None:
+        _need("bias", bias, torch.float32, 1)
+    _same_device(x.device, router=router, bias=bias, split=split, norms=norms)
     t, h = x.shape
     e = router.shape[0]
+    if (router.shape[1] != h or tuple(split.shape) != (e, 2 * h) or tuple(norms.shape) != (e,)
+            or (bias is not None and tuple(bias.shape) != (e,))):
+        raise ValueError(f"router [E, {h}], split [E, {2 * h}], norms [E] and bias [E] expected")
     w = torch.empty((t, k), dtype=torch.float32, device=x.device)
     ids = torch.empty((t, k), dtype=torch.int32, device=x.device)
     nbytes = int(_lib.lib().kdb_moe_route_fast_workspace_bytes(t, e))
@@ -155,7 +185,21 @@ def moe(x: torch.Tensor, router: torch.Tensor, router_bias: Optional[torch.Tenso
         shared, shared_i = shared_gate_up_packed.shape[0], shared_gate_up_packed.shape[1] // 2
     if router_bias is not None:
         _need("router_bias", router_bias, torch.float32, 1)
+        if tuple(router_bias.shape) != (e,):
+            raise ValueError(f"router_bias must be [{e}]")
+    if (router_split is None) != (router_norms is None):
+        raise ValueError("router_split and router_norms come together (prepare_router)")
+    if router_split is not None:
+        _need("router_split", router_split, torch.bfloat16, 2)
+        _need("router_norms", router_norms, torch.float32, 1)
+        if tuple(router_split.shape) != (e, 2 * h) or tuple(router_norms.shape) != (e,):
+            raise ValueError(f"router_split must be [{e}, {2 * h}] and router_norms [{e}]")
+    if shared_gate_up_packed is not None and tuple(shared_down.shape) != (shared, h, shared_i):
+        raise ValueError(f"shared_down must be [{shared}, {h}, {shared_i}]")
     dev = x.device
+    _same_device(dev, router=router, router_bias=router_bias, router_split=router_split, router_norms=router_norms,
+                 w_gate_up_packed=w_gate_up_packed, w_down=w_down, shared_gate_up_packed=shared_gate_up_packed,
+                 shared_down=shared_down)
     y = torch.empty((t, h), dtype=torch.bfloat16, device=dev)
     w = torch.empty((t, k), dtype=torch.float32, device=dev)
     ids = torch.empty((t, k), dtype=torch.int32, device=dev)

@@ -47,27 +47,49 @@ def prepare(weights: dict, device: str | torch.device = "cuda") -> dict:
             "local": L, "i": rows13 // 2, "h": weights["w2"].shape[1]}
 
 
+def _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_total):
+    """Shapes, dtypes and devices of kdb200::moe_w4a16's arguments; returns (T, H, I, local, k).  The kernel
+    receives raw pointers, so every tensor must be contiguous and on x's CUDA device."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("x must be bf16 [T, H]")
+    if topk_ids.dtype != torch.int32 or topk_w.dtype != torch.float32 or topk_ids.dim() != 2:
+        raise TypeError("topk_ids must be int32 and topk_w fp32, both [T, k]")
+    if w13_blocks.dtype != torch.uint8 or w2_blocks.dtype != torch.uint8 or w13_blocks.dim() != 4:
+        raise TypeError("NVFP4 blocks must be uint8 [local, tiles, k chunks, 9216] (use moe_w4a16.prepare)")
+    if w13_gscale.dtype != torch.float32 or w2_gscale.dtype != torch.float32:
+        raise TypeError("global scales must be fp32 [local]")
+    t, h = x.shape
+    k = topk_ids.shape[1]
+    local = w13_blocks.shape[0]
+    i = w13_blocks.shape[1] * 128
+    if topk_ids.shape != topk_w.shape or topk_ids.shape[0] != t:
+        raise ValueError(f"topk_ids {tuple(topk_ids.shape)} and topk_w {tuple(topk_w.shape)} must be [{t}, k]")
+    if tuple(w13_blocks.shape[2:]) != (h // 64, 9216) or tuple(w2_blocks.shape) != (local, h // 256, i // 64, 9216):
+        raise ValueError("NVFP4 blocks do not match x's hidden size (use moe_w4a16.prepare)")
+    if tuple(w13_gscale.shape) != (local,) or tuple(w2_gscale.shape) != (local,):
+        raise ValueError(f"global scales must be [{local}]")
+    if not local <= e_total:
+        raise ValueError(f"e_total ({e_total}) must be at least the number of local experts ({local})")
+    tensors = (x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale)
+    if not x.is_cuda or any(a.device != x.device for a in tensors):
+        raise ValueError("all tensors must be on one CUDA device (there is no CPU path)")
+    if not all(a.is_contiguous() for a in tensors):
+        raise ValueError("all tensors must be contiguous")
+    return t, h, i, local, k
+
+
 @torch.library.custom_op("kdb200::moe_w4a16", mutates_args=())
 def moe_w4a16(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13_blocks: torch.Tensor,
               w13_gscale: torch.Tensor, w2_blocks: torch.Tensor, w2_gscale: torch.Tensor, e_total: int) -> torch.Tensor:
     """y bf16 [T, H]: the rank's local routes (ids < local) through NVFP4 experts, RMS-normalised and
     weighted (kdb_moe_w4a16_forward)."""
-    if not x.is_cuda or x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
-        raise TypeError("x must be a contiguous bf16 [T, H] CUDA tensor (there is no CPU path)")
-    if topk_ids.dtype != torch.int32 or topk_w.dtype != torch.float32 or topk_ids.shape != topk_w.shape:
-        raise TypeError("topk_ids int32 and topk_w fp32, both [T, k]")
-    t, h = x.shape
-    k = topk_ids.shape[1]
-    local = w13_blocks.shape[0]
-    i = w13_blocks.shape[1] * 128
-    if tuple(w13_blocks.shape[2:]) != (h // 64, 9216) or tuple(w2_blocks.shape) != (local, h // 256, i // 64, 9216):
-        raise ValueError("NVFP4 blocks do not match x's hidden size (use moe_w4a16.prepare)")
+    t, h, i, local, k = _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_total)
     y = torch.empty((t, h), dtype=torch.bfloat16, device=x.device)
     nbytes = int(_lib.lib().kdb_moe_w4a16_workspace_bytes(t, h, i, local, e_total, k))
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         rc = _lib.lib().kdb_moe_w4a16_forward(
-            x.data_ptr(), topk_ids.contiguous().data_ptr(), topk_w.contiguous().data_ptr(), w13_blocks.data_ptr(),
+            x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), w13_blocks.data_ptr(),
             w13_gscale.data_ptr(), w2_blocks.data_ptr(), w2_gscale.data_ptr(), y.data_ptr(), t, h, i, local, e_total,
             k, ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream)
     _lib.check("kdb_moe_w4a16_forward", rc)
@@ -80,5 +102,5 @@ def _moe_w4a16_fake(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_g
 
 
 def forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, state: dict, e_total: int) -> torch.Tensor:
-    return moe_w4a16(x, topk_ids, topk_w, state["w13_blocks"], state["w13_gscale"], state["w2_blocks"],
-                     state["w2_gscale"], int(e_total))
+    return moe_w4a16(x, topk_ids.contiguous(), topk_w.contiguous(), state["w13_blocks"], state["w13_gscale"],
+                     state["w2_blocks"], state["w2_gscale"], int(e_total))

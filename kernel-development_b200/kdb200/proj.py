@@ -96,6 +96,8 @@ def proj_f32w(x: torch.Tensor, w_split: torch.Tensor) -> torch.Tensor:
     n, k2 = w_split.shape
     if k2 != 2 * k:
         raise ValueError(f"x is [{m}, {k}] but w_split is [{n}, {k2}]: expected [{n}, {2 * k}]")
+    if w_split.device != x.device:
+        raise ValueError("x and w_split must be on the same device")
     y = torch.empty((m, n), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
         nbytes = int(_lib.lib().kdb_proj_f32w_workspace_bytes(m, n, k)) if m > 0 and n > 0 and k > 0 else 0
