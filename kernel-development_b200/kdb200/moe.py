@@ -43,6 +43,19 @@ def _same_device(dev: torch.device, **tensors: Optional[torch.Tensor]) -> None:
             raise ValueError(f"{name} is on {t.device}, expected {dev} (the kernels read every operand there)")
 
 
+def _check_groups(a: torch.Tensor, width: int, groups: int, offsets: Optional[torch.Tensor],
+                  mtile_start: Optional[torch.Tensor]) -> None:
+    """Rows a [R, width] grouped by offsets [groups + 1] (+ the m-tile prefix, same length) on a's device."""
+    if a.shape[1] != width:
+        raise ValueError(f"rows are {a.shape[1]} wide, the weights expect {width}")
+    for name, t in (("offsets", offsets), ("mtile_start", mtile_start)):
+        if t is not None:
+            _need(name, t, torch.int32, 1)
+            if t.numel() != groups + 1:
+                raise ValueError(f"{name} must have groups + 1 = {groups + 1} entries")
+    _same_device(a.device, offsets=offsets, mtile_start=mtile_start)
+
+
 def pack_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
     """[E, 2I, H] (gate rows then up rows) -> the packed layout the gate_up GEMM reads."""
     _need("w_gate_up", w_gate_up, torch.bfloat16, 3)
@@ -255,7 +268,11 @@ def forward(x: torch.Tensor, state: dict):
 def gather_rows(x: torch.Tensor, index: torch.Tensor, div: int = 1, rows: Optional[int] = None) -> torch.Tensor:
     """out[r] = x[index[r] // div] (bf16 rows)."""
     _need("x", x, torch.bfloat16, 2)
+    _need("index", index, torch.int32, 1)
+    _same_device(x.device, index=index)
     n = index.numel() if rows is None else int(rows)
+    if not 0 <= n <= index.numel():
+        raise ValueError(f"rows ({n}) must be within the index's {index.numel()} entries")
     out = torch.empty((n, x.shape[1]), dtype=torch.bfloat16, device=x.device)
     with torch.cuda.device(x.device):
         rc = _lib.lib().kdb_moe_gather_rows(x.data_ptr(), index.data_ptr(), div, out.data_ptr(), n, x.shape[1],
@@ -267,7 +284,10 @@ def gather_rows(x: torch.Tensor, index: torch.Tensor, div: int = 1, rows: Option
 def expert_gate_up(a: torch.Tensor, w_packed: torch.Tensor, offsets: Optional[torch.Tensor] = None,
                    mtile_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Grouped gate_up + SwiGLU: a bf16 [R, H] (rows grouped as offsets say) -> bf16 [R, I]."""
+    _need("a", a, torch.bfloat16, 2)
+    _need("w_packed", w_packed, torch.bfloat16, 3)
     groups, two_i, h = w_packed.shape
+    _check_groups(a, h, groups, offsets, mtile_start)
     out = torch.empty((a.shape[0], two_i // 2), dtype=torch.bfloat16, device=a.device)
     with torch.cuda.device(a.device):
         rc = _lib.lib().kdb_moe_expert_gate_up(a.data_ptr(), a.shape[0], w_packed.data_ptr(), groups, two_i // 2, h,
@@ -279,7 +299,15 @@ def expert_gate_up(a: torch.Tensor, w_packed: torch.Tensor, offsets: Optional[to
 def expert_down(a: torch.Tensor, w_down: torch.Tensor, offsets: Optional[torch.Tensor] = None,
                 mtile_start: Optional[torch.Tensor] = None, row_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Grouped down projection: a bf16 [R, I] -> bf16 [R, H] (rows scaled by row_scale when given)."""
+    _need("a", a, torch.bfloat16, 2)
+    _need("w_down", w_down, torch.bfloat16, 3)
     groups, h, i = w_down.shape
+    _check_groups(a, i, groups, offsets, mtile_start)
+    if row_scale is not None:
+        _need("row_scale", row_scale, torch.float32, 1)
+        _same_device(a.device, row_scale=row_scale)
+        if row_scale.numel() != a.shape[0]:
+            raise ValueError(f"row_scale must have one entry per row ({a.shape[0]})")
     out = torch.empty((a.shape[0], h), dtype=torch.bfloat16, device=a.device)
     with torch.cuda.device(a.device):
         rc = _lib.lib().kdb_moe_expert_down(a.data_ptr(), a.shape[0], w_down.data_ptr(), groups, i, h, _ptr(offsets),
@@ -291,7 +319,22 @@ def expert_down(a: torch.Tensor, w_down: torch.Tensor, offsets: Optional[torch.T
 def combine(rows: torch.Tensor, slot_pos: torch.Tensor, t: int, k: int, slot_w: Optional[torch.Tensor] = None,
             shared_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y[t] = sum_j (slot_w or 1) * rows[slot_pos[t*k + j]] (+ shared_rows[t]) in fp32, bf16 out."""
+    _need("slot_pos", slot_pos, torch.int32, 1)
+    if rows.dim() == 2:
+        _need("rows", rows, torch.bfloat16, 2)
+    elif shared_rows is None:
+        raise ValueError("rows must be bf16 [R, H] unless shared_rows gives H")
+    if slot_pos.numel() != t * k:
+        raise ValueError(f"slot_pos must have t * k = {t * k} entries")
+    if slot_w is not None:
+        if slot_w.dtype != torch.float32 or slot_w.numel() != t * k or not slot_w.is_contiguous():
+            raise ValueError(f"slot_w must be contiguous fp32 with t * k = {t * k} entries")
+    if shared_rows is not None:
+        _need("shared_rows", shared_rows, torch.bfloat16, 2)
     h = rows.shape[1] if rows.dim() == 2 else shared_rows.shape[1]
+    if shared_rows is not None and tuple(shared_rows.shape) != (t, h):
+        raise ValueError(f"shared_rows must be [{t}, {h}]")
+    _same_device(slot_pos.device, rows=rows, slot_w=slot_w, shared_rows=shared_rows)
     y = torch.empty((t, h), dtype=torch.bfloat16, device=slot_pos.device)
     with torch.cuda.device(slot_pos.device):
         rc = _lib.lib().kdb_moe_combine(rows.data_ptr(), slot_pos.data_ptr(), _ptr(slot_w), _ptr(shared_rows),
@@ -304,6 +347,14 @@ def ep_regroup(counts: torch.Tensor, rows_in: Optional[torch.Tensor], to_expert_
                rows_out: Optional[torch.Tensor] = None):
     """Block transpose between source-major (s, e) and expert-major rows for counts int32 [P, Er];
     returns (rows_out, offsets [Er + 1], mtile_start [Er + 1])."""
+    _need("counts", counts, torch.int32, 2)
+    if rows_in is not None:
+        _need("rows_in", rows_in, torch.bfloat16, 2)
+        if rows_out is not None:
+            _need("rows_out", rows_out, torch.bfloat16, 2)
+            if rows_out.shape != rows_in.shape:
+                raise ValueError("rows_out must have rows_in's shape")
+    _same_device(counts.device, rows_in=rows_in, rows_out=rows_out)
     p, er = counts.shape
     dev = counts.device
     offsets = torch.empty(er + 1, dtype=torch.int32, device=dev)

@@ -71,3 +71,19 @@ def test_moe_helpers_check_before_launch():
         moe.route_fast(x, torch.zeros((8, 64)), None, torch.zeros((8, 128), dtype=torch.bfloat16), torch.zeros(8), 2)
     with pytest.raises(ValueError, match="CUDA"):
         moe.plan(torch.zeros((4, 2), dtype=torch.int32), torch.zeros((4, 2)), 8)
+
+
+def test_moe_stage_entry_points_check_before_launch():
+    from kdb200 import moe
+    a = torch.zeros((6, 64), dtype=torch.bfloat16)
+    idx = torch.zeros(6, dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe.gather_rows(a, idx)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe.expert_gate_up(a, torch.zeros((2, 256, 64), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        moe.expert_down(a, torch.zeros((2, 64, 64), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        moe.combine(a, idx, 3, 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe.ep_regroup(torch.zeros((2, 3), dtype=torch.int32), a, True)
