@@ -14,6 +14,8 @@ What it restates:
               sc_h.cu:374-381 weighted combine), with the math of the bf16 layer.
   routing.c   the integer/bit-exact part of routing in C: fixed-order fp64 router logits, top-k,
               the stable (expert, token) permutation.  Built by oracle/build.py.
+  moe_w4a16.py  the NVFP4 w4a16 MoE layer of one expert-parallel rank (post-expert RMS norm).
+  attention.py  fp8-KV paged decode / verify attention with its check (no GPU kernel for it yet).
   problems/   kdev problem dirs (TASK.md + reference.py) and TOMLs so kdev's OKC adapter, `kdev check`
               and `kdev ab` drive the ops unchanged.
 
