@@ -492,7 +492,10 @@ def run_reference(args, dist: Dist) -> dict | None:
                                                              "n_per_gpu": cfg.n},
             "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
-    b = cpu_baseline_moe(args.workload, steps=args.steps + args.warmup)
+    if args.workload.startswith("w4a16"):
+        b = cpu_baseline_w4a16(args.workload, steps=args.steps + args.warmup)
+    else:
+        b = cpu_baseline_moe(args.workload, steps=args.steps + args.warmup)
     return {"impl": "reference", "metric": "MoE layer tokens/s", "value": b["value"], "unit": "tokens/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload},
@@ -528,6 +531,32 @@ def cpu_baseline_moe(workload: str, steps: int = 3) -> dict:
     return {"value": round(statistics.median(rates), 2), "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{t_s} of {cfg.t} tokens through the full layer (router over all {cfg.e} experts, the "
                       f"{len(used)} experts they route to, shared expert), oracle/moe.py, median of {len(rates)}"}
+
+
+def cpu_baseline_w4a16(workload: str, steps: int = 3) -> dict:
+    """Oracle NVFP4 w4a16 layer (oracle/moe_w4a16.py: dequantise, fp32 GEMMs, RMS norm) on the host cores
+    over a bounded token sample, with the weights of the local experts that sample routes to."""
+    from kdb200 import workloads as W
+    from oracle import moe_w4a16 as ow
+
+    cores = _cpu_threads()
+    cfg = W.W4A16_CONFIGS[workload]
+    ids, tw = W.w4a16_routing(cfg, 1)
+    t_s = min(cfg.t, 16)
+    ids, tw = ids[:t_s], tw[:t_s]
+    hit = sorted({int(e) for e in ids.flatten().tolist() if int(e) < cfg.local})
+    remap = {e: j for j, e in enumerate(hit)}
+    sub = ids.clone().apply_(lambda e: remap.get(e, len(hit) + e))     # remote routes stay >= the local count
+    wts = W.w4a16_weights(cfg, 1, experts=hit)
+    x = W.moe_input(t_s, cfg.h, 1)
+    rates = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        ow.w4a16_ref(x, sub, tw, wts, len(hit))
+        rates.append(t_s / (time.perf_counter() - t0))
+    return {"value": round(statistics.median(rates), 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{t_s} of {cfg.t} tokens through the layer ({len(hit)} local experts hit), "
+                      f"oracle/moe_w4a16.py, median of {len(rates)}"}
 
 
 # ------------------------------------------------------------------------------------------------ main

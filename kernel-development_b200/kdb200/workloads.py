@@ -280,12 +280,13 @@ def nvfp4_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     return (vals.reshape(rows, -1, 16) * scales.float().unsqueeze(-1)).reshape(rows, -1)
 
 
-def w4a16_weights(cfg: W4A16Config, seed: int = 0) -> dict:
+def w4a16_weights(cfg: W4A16Config, seed: int = 0, experts: list[int] | None = None) -> dict:
     """NVFP4 weights of the local experts (CPU): w13 [L, 2I, H/2] uint8 (rows 0..I-1 gate, I..2I-1 up),
-    w13_scale [L, 2I, H/16] e4m3, w13_gscale [L] fp32, w2 [L, H, I/2], w2_scale [L, H, I/16], w2_gscale [L]."""
-    L, H, I = cfg.local, cfg.h, cfg.i
+    w13_scale [L, 2I, H/16] e4m3, w13_gscale [L] fp32, w2 [L, H, I/2], w2_scale [L, H, I/16], w2_gscale [L].
+    `experts` restricts (and orders) the experts drawn; each is the same as in the full set."""
+    H, I = cfg.h, cfg.i
     out = {k: [] for k in ("w13", "w13_scale", "w13_gscale", "w2", "w2_scale", "w2_gscale")}
-    for e in range(L):
+    for e in (range(cfg.local) if experts is None else experts):
         w13 = _randn((2 * I, H), (seed * 1000 + _TID_GU) * 4096 + e, "cpu", 1.0 / math.sqrt(H), torch.float32)
         w2 = _randn((H, I), (seed * 1000 + _TID_DOWN) * 4096 + e, "cpu", 1.0 / math.sqrt(I), torch.float32)
         for name, w in (("w13", w13), ("w2", w2)):

@@ -237,6 +237,16 @@ def test_e2m1_encoder_is_nearest_with_ties_to_even():
     assert torch.equal(codes, want)
 
 
+def test_w4a16_expert_subset_equals_full_set():
+    from kdb200 import workloads as W
+    cfg = W.W4A16Config("sub", 2, 256, 128, 4, 32, 2)
+    full = W.w4a16_weights(cfg, 3)
+    sub = W.w4a16_weights(cfg, 3, experts=[2, 0])
+    for k in ("w13", "w2", "w13_gscale", "w2_gscale"):
+        assert torch.equal(sub[k][0], full[k][2]) and torch.equal(sub[k][1], full[k][0])
+    assert torch.equal(sub["w13_scale"][0].view(torch.uint8), full["w13_scale"][2].view(torch.uint8))
+
+
 def test_w4a16_oracle_skips_remote_routes_and_normalises():
     from kdb200 import workloads as W
     from oracle import moe_w4a16 as ow
