@@ -239,7 +239,7 @@ def prepare(weights: dict, k: int) -> dict:
     """Untimed state for kernel_fn: packed gate/up weights; other weights referenced as given
     (the caller's tensors are not modified, and every value is kept bit-exact)."""
     dev = weights["w_gate_up"].device
-    if dev.type != "cuda":
+    if not weights["w_gate_up"].is_cuda:
         raise ValueError("MoE weights must be on a CUDA device")
     sgu = weights.get("shared_gate_up")
     bias = weights.get("router_bias")
