@@ -104,3 +104,34 @@ def test_case_fields_and_lengths():
     assert (c.q_heads, c.kv_heads) == (8, 1)
     lens = A.seq_lens(c, torch.Generator().manual_seed(0))
     assert int(lens[0]) == 80000 and bool((lens >= 5000).all()) and bool((lens <= 80000).all())
+
+
+# Case fields of the reference's own attention tests (muse_attention_decode.toml [[tests]] t0-t7, t9, t10,
+# t12, t13, t15); the ctx = 80k and 1M cases are left to the GPU.
+REFERENCE_TEST_CASES = {
+    "t0": {"batch": 1, "ctx": 10, "heads": "tp8", "layer": "sliding"},
+    "t1": {"batch": 3, "ctx": 2047, "heads": "tp8", "layer": "sliding"},
+    "t2": {"batch": 5, "ctx": 5000, "heads": "tp8", "layer": "sliding", "q_len": 8, "spread": "mixed", "page": 1},
+    "t3": {"batch": 4, "ctx": 3000, "heads": "tp8", "layer": "full"},
+    "t4": {"batch": 8, "ctx": 8192, "heads": "dp", "layer": "full", "spread": "mixed"},
+    "t6": {"batch": 4, "ctx": 6000, "heads": "tp8", "layer": "sliding", "dist": "edges", "page": 1},
+    "t7": {"batch": 4, "ctx": 6000, "heads": "tp8", "layer": "full", "q_len": 8, "dist": "edges"},
+    "t9": {"batch": 3, "ctx": 4000, "heads": "tp8", "layer": "sliding", "q_len": 8, "page": 1, "kv_scale": 0.015625},
+    "t10": {"batch": 2, "ctx": 9000, "heads": "tp8", "layer": "full", "kv_scale": 0.015625},
+    "t12": {"batch": 4, "ctx": 6000, "heads": "tp8", "layer": "sliding", "q_len": 8, "dist": "soft", "page": 1},
+    "t13": {"batch": 2, "ctx": 20000, "heads": "dp", "layer": "full", "q_len": 8, "dist": "soft"},
+    "t15": {"batch": 2, "ctx": 20000, "heads": "dp", "layer": "full", "q_len": 8, "dist": "coherent"},
+}
+
+
+@pytest.mark.parametrize("name", sorted(REFERENCE_TEST_CASES))
+def test_reference_test_shapes_run_and_check(name):
+    case = REFERENCE_TEST_CASES[name]
+    data = A.generate_input(case, seed=100 + len(name))
+    c = A.AttnCase.from_dict(case)
+    assert data["q"].shape == (c.batch, c.q_len, c.q_heads, A.HEAD_DIM)
+    assert data["k_cache"].dtype == torch.float8_e4m3fn and int(data["seq_lens"].max()) <= c.ctx
+    ref = A.attention_ref(data)
+    assert bool(torch.isfinite(ref).all())
+    ok, msg = A.check(data, ref.to(torch.bfloat16))
+    assert ok, msg
