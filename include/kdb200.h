@@ -7,7 +7,10 @@
  * synchronise: scratch comes from a caller-provided workspace, so each call is capturable in a CUDA
  * graph.  They return KDB_OK (0) or one of the KDB_ERR_* codes in kdb_status.h; asynchronous device
  * errors (a bounded wait that timed out, a kernel's own bounds check) land in the device status
- * word read by kdb_status_read().
+ * word read by kdb_status_read().  Two entry points depart from this, each described at its
+ * declaration: kdb_status_read synchronises the stream it is given, and kdb_moe_plan_noalloc takes
+ * its scratch from a fixed array inside the library (not from a workspace) and resolves that array's
+ * address with a runtime call on its first use per device, which must not happen inside a capture.
  *
  * The reference reaches these paths only through its problem-adapter boundary: the submission's
  * `prepare(weights) -> state` and `kernel_fn(data, state) -> out`, called by
@@ -57,6 +60,16 @@ int kdb_last_cuda_error(void);
  * its bounded spins (okc-challenge/engines/sc_h.cu:75-90), without the trap.
  */
 int kdb_status_read(uint32_t out[4], int clear, void* stream);
+
+/*
+ * Self-test of the device failure path: one CTA waits, with a limit of limit_ns of global time
+ * (1 us .. 2 s), on a barrier nothing arrives on, records KDB_ERR_TIMEOUT at site 0x1F0 in the device
+ * status word, frees its tensor memory and returns, exactly as any kernel of the library does when
+ * one of its bounded waits runs out.  Read the result with kdb_status_read.  No counterpart in the
+ * reference, whose bounded spins count timeouts into a debug buffer (okc-challenge/engines/
+ * sc_h.cu:75-90) that its tests never make run out.
+ */
+int kdb_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- */
 /* bf16 dense projection                                                                           */
@@ -166,8 +179,11 @@ int kdb_moe_plan(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_
  * cudaMalloc), who pass only their inputs and outputs.  Its scratch is a fixed 1,577,216-byte array
  * inside the library (held on every GPU that loads it until exit); limits t*k <= 131072,
  * e <= 1024, ceil(t/256)*e <= 65536, else KDB_ERR_UNSUPPORTED.  The first call on a device resolves
- * the array's address (a runtime call): make it before any stream capture.  Calls share the array:
- * calls that overlap on the GPU race, so issue them on one stream.  Outputs as kdb_moe_plan.
+ * the array's address (a runtime call): make it before any stream capture.  The address is cached for
+ * the life of the process; a caller that resets a device (cudaDeviceReset, or tearing down and
+ * re-creating its primary context) must not call this entry point on that device afterwards.  Calls
+ * share the array: calls that overlap on the GPU race, so issue them on one stream.  Outputs as
+ * kdb_moe_plan.
  */
 int kdb_moe_plan_noalloc(const int32_t* topk_ids, const float* topk_w, int64_t t, int64_t e, int64_t k,
                          int32_t* counts, int32_t* offsets, int32_t* perm_slot, int32_t* slot_pos, void* stream);

@@ -10,6 +10,7 @@
 
 namespace kdb {
 cudaError_t last_cuda_error();
+int selftest_wait_timeout(unsigned long long limit_ns, cudaStream_t s);
 }  // namespace kdb
 
 extern "C" {
@@ -51,6 +52,10 @@ int kdb_status_read(uint32_t out[4], int clear, void* stream) {
     rc = kdb::cuda_status(cudaStreamSynchronize(s));
   }
   return rc;
+}
+
+int kdb_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  return kdb::selftest_wait_timeout(limit_ns, static_cast<cudaStream_t>(stream));
 }
 
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,

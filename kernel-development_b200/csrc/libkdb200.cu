@@ -9,4 +9,5 @@
 #include "moe_ep.cu"
 #include "moe_noalloc.cu"
 #include "moe_w4a16.cu"
+#include "selftest.cu"
 #include "capi.cu"

@@ -14,7 +14,9 @@
 // Host code cannot use the array's name as a device address: its device address is resolved once per
 // device with cudaGetSymbolAddress, with that device current, the first time this entry point runs on
 // it.  That first call therefore makes a runtime call that must not happen inside a stream capture;
-// make it once before capturing.
+// make it once before capturing.  The resolved address is cached for the life of the process: after a
+// device reset (cudaDeviceReset, or a primary context torn down and created again) it no longer names
+// the array, so a caller that resets a device must not use this entry point on that device again.
 //
 // Every call shares the array and it keeps the last call's contents.  Nothing in it has to start at
 // zero: each call writes every cell it later reads (the per-chunk counts are written for every chunk

@@ -85,10 +85,11 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0u;
 }
 
-// Bounded wait for the phase of `bar` with parity `parity` to complete.  `abort_flag` is the CTA's
-// shared abort word: once any role of the CTA has given up, every other wait gives up too.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int site) {
+// Bounded wait for the phase of `bar` with parity `parity` to complete, giving up after `limit_ns` of
+// global time.  `abort_flag` is the CTA's shared abort word: once any role of the CTA has given up,
+// every other wait gives up too.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              unsigned int site, uint64_t limit_ns) {
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   uint32_t it = 0;
@@ -96,13 +97,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_test(bar, parity)) return true;
     if (((++it) & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > KDB_WAIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         report(KDB_ERR_TIMEOUT, site);
         *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// The library's waits: mbar_wait_for with the KDB_WAIT_NS limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int site) {
+  return mbar_wait_for(bar, parity, abort_flag, site, KDB_WAIT_NS);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_strerror": (ctypes.c_char_p, [_c_int]),
     "kdb_last_cuda_error": (_c_int, []),
     "kdb_status_read": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int, _c_vp]),
+    "kdb_selftest_wait_timeout": (_c_int, [ctypes.c_uint64, _c_vp]),
     "kdb_proj_bf16": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp]),
     "kdb_proj_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "kdb_proj_bf16_ws": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp]),

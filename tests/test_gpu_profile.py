@@ -10,7 +10,8 @@ import pytest
 
 from kdb200 import gpus
 
-KDEV_SRC = Path(os.environ.get("KDEV_SRC", "/root/reference/src"))
+# kdev itself: $KDEV_SRC (a source tree's `src`), else its offline install under baseline/_ref
+KDEV_SRC = Path(os.environ["KDEV_SRC"]) if os.environ.get("KDEV_SRC") else Path(__file__).resolve().parent.parent / "baseline" / "_ref"
 
 
 def test_profile_parses_without_kdev():

@@ -5,7 +5,7 @@ kdev's OkcAdapter (src/kdev/adapters/okc.py:318-577) loads the problem dirs and 
 `kdev check` does (src/kdev/checks/check.py:362-448).  The real submissions need a GPU, so the call
 path uses a CPU stand-in with the same two entry points; the real submission files are loaded (not
 called) to show they import cleanly through kdev's loader.  Skipped when kdev's sources are absent
-(KDEV_SRC, default: the reference checkout of this container)."""
+($KDEV_SRC, else kdev's offline install under baseline/_ref)."""
 from __future__ import annotations
 
 import os
@@ -17,7 +17,8 @@ import pytest
 import torch
 
 ROOT = Path(__file__).resolve().parent.parent
-KDEV_SRC = Path(os.environ.get("KDEV_SRC", "/root/reference/src"))
+# kdev itself: $KDEV_SRC (a source tree's `src`), else its offline install under baseline/_ref
+KDEV_SRC = Path(os.environ["KDEV_SRC"]) if os.environ.get("KDEV_SRC") else Path(__file__).resolve().parent.parent / "baseline" / "_ref"
 PROBLEMS = ROOT / "oracle" / "problems"
 SUBS = ROOT / "kernel-development_b200" / "submissions"
 

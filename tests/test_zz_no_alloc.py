@@ -76,4 +76,8 @@ def test_noalloc_plan_rejects_sizes_beyond_its_array():
     assert rc == _lib.KDB_ERR_UNSUPPORTED
     rc = lib.kdb_moe_plan_noalloc(ids.data_ptr(), w.data_ptr(), 4, 1025, 2, _vp(16), _vp(16), _vp(16), _vp(16), None)
     assert rc == _lib.KDB_ERR_UNSUPPORTED
+    # within the slot and expert limits but ceil(t / 256) * e = 256 * 1024 chunk cells > 65536
+    rc = lib.kdb_moe_plan_noalloc(ids.data_ptr(), w.data_ptr(), 65536, 1024, 1, _vp(16), _vp(16), _vp(16), _vp(16),
+                                  None)
+    assert rc == _lib.KDB_ERR_UNSUPPORTED
     assert b"not supported" in lib.kdb_strerror(rc)
