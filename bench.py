@@ -1,22 +1,24 @@
 #!/usr/bin/env python
-"""bench.py — throughput of the B200 bf16 projection / fused MoE layer, one JSON line.
+"""bench.py — throughput of the B200 fused MoE layer and bf16 projection, one JSON line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
 
-Default workload: proj_7168_m4096, Y[4096, 7168] = X[4096, 7168] · W[7168, 7168]ᵀ (the projection
-the ≥70 %-of-bf16-peak target is quoted on).  Other workloads: proj_2048, proj_7168_m{16,128,1024,16384},
-moe_decode, moe_prefill, moe_skewed (see kernel-development_b200/kdb200/workloads.py).
+Default workload: moe_prefill, the MoE layer the >=55 %-of-roofline and >=6x-at-8-GPUs targets are quoted on
+(T=8192 tokens, H=7168, 256 routed experts of I=2048 plus one shared expert, top-8; expert-parallel at
+N > 1 with T tokens and E/N experts per GPU).  The same line nests, under "projection", the
+Y[4096, 7168] = X[4096, 7168] . W[7168, 7168]^T projection (the >=70 %-of-bf16-peak target; column-parallel
+over N, no collective).  Other workloads: proj_2048, proj_7168_m{16,128,1024,4096,16384}, moe_decode,
+moe_skewed, moe_prefill_e32, w4a16_* (see kernel-development_b200/kdb200/workloads.py).
 
-A step is one pass of the op over one batch already resident in HBM, replayed from a CUDA graph.
-The L2 is flushed (a 512 MiB device write, then a read of it, untimed) before every timed step; each step is timed
-with CUDA events on its own stream; the time is the max over ranks.  At N > 1 the projection is
-column-parallel with N·7168 global output columns (each rank its own 7168-column shard, no
-collective: weak scaling); the MoE layer runs expert-parallel (E/N experts and T tokens per GPU, NCCL
-all-to-all dispatch and combine: weak scaling).
+A step is one pass of the op over one batch already resident in HBM, replayed from a CUDA graph (the
+expert-parallel layer runs eagerly).  The L2 is flushed (a 512 MiB device write, then a read of it, untimed)
+before every timed step; each step is timed with CUDA events on its own stream; the time is the max over
+ranks.  "e2e" repeats the measurement through the kdev-facing submission call with the inputs copied in
+from pinned host memory and the outputs copied back inside each timed step.
 
---impl reference times the oracle (the CPU restatement of the same math) on this host's cores on a
-bounded sample of the workload, and prints the same line with "impl": "reference".
+--impl reference times the path's PyTorch fp32 formulation (the oracle) on this host's cores on a bounded
+sample of the same workload and prints the same line with "impl": "reference".
 """
 from __future__ import annotations
 
@@ -36,7 +38,9 @@ for _p in (str(ROOT), str(ROOT / "kernel-development_b200")):
 
 import torch  # noqa: E402
 
-DEFAULT_WORKLOAD = "proj_7168_m4096"
+DEFAULT_WORKLOAD = "moe_prefill"
+NESTED_PROJ_WORKLOAD = "proj_7168_m4096"
+PROJ_METRIC = "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in roofline.frac)"
 FLUSH_BYTES = 512 << 20
 PROFILES = ROOT / "profiles"
 
@@ -298,15 +302,11 @@ def bench_proj(args, dist: Dist) -> dict | None:
         roof["kernel"] = (f"gemm_tn_pair_kernel<ProjSched<256,{bn}>> (256 x {bn} tiles on 2-CTA clusters)" if pair else
                           f"gemm_tn_kernel<ProjSched<128,{bn}>> (128 x {bn} tiles)") + ", one launch per step"
     line = {
-        "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in roofline.frac)",
+        "metric": PROJ_METRIC,
         "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded X~N(0,1), W~N(0,1/K), bf16)",
-        "config": {"workload": args.workload, "m": cfg.m, "k": cfg.k, "n_per_gpu": cfg.n,
-                   "n_total": cfg.n * dist.world,
-                   "parallelism": f"column-parallel over N, {dist.world} shard(s), no collective",
-                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
-                   "graph": "CUDA graph replay per step"},
+        "config": _proj_config(cfg, dist.world, args.workload),
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "path": "submissions/b200_bf16_proj.py kernel_fn (kdev adapter API) -> kdb_proj_bf16",
@@ -365,6 +365,42 @@ def cpu_baseline_proj(cfg, seconds: float, steps: int | None = None) -> dict:
 
 
 # ------------------------------------------------------------------------------------------------ MoE
+MOE_LAUNCHES_PER_CALL = {
+    # router pre-pass GEMM, candidates, exact top-k; plan count/scan/scatter; gather; grouped gate_up;
+    # grouped down; combine; [shared expert gate_up + down]
+    "base": 10, "shared": 2,
+    # expert parallel: two regroups of two kernels each
+    "ep": 4,
+}
+
+
+def _time_dominant_gate_up(state, x, cfg, flush, steps: int) -> dict:
+    """The layer's dominant kernel, the grouped SwiGLU gate_up GEMM, timed alone: its inputs (the routed
+    and permuted rows and the plan) are built once by the stage entry points, then each timed launch
+    follows an untimed L2 flush.  Returns its mean ms and algorithmic FLOPs per launch."""
+    from kdb200 import moe as M
+    w, ids = M.route_fast(x, state["router"], state["router_bias"], state["router_split"], state["router_norms"],
+                          cfg.k)
+    pl = M.plan(ids, w, cfg.e)
+    tiles = ((pl["counts"] + 511) // 512).to(torch.int32)
+    mtile = torch.zeros(cfg.e + 1, dtype=torch.int32, device=x.device)
+    mtile[1:] = torch.cumsum(tiles, 0)
+    xp = M.gather_rows(x, pl["perm_slot"], div=cfg.k)
+    for _ in range(3):
+        M.expert_gate_up(xp, state["w_gate_up_packed"], pl["offsets"], mtile)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        M.expert_gate_up(xp, state["w_gate_up_packed"], pl["offsets"], mtile)
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return {"ms": statistics.mean(times), "flops": 4.0 * cfg.t * cfg.k * cfg.h * cfg.i}
+
+
 def bench_moe(args, dist: Dist) -> dict | None:
     from kdb200 import moe as M
     from kdb200 import workloads as W
@@ -377,6 +413,7 @@ def bench_moe(args, dist: Dist) -> dict | None:
     holder = {}
     sampler = ClockSampler(_physical_index(dist.local)) if dist.rank == 0 else None
     ep = dist.world > 1
+    state = None
     if ep:
         # Expert parallel: this rank's T tokens, its E/P experts; rows cross NVLink by NCCL all-to-all.
         from kdb200 import ep as EP
@@ -401,14 +438,16 @@ def bench_moe(args, dist: Dist) -> dict | None:
             holder["out"] = M.forward(x, state)
 
         run_step = _capture(step).replay
+        sub = _load_submission("b200_moe_prefill")
 
         def forward(xx):
-            return M.forward(xx, state)
+            return sub.kernel_fn({"x": xx, "config": cfg.as_case()}, state)
     per_step, region_ms = timed_steps(run_step, args.steps, args.warmup, flush, dist, sampler)
     ms = dist.max(statistics.mean(per_step))
     value = cfg.t * dist.world / (ms * 1e-3)
     ids = holder["out"][2]
     distinct = int(torch.unique(ids).numel())
+    y_dev = holder["out"][0].clone()
 
     x_host = x.cpu().pin_memory()
     y_host = torch.empty((cfg.t, cfg.h), dtype=torch.bfloat16).pin_memory()
@@ -425,46 +464,62 @@ def bench_moe(args, dist: Dist) -> dict | None:
 
     e2e_steps, _ = timed_steps(e2e_step, max(3, args.steps // 4), 2, flush, dist, None)
     e2e_ms = dist.max(statistics.mean(e2e_steps))
+    if not torch.equal(y_host.to(dev), y_dev):
+        raise RuntimeError("e2e output differs from the device-resident run")
+    dom = _time_dominant_gate_up(state, x, cfg, flush, max(3, args.steps // 2)) if state is not None else None
     if dist.rank != 0:
         return None
     peaks = _peaks()
     flops = W.moe_flops(cfg)                   # per rank: T tokens' routed work (weak scaling under EP)
     nbytes = W.moe_bytes(cfg, cfg.e // dist.world if ep else distinct)
-    t_c = flops / (peaks["bf16_tflops_sustained"] * 1e12)
+    # each step is one flushed graph replay timed alone: the burst tensor peak applies
+    t_c = flops / (peaks["bf16_tflops"] * 1e12)
     t_m = nbytes / (peaks["hbm_gbs"] * 1e9)
     layer_s = statistics.mean(per_step) * 1e-3
     bound = "tensor" if t_c >= t_m else "hbm"
     if bound == "tensor":
         ach = flops / layer_s / 1e12
-        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops_sustained"],
-                "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops_sustained"], 4)}
+        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4)}
     else:
         ach = nbytes / layer_s / 1e9
         roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(ach / peaks["hbm_gbs"], 4)}
-    roof.update({"traffic": None, "peak_source": f"{peaks['source']} (sustained for tensor)",
-                 "kernel": "whole layer (route, plan, gather, grouped gate_up, grouped down, combine)",
-                 "layer_roofline_ms": round(max(t_c, t_m) * 1e3, 4)})
-    # ours per step: router pre-pass GEMM, candidates, exact top-k; plan (3); gather; [EP: 2 regroups of
-    # 2 kernels]; grouped gate_up; grouped down; [shared gate_up + down]; combine
-    launches = 10 + (4 if ep else 0) + (2 if cfg.shared else 0)
+    traffic = _profile_traffic("moe_layer", args.workload)
+    roof.update({"traffic": traffic, "peak_source": f"{peaks['source']} (burst: each step is timed alone)",
+                 "kernel": "whole layer per graph replay (route, plan, gather, grouped gate_up, grouped down, "
+                           "combine, shared expert)",
+                 "algorithmic_flops": flops, "algorithmic_bytes": nbytes, "distinct_experts_hit": distinct,
+                 "layer_roofline_ms": round(max(t_c, t_m) * 1e3, 4),
+                 "frac_of_layer_roofline": round(max(t_c, t_m) / layer_s, 4)})
+    if dom is not None:
+        common = {"ms_per_launch": round(dom["ms"], 4), "traffic": _profile_traffic("moe_gate_up", args.workload),
+                  "timing": "CUDA events around each launch after an untimed L2 flush"}
+        if cfg.t > 64:
+            dach = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
+            roof["dominant_kernel"] = {
+                "kernel": "gemm_grouped_pair_kernel<GroupedPairSched, SwigluGpEpi> (routed gate_up + SwiGLU)",
+                "bound": "tensor", "achieved": round(dach, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(dach / peaks["bf16_tflops"], 4), **common}
+        else:
+            gu_bytes = distinct * 2.0 * cfg.i * cfg.h * 2 + cfg.t * cfg.k * (cfg.h + cfg.i) * 2
+            gbs = gu_bytes / (dom["ms"] * 1e-3) / 1e9
+            roof["dominant_kernel"] = {
+                "kernel": "gemm_swap_kernel<StreamSched, SwigluStreamEpi> (routed gate_up + SwiGLU, weight stream)",
+                "bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(gbs / peaks["hbm_gbs"], 4), **common}
+    launches = MOE_LAUNCHES_PER_CALL["base"] + (MOE_LAUNCHES_PER_CALL["ep"] if ep else 0) + \
+        (MOE_LAUNCHES_PER_CALL["shared"] if cfg.shared else 0)
     if ep:
-        par = (f"expert-parallel over {dist.world} GPUs ({cfg.e // dist.world} experts each, NCCL all-to-all "
-               "dispatch and combine, weak scaling: T tokens per GPU)")
-        graph = "eager (row split sizes read back to the host once per call)"
         path = "kdb200.ep.ExpertParallelMoE -> kdb_moe_* stage entry points + NCCL all_to_all_single"
     else:
-        par, graph = "1 GPU", "CUDA graph replay per step"
-        path = "kdb200.moe.forward (kdev kernel_fn path) -> kdb_moe_forward"
-    return {
+        path = "submissions/b200_moe_prefill.py kernel_fn (kdev adapter API) -> kdb_moe_forward"
+    line = {
         "metric": "MoE layer tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; x~N(0,1) bf16, router N(0,1/H) fp32, experts N(0,1/fan_in) bf16)",
-        "config": {"workload": args.workload, **cfg.as_case(), "distinct_experts_hit": distinct,
-                   "parallelism": par,
-                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
-                   "graph": graph},
+        "config": _moe_config(cfg, dist.world, args.workload),
         "e2e": {"value": round(cfg.t * dist.world / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": cfg.t * cfg.h * 2,
                 "d2h_bytes_per_step": cfg.t * cfg.h * 2 + cfg.t * cfg.k * 8,
@@ -475,62 +530,138 @@ def bench_moe(args, dist: Dist) -> dict | None:
         "clocks": sampler.summary() if sampler else None,
         "timed_region_ms": round(region_ms, 2),
     }
+    if not args.no_cpu_baseline and dist.world == 1:
+        line["cpu_baseline"] = cpu_baseline_moe(args.workload, seconds=args.cpu_seconds)
+    return line
+
+
+def _load_submission(name: str):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        f"{name}_sub", ROOT / "kernel-development_b200" / "submissions" / f"{name}.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 # ------------------------------------------------------------------------------------------------ reference arm
-def run_reference(args, dist: Dist) -> dict | None:
+def _proj_config(cfg, world: int, workload: str) -> dict:
+    return {"workload": workload, "m": cfg.m, "k": cfg.k, "n_per_gpu": cfg.n, "n_total": cfg.n * world,
+            "parallelism": f"column-parallel over N, {world} shard(s), no collective",
+            "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
+            "graph": "CUDA graph replay per step"}
+
+
+def _moe_config(cfg, world: int, workload: str) -> dict:
+    if world > 1:
+        par = (f"expert-parallel over {world} GPUs ({cfg.e // world} experts each, NCCL all-to-all "
+               "dispatch and combine, weak scaling: T tokens per GPU)")
+        graph = "eager (row split sizes read back to the host once per call)"
+    else:
+        par, graph = "1 GPU", "CUDA graph replay per step"
+    return {"workload": workload, **cfg.as_case(), "parallelism": par,
+            "l2": "flushed before every timed step (512 MiB device write then read, untimed)", "graph": graph}
+
+
+def run_reference(args, dist) -> dict | None:
+    """The reference arm: the path's PyTorch fp32 formulation (the oracle) on this host's cores, on the same
+    workload, config, metric and unit as our arm; rank 0 only."""
+    from kdb200 import workloads as W
     if dist.rank != 0:
         return None
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    n = args.steps + args.warmup
     if args.workload.startswith("proj"):
         cfg = _proj_cfg(args.workload)
-        b = cpu_baseline_proj(cfg, 0.0, steps=args.steps + args.warmup)
+        b = cpu_baseline_proj(cfg, 0.0, steps=n)
         return {
-            "impl": "reference", "metric": "achieved TFLOP/s of the bf16 projection (% of bf16 tensor peak in "
-            "roofline.frac)", "value": b["value"], "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload, "m": cfg.m, "k": cfg.k,
-                                                             "n_per_gpu": cfg.n},
+            "impl": "reference", "metric": PROJ_METRIC, "value": b["value"], "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": _proj_config(cfg, world, args.workload),
             "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
     if args.workload.startswith("w4a16"):
-        b = cpu_baseline_w4a16(args.workload, steps=args.steps + args.warmup)
+        b = cpu_baseline_w4a16(args.workload, steps=n)
+        config = {"workload": args.workload}
     else:
-        b = cpu_baseline_moe(args.workload, steps=args.steps + args.warmup)
-    return {"impl": "reference", "metric": "MoE layer tokens/s", "value": b["value"], "unit": "tokens/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": {"workload": args.workload},
+        b = cpu_baseline_moe(args.workload, steps=n)
+        config = _moe_config(W.MOE_CONFIGS[args.workload], world, args.workload)
+    line = {"impl": "reference", "metric": "MoE layer tokens/s", "value": b["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
             "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
+    if args.workload == DEFAULT_WORKLOAD and not args.no_projection:
+        pcfg = _proj_cfg(NESTED_PROJ_WORKLOAD)
+        pb = cpu_baseline_proj(pcfg, 0.0, steps=n)
+        line["projection"] = {"metric": PROJ_METRIC, "value": pb["value"], "unit": "TFLOP/s",
+                              "config": _proj_config(pcfg, world, NESTED_PROJ_WORKLOAD), "cpu_baseline": pb}
+    return line
 
 
-def cpu_baseline_moe(workload: str, steps: int = 3) -> dict:
-    """Oracle MoE layer on the host cores over a bounded token sample with CPU-generated weights of the
-    workload's shape restricted to the experts the sample routes to."""
+def cpu_baseline_moe(workload: str, seconds: float = 10.0, steps: int | None = None) -> dict:
+    """The layer's PyTorch fp32 formulation on the host cores, costed per stage at the workload's real
+    sizes and extrapolated to the whole batch:
+      router  softmax(x.float() @ Wr.T (+ b)) -> top-k -> renormalised weights, on a token sample;
+      routed  the oracle's SwiGLU expert (fp32 GEMMs from bf16 weights, bf16 intermediate) on sampled
+              experts with all the tokens the full batch routes to them, plus the weighted index-add;
+      shared  the shared expert on a token sample.
+    tokens/s = 1 / (router s/token + k * routed s/route + shared s/token).  One evaluation runs each
+    stage once; evaluations repeat until `seconds` (or `steps` evaluations) and the median is reported."""
     from kdb200 import workloads as W
     from oracle import moe as om
 
     cores = _cpu_threads()
     cfg = W.MOE_CONFIGS[workload]
-    t_s = min(cfg.t, 16)
-    x = W.moe_input(t_s, cfg.h, seed=1)
-    router = W._randn((cfg.e, cfg.h), 3, "cpu", 1.0 / cfg.h ** 0.5, torch.float32)
+    x = W.moe_input(cfg.t, cfg.h, seed=1)
+    router = W._randn((cfg.e, cfg.h), 1 * 1000 + 3, "cpu", 1.0 / cfg.h ** 0.5, torch.float32)
     bias = W.zipf_router_bias(cfg.e, cfg.zipf_s, 1) if cfg.zipf_s > 0 else None
-    lg, ids, w = om.route(x, router, bias, cfg.k)
-    used = sorted(set(ids.reshape(-1).tolist()))
-    remap = {e: j for j, e in enumerate(used)}
-    sub_cfg = W.MoeConfig("cpu", t_s, cfg.h, len(used), cfg.i, cfg.k, cfg.shared, cfg.shared_i)
-    wts = W.moe_weights(sub_cfg, seed=1)
-    wts["router"] = router
-    ids_sub = ids.clone().apply_(lambda e: remap[e])
-    rates = []
-    for _ in range(max(1, steps)):
+    # routing of the whole batch (untimed) gives each sampled expert its real token count
+    lg = om.torch_fp32_logits(x, router, bias)
+    ids_all = torch.topk(lg, cfg.k, dim=-1).indices
+    counts = torch.bincount(ids_all.reshape(-1), minlength=cfg.e)
+    order = torch.argsort(counts, descending=True)
+    n_sample = 2 if cfg.e >= 2 else 1
+    sample_experts = [int(order[len(order) // 2 + j]) for j in range(n_sample)]   # median-popularity experts
+    sub_cfg = W.MoeConfig("cpu", cfg.t, cfg.h, cfg.e, cfg.i, cfg.k, cfg.shared, cfg.shared_i)
+    wts = W.moe_weights(sub_cfg, seed=1, experts=sample_experts)
+    rows_of = [(ids_all == e).any(dim=1).nonzero().flatten() for e in sample_experts]
+    t_r = min(cfg.t, 256)
+    xf = x.float()
+
+    def evaluate() -> float:
         t0 = time.perf_counter()
-        lg2, ids2, w2 = om.route(x, router, bias, cfg.k)
-        om.moe_ref(x, wts, cfg.k, route_out=(lg2, ids_sub, w2))
-        rates.append(t_s / (time.perf_counter() - t0))
+        l = xf[:t_r] @ router.T
+        if bias is not None:
+            l = l + bias
+        p = torch.softmax(l, dim=-1)
+        v, _ = torch.topk(p, cfg.k, dim=-1)
+        _ = v / v.sum(dim=-1, keepdim=True)
+        s_router = (time.perf_counter() - t0) / t_r
+        y = torch.zeros((cfg.t, cfg.h), dtype=torch.float32)
+        t0 = time.perf_counter()
+        routes = 0
+        for j, rows in enumerate(rows_of):
+            ye = om._expert(xf[rows], wts["w_gate_up"][j], wts["w_down"][j])
+            y.index_add_(0, rows, ye * 0.125)
+            routes += rows.numel()
+        s_route = (time.perf_counter() - t0) / max(routes, 1)
+        s_shared = 0.0
+        if cfg.shared:
+            t0 = time.perf_counter()
+            om._expert(xf[:t_r], wts["shared_gate_up"][0], wts["shared_down"][0])
+            s_shared = (time.perf_counter() - t0) / t_r
+        return 1.0 / (s_router + cfg.k * s_route + s_shared)
+
+    evaluate()   # warm-up
+    rates, t_end = [], time.perf_counter() + seconds
+    while (steps is None and (time.perf_counter() < t_end or len(rates) < 3)) or (steps is not None and len(rates) < steps):
+        rates.append(evaluate())
     return {"value": round(statistics.median(rates), 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{t_s} of {cfg.t} tokens through the full layer (router over all {cfg.e} experts, the "
-                      f"{len(used)} experts they route to, shared expert), oracle/moe.py, median of {len(rates)}"}
+            "sample": (f"PyTorch fp32 layer on the host: router on {t_r} of {cfg.t} tokens; experts "
+                       f"{sample_experts} (median popularity) with all {sum(int(r.numel()) for r in rows_of)} "
+                       f"routes the full batch sends them (oracle/moe.py _expert); shared expert on {t_r} tokens; "
+                       f"extrapolated to {cfg.t} tokens x top-{cfg.k}; median of {len(rates)} evaluations")}
 
 
 def cpu_baseline_w4a16(workload: str, steps: int = 3) -> dict:
@@ -627,12 +758,14 @@ def bench_w4a16(args, dist: Dist) -> dict | None:
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-projection", action="store_true",
+                    help=f"default workload only: skip the nested {NESTED_PROJ_WORKLOAD} projection record")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -649,6 +782,15 @@ def main() -> int:
             line = bench_proj(args, dist)
         elif args.workload.startswith("moe"):
             line = bench_moe(args, dist)
+            if args.workload == DEFAULT_WORKLOAD and not args.no_projection:
+                # the projection headline of the same run, nested so one line carries both paths
+                torch.cuda.empty_cache()
+                pargs = argparse.Namespace(**{**vars(args), "workload": NESTED_PROJ_WORKLOAD})
+                pline = bench_proj(pargs, dist)
+                if line is not None and pline is not None:
+                    for key in ("n_gpus", "steps", "warmup", "higher_is_better", "scaling", "vs_baseline"):
+                        pline.pop(key, None)
+                    line["projection"] = pline
         elif args.workload.startswith("w4a16"):
             line = bench_w4a16(args, dist)
         else:
@@ -656,6 +798,8 @@ def main() -> int:
         if line is not None and dist.rank == 0:
             if dist.world > 1:
                 line.pop("cpu_baseline", None)
+                if "projection" in line:
+                    line["projection"].pop("cpu_baseline", None)
             print(json.dumps(line), flush=True)
     finally:
         dist.close()

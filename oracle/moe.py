@@ -134,10 +134,13 @@ def torch_fp32_logits(x: torch.Tensor, router: torch.Tensor, bias=None) -> torch
 
 
 def compare(out: torch.Tensor, ref: torch.Tensor) -> dict:
+    """max-abs, relative Frobenius and worst-row (token) relative L2 error of `out` against fp32 `ref`."""
     o, r = out.detach().cpu().float(), ref.detach().cpu().float()
     d = o - r
+    rows = d.norm(dim=-1) / r.norm(dim=-1).clamp_min(1e-30) if r.dim() == 2 else d.abs()
     return {"max_abs": float(d.abs().max()) if d.numel() else 0.0,
             "rel_fro": float(d.norm() / r.norm().clamp_min(1e-30)),
+            "worst_row": float(rows.max()) if rows.numel() else 0.0,
             "nonfinite": int((~torch.isfinite(o)).sum())}
 
 
@@ -153,7 +156,7 @@ def check(out: tuple, ref: dict) -> tuple[bool, str]:
     yc = compare(y, ref["y32"])
     ok = (id_bad == 0 and yc["nonfinite"] == 0 and yc["max_abs"] <= MAX_ABS_TOL and yc["rel_fro"] <= REL_FRO_TOL
           and wc["max_abs"] <= WEIGHT_RTOL * 10)
-    msg = (f"relative L2 error {yc['rel_fro']:.3e} (worst row {yc['rel_fro']:.3e}) max-abs {yc['max_abs']:.3e}; "
+    msg = (f"relative L2 error {yc['rel_fro']:.3e} (worst row {yc['worst_row']:.3e}) max-abs {yc['max_abs']:.3e}; "
            f"routing ids mismatched {id_bad}; weights max-abs {wc['max_abs']:.3e} "
            f"[bound {REL_FRO_TOL}: max-abs <= {MAX_ABS_TOL}, ids exact]")
     return ok, msg

@@ -152,6 +152,23 @@ def test_check_messages_parse_like_kdev():
     assert not bad
 
 
+def test_moe_check_reports_the_worst_token_row():
+    """The MoE check's "(worst row Y)" is the largest per-token relative L2 error, not the overall one: a
+    mistake planted in one token's output row of the oracle's own result shows up there alone."""
+    import re
+    cfg = W.MoeConfig("worst", 12, 64, 4, 128, 2)
+    x = W.moe_input(cfg.t, cfg.h, 5)
+    wts = W.moe_weights(cfg, 5)
+    ref = om.moe_ref(x, wts, cfg.k)
+    y = ref["y32"].clone()
+    y[7] *= 1.015                                      # 1.5 % on one token only
+    _, msg = om.check((y.bfloat16(), ref["w"], ref["ids"]), ref)
+    f = r"([0-9.]+(?:e[+-]?\d+)?)"
+    overall = float(re.search(r"relative L2 error " + f, msg).group(1))
+    worst = float(re.search(r"worst row " + f, msg).group(1))
+    assert 1.2e-2 < worst < 1.8e-2 and worst > 2 * overall, msg
+
+
 def test_zipf_bias_fits_exponent():
     tau, s_fit = W.zipf_tau(128, 1.2)
     assert 0.1 < tau < 2.0

@@ -153,15 +153,19 @@ def test_graph_replay_bitwise_equal_to_eager():
     _assert_close(out, op.proj_ref(x2, w))
 
 
-def test_full_size_sampled_rows():
-    """4096 x 7168 x 7168 (the headline configuration): rows sampled across the whole output are
-    checked against the oracle; row-independence makes the sample representative."""
-    m, k, n = 4096, 7168, 7168
+@pytest.mark.parametrize("m", [1024, 4096, 16384])
+def test_full_size_sampled_rows(m):
+    """K = N = 7168 sweep sizes M = 1024, 4096 (the headline configuration) and 16384: rows sampled
+    across the whole output (tile edges and random rows) are checked against the oracle; row
+    independence makes the sample representative."""
+    k, n = 7168, 7168
     gx = W.proj_input(m, k, 3, device="cuda")
     gw = W.proj_weight(k, n, 3, device="cuda")
     y = proj(gx, gw)
     torch.cuda.synchronize()
-    rows = torch.tensor([0, 1, 127, 128, 1000, 2047, 2048, 3333, 4094, 4095])
+    edges = [0, 1, 127, 128, 255, 256, m // 2 - 1, m // 2, m - 2, m - 1]
+    rand = torch.randperm(m, generator=torch.Generator().manual_seed(m))[:22].tolist()
+    rows = torch.tensor(sorted(set(edges + rand)))
     ref = gx[rows].cpu().float() @ gw.cpu().float().T
     _assert_close(y[rows], ref)
 
