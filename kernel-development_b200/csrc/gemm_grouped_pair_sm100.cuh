@@ -47,8 +47,9 @@ struct GpLayout {
   static_assert(ABOXES == 1 || ABOXES == 2, "one 128-row or two 64-row weight boxes per CTA");
   static constexpr int kABoxRows = 128 / ABOXES;
   static constexpr int kABytes = 128 * kBK * 2;           // this CTA's 128 weight rows
-  static constexpr int kBRegion = 128 * kBK * 2;          // <= 128 token rows of one token group
-  static constexpr int kStageBytes = kABytes + 2 * kBRegion;
+  static constexpr int kBRegion = 128 * kBK * 2;          // this CTA's <= 128 rows of tokens [0, 256)
+  static constexpr int kBRegion2 = (kGpTokens - kGpSlotCols) / 2 * kBK * 2;   // its rows of tokens [256, n)
+  static constexpr int kStageBytes = kABytes + kBRegion + kBRegion2;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   static constexpr int kBarOffset = kEpiOffset + EPI_BYTES;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;

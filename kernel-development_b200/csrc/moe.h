@@ -29,6 +29,13 @@ int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups
                      const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens = 0);
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
                   const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens = 0);
+// Grouped down (CTA-pair path) with the weighted combine fused into its epilogue: rows_out receives the
+// scaled per-slot rows, y[t] the combine of token t's k slot rows (+ yshared[t]); arrivals int32
+// [T, H / 128] must be zero at launch.  H % 128 == 0.
+int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int groups, int I, int H,
+                          const int* offsets, const int* mtile_start, const float* row_scale, const int* perm_slot,
+                          const int* slot_pos, int* arrivals, const void* yshared, void* rows_out, void* y, int T,
+                          int k, cudaStream_t s);
 
 // NVFP4 w4a16 layer of one expert-parallel rank (moe_w4a16.cu).
 size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long long L, long long E, long long k);

@@ -193,6 +193,108 @@ struct ScaleGpEpi {
   }
 };
 
+// down with the weighted combine fused in.  As ScaleGpEpi, each 32-token chunk's scaled bf16 rows go to the
+// per-slot buffer `out`; then every row counts one arrival on (its token, this CTA's 128-feature block).
+// The tile whose arrival completes a token's block (k arrivals: one per routed expert) merges that block:
+// y[t][block] = bf16( sum over j of out[slot_pos[t*k + j]][block] (+ yshared[t][block]) ), fp32 in slot
+// order then the shared row, exactly as moe_combine_kernel.  Determinism does not depend on which tile
+// arrives last.  Ordering: every thread fences its slot-row stores before the group barrier that precedes
+// the arrivals; the merging thread fences after its arrival; the merge reads bypass L1 (__ldcg).
+// The arrival counters ([T, H / 128] int32) are zeroed before the launch.
+struct ScaleCombineGpEpi {
+  static constexpr int kTileElems = 32 * 128;
+  static constexpr int kSmemBytes = 2 * kTileElems * 2 + 2 * 33 * 4;
+  struct Params {
+    __nv_bfloat16* out;           // [rows, ld_out] per-slot rows (scaled)
+    const float* row_scale;       // [rows]
+    int ld_out;                   // = H, a multiple of 128
+    const int* perm_slot;         // [rows]: slot t*k + j held by each permuted row
+    const int* slot_pos;          // [T*k]: permuted row of each slot (< 0: none)
+    int* arrivals;                // [T, ld_out / 128], zero at launch
+    const __nv_bfloat16* yshared; // [T, ld_out] or null
+    __nv_bfloat16* y;             // [T, ld_out]
+    int k;
+  };
+  __device__ static void run(const Params& p, const GpTile& ti, int quad, int lane, int rank, int grp,
+                             uint32_t taddr, int tok0, int ncols, uint8_t* smem, uint32_t& seq) {
+    const int r = quad * 32 + lane;
+    const int etid = r;
+    const int fbase = ti.f0 + rank * 128;
+    const int fb = fbase >> 7;
+    const int nfb = p.ld_out >> 7;
+    const int row_base = ti.b_row + tok0;
+#pragma unroll 1
+    for (int c0 = 32 * grp; c0 < ncols; c0 += 64, ++seq) {
+      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + (seq & 1u) * kTileElems;
+      int* list = reinterpret_cast<int*>(smem + 2 * kTileElems * 2) + (seq & 1u) * 33;   // [0] count, tokens
+      const int n = min(32, ncols - c0);
+      const float my_scale = lane < n ? __ldg(p.row_scale + row_base + c0 + lane) : 1.0f;
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(taddr + c0, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float sc = __shfl_sync(0xffffffffu, my_scale, i);
+        tile[i * 128 + r] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
+      }
+      if (etid == 0) list[0] = 0;
+      epi_bar_sync(grp);
+      epi_copy_out<128>(tile, n, p.out, p.ld_out, row_base + c0, fbase, p.ld_out, true, etid);
+      __threadfence();
+      epi_bar_sync(grp);
+      if (etid < n) {
+        const int tok = __ldg(p.perm_slot + row_base + c0 + etid) / p.k;
+        const int old = atomicAdd(p.arrivals + static_cast<long long>(tok) * nfb + fb, 1);
+        if (old == p.k - 1) {
+          __threadfence();
+          list[1 + atomicAdd(list, 1)] = tok;
+        }
+      }
+      epi_bar_sync(grp);
+      const int nm = list[0];
+      const int c8 = (etid & 15) * 8;
+#pragma unroll 1
+      for (int m = etid >> 4; m < nm; m += 8) {
+        const int tok = list[1 + m];
+        float acc[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 1
+        for (int j = 0; j < p.k; ++j) {
+          const int pos = __ldg(p.slot_pos + static_cast<long long>(tok) * p.k + j);
+          if (pos < 0) continue;
+          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.out + static_cast<long long>(pos) * p.ld_out +
+                                                                fbase + c8));
+          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(b[q]);
+            acc[2 * q] += f.x;
+            acc[2 * q + 1] += f.y;
+          }
+        }
+        if (p.yshared) {
+          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.yshared + static_cast<long long>(tok) * p.ld_out +
+                                                                fbase + c8));
+          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(b[q]);
+            acc[2 * q] += f.x;
+            acc[2 * q + 1] += f.y;
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(p.y + static_cast<long long>(tok) * p.ld_out + fbase + c8) = o;
+      }
+    }
+  }
+};
+
 // ---------------------------------------------------------------------------------------------------
 // Weight-streaming path (every group holds <= 64 tokens, as in decode): one CTA per tile of 256 weight rows
 // (two 128-row parts) x the group's tokens on the single-CTA swapped-operand core (gemm_swap_sm100.cuh).
@@ -458,6 +560,40 @@ int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int
   ep.n_total = H;
   ep.vec_ok = aligned16(out) && H % 8 == 0;
   return launch_grouped_pair<ScaleGpEpi, 1>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep, s);
+}
+
+int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int groups, int I, int H,
+                          const int* offsets, const int* mtile_start, const float* row_scale, const int* perm_slot,
+                          const int* slot_pos, int* arrivals, const void* yshared, void* rows_out, void* y, int T,
+                          int k, cudaStream_t s) {
+  if (a_rows <= 0) return KDB_OK;
+  if (H % 128 != 0 || !aligned16(rows_out) || !aligned16(y) || (yshared && !aligned16(yshared)))
+    return KDB_ERR_UNSUPPORTED;
+  GroupedPairSched::Params sp;
+  sp.offsets = offsets;
+  sp.tile_start = mtile_start;
+  sp.groups = groups;
+  sp.rows = a_rows;
+  sp.f_tiles = (H + 255) / 256;   // 256 output features per pair tile
+  sp.nkb = (I + kBK - 1) / kBK;
+  sp.a_rows_per_group = H;
+  sp.a_f_stride = 256;
+  sp.a_box_stride = 0;
+  sp.a_rank_stride = 128;
+  sp.f_step = 256;
+  ScaleCombineGpEpi::Params ep;
+  ep.out = static_cast<__nv_bfloat16*>(rows_out);
+  ep.row_scale = row_scale;
+  ep.ld_out = H;
+  ep.perm_slot = perm_slot;
+  ep.slot_pos = slot_pos;
+  ep.arrivals = arrivals;
+  ep.yshared = static_cast<const __nv_bfloat16*>(yshared);
+  ep.y = static_cast<__nv_bfloat16*>(y);
+  ep.k = k;
+  (void)T;
+  return launch_grouped_pair<ScaleCombineGpEpi, 1>(a, a_rows, w_down, static_cast<uint64_t>(groups) * H, I, sp, ep,
+                                                   s);
 }
 
 }  // namespace kdb

@@ -298,3 +298,31 @@ def test_sm_budget_leaves_results_unchanged():
     torch.cuda.synchronize()
     assert L.lib().kdb_sm_budget() == prev
     assert torch.equal(y0, y1) and torch.equal(w0, w1) and torch.equal(i0, i1)
+
+
+@pytest.mark.parametrize("cfg", [
+    W.MoeConfig("fused_plain", 300, 512, 16, 256, 4),
+    W.MoeConfig("fused_shared", 700, 1024, 32, 256, 8, shared=1, shared_i=256),
+    W.MoeConfig("fused_skew", 2048, 512, 64, 128, 4, zipf_s=1.2),
+])
+def test_fused_combine_equals_stage_composition(cfg):
+    """The layer's down GEMM merges each token's slot rows in its epilogue (the last of the token's k tiles
+    to arrive sums them in slot order).  Its output must equal, bitwise, the separate stages: grouped down
+    into per-slot rows, then the combine kernel."""
+    x = W.moe_input(cfg.t, cfg.h, 21, device="cuda")
+    state = M.prepare(W.moe_weights(cfg, 21, device="cuda"), cfg.k)
+    y, w, ids = M.forward(x, state)
+    p = M.plan(ids, w, cfg.e)
+    mt = torch.zeros(cfg.e + 1, dtype=torch.int32, device="cuda")
+    mt[1:] = torch.cumsum((p["counts"] + 511) // 512, 0)
+    xp = M.gather_rows(x, p["perm_slot"], div=cfg.k)
+    h = M.expert_gate_up(xp, state["w_gate_up_packed"], p["offsets"], mt)
+    perm_w = w.reshape(-1)[p["perm_slot"].long()].contiguous()
+    rows = M.expert_down(h, state["w_down"], p["offsets"], mt, perm_w)
+    ys = None
+    if cfg.shared:
+        hs = M.expert_gate_up(x, state["shared_gate_up_packed"])
+        ys = M.expert_down(hs, state["shared_down"])
+    y2 = M.combine(rows, p["slot_pos"], cfg.t, cfg.k, shared_rows=ys)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
