@@ -203,7 +203,9 @@ struct ScaleGpEpi {
 // The arrival counters ([T, H / 128] int32) are zeroed before the launch.
 struct ScaleCombineGpEpi {
   static constexpr int kTileElems = 32 * 128;
-  static constexpr int kSmemBytes = 2 * kTileElems * 2 + 2 * 33 * 4;
+  static constexpr int kListInts = 36;   // merge list of one chunk: [0] count, then up to 32 tokens (16-B multiple)
+  static constexpr int kSmemBytes = 2 * kTileElems * 2 + 2 * kListInts * 4;
+  static_assert(kSmemBytes % 16 == 0, "the second epilogue group's tile must stay 16-byte aligned");
   struct Params {
     __nv_bfloat16* out;           // [rows, ld_out] per-slot rows (scaled)
     const float* row_scale;       // [rows]
@@ -223,10 +225,11 @@ struct ScaleCombineGpEpi {
     const int fb = fbase >> 7;
     const int nfb = p.ld_out >> 7;
     const int row_base = ti.b_row + tok0;
+    if (fbase >= p.ld_out) return;   // CTA 1 of a last pair tile past H (H % 256 == 128): no features
 #pragma unroll 1
     for (int c0 = 32 * grp; c0 < ncols; c0 += 64, ++seq) {
       __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + (seq & 1u) * kTileElems;
-      int* list = reinterpret_cast<int*>(smem + 2 * kTileElems * 2) + (seq & 1u) * 33;   // [0] count, tokens
+      int* list = reinterpret_cast<int*>(smem + 2 * kTileElems * 2) + (seq & 1u) * kListInts;
       const int n = min(32, ncols - c0);
       const float my_scale = lane < n ? __ldg(p.row_scale + row_base + c0 + lane) : 1.0f;
       uint32_t v[32];

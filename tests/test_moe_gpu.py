@@ -304,6 +304,7 @@ def test_sm_budget_leaves_results_unchanged():
     W.MoeConfig("fused_plain", 300, 512, 16, 256, 4),
     W.MoeConfig("fused_shared", 700, 1024, 32, 256, 8, shared=1, shared_i=256),
     W.MoeConfig("fused_skew", 2048, 512, 64, 128, 4, zipf_s=1.2),
+    W.MoeConfig("fused_h384", 200, 384, 8, 128, 2, shared=1, shared_i=128),   # last pair tile half past H
 ])
 def test_fused_combine_equals_stage_composition(cfg):
     """The layer's down GEMM merges each token's slot rows in its epilogue (the last of the token's k tiles
