@@ -254,10 +254,13 @@ __global__ void __launch_bounds__(kGpThreads, 1)
     int next = 0;
     uint32_t chunk_seq = 0;
     bool live = true;
+    Epi::init_smem(gsmem, quad * 32 + static_cast<int>(lane));
+    epi_bar_sync(grp);
     for (int t = pair; live && t < ntiles; t += npairs) {
       const GpTile ti = sched.tile(t);
       const GpSplit sp2(ti.n_valid);
       const int nslots = sp2.m2 > 0 ? 2 : 1;
+      int done_tok0[2] = {0, 0}, done_ncols[2] = {0, 0};
       for (int k = 0; k < nslots; ++k) {
         const int s = k == 0 ? next : next ^ 1;
         const bool ok = mbar_wait(&tfull[s], (ph >> s) & 1u, abort_flag, kSiteEpiTmemFull);
@@ -274,9 +277,16 @@ __global__ void __launch_bounds__(kGpThreads, 1)
         tc_fence_before();
         if (leader) mbar_arrive(&tempty[s]);
         else mbar_arrive_cluster(tempty_lead + 8u * s);
+        done_tok0[k] = tok0;
+        done_ncols[k] = ncols;
         ph ^= 1u << s;
       }
       if (nslots == 1) next ^= 1;
+      // work that needs no accumulator, once every slot of the tile is back with the MMA
+      if (live)
+        for (int k = 0; k < nslots; ++k)
+          Epi::after_release(ep, ti, quad, static_cast<int>(lane), static_cast<int>(rank), grp, gsmem, done_tok0[k],
+                             done_ncols[k]);
     }
   }
 

@@ -112,6 +112,9 @@ __device__ __forceinline__ void epi_copy_out(const __nv_bfloat16* tile, int rows
 // [32 tokens][64 features] tile, and the group stores the tile's rows with 16-byte vectors.
 struct SwigluGpEpi {
   static constexpr int kXFloats = 64 * 17;
+  struct Params;
+  __device__ static void init_smem(uint8_t*, int) {}
+  __device__ static void after_release(const Params&, const GpTile&, int, int, int, int, uint8_t*, int, int) {}
   static constexpr int kSmemBytes = 2 * kXFloats * 4 + 32 * 64 * 2;
   struct Params {
     __nv_bfloat16* out;   // [rows, ld_out] intermediate
@@ -161,6 +164,9 @@ struct SwigluGpEpi {
 // tile (double-buffered) and stores its rows with 16-byte vectors.
 struct ScaleGpEpi {
   static constexpr int kTileElems = 32 * 128;
+  struct Params;
+  __device__ static void init_smem(uint8_t*, int) {}
+  __device__ static void after_release(const Params&, const GpTile&, int, int, int, int, uint8_t*, int, int) {}
   static constexpr int kSmemBytes = 2 * kTileElems * 2;
   struct Params {
     __nv_bfloat16* out;       // [rows, ld_out]
@@ -194,17 +200,20 @@ struct ScaleGpEpi {
 };
 
 // down with the weighted combine fused in.  As ScaleGpEpi, each 32-token chunk's scaled bf16 rows go to the
-// per-slot buffer `out`; then every row counts one arrival on (its token, this CTA's 128-feature block).
-// The tile whose arrival completes a token's block (k arrivals: one per routed expert) merges that block:
+// per-slot buffer `out`.  Once the accumulator slot is handed back to the MMA (after_release), every row of
+// the slot counts one arrival on (its token, this CTA's 128-feature block), and the tile whose arrival
+// completes a token's block (k arrivals: one per routed expert) merges that block:
 // y[t][block] = bf16( sum over j of out[slot_pos[t*k + j]][block] (+ yshared[t][block]) ), fp32 in slot
-// order then the shared row, exactly as moe_combine_kernel.  Determinism does not depend on which tile
-// arrives last.  Ordering: every thread fences its slot-row stores before the group barrier that precedes
-// the arrivals; the merging thread fences after its arrival; the merge reads bypass L1 (__ldcg).
-// The arrival counters ([T, H / 128] int32) are zeroed before the launch.
+// order then the shared row, exactly as moe_combine_kernel, so the result does not depend on which tile
+// arrives last.  Running the arrivals and merges after the release overlaps their memory latency (the
+// merge reads other tiles' rows, mostly from HBM) with the next tile's MMAs.  Ordering (the release /
+// acquire pattern of a split-K semaphore): each thread fences its slot-row stores, the group meets at a
+// barrier, then the arrivals; the thread completing a block fences before publishing it to its group, and
+// merge reads bypass L1.  The arrival counters ([T, H / 128] int32) are zeroed before the launch.
 struct ScaleCombineGpEpi {
   static constexpr int kTileElems = 32 * 128;
-  static constexpr int kListInts = 36;   // merge list of one chunk: [0] count, then up to 32 tokens (16-B multiple)
-  static constexpr int kSmemBytes = 2 * kTileElems * 2 + 2 * kListInts * 4;
+  static constexpr int kListInts = 132;   // [0] count, then the tokens to merge (<= 128 rows per group and slot)
+  static constexpr int kSmemBytes = kTileElems * 2 + kListInts * 4;
   static_assert(kSmemBytes % 16 == 0, "the second epilogue group's tile must stay 16-byte aligned");
   struct Params {
     __nv_bfloat16* out;           // [rows, ld_out] per-slot rows (scaled)
@@ -217,19 +226,20 @@ struct ScaleCombineGpEpi {
     __nv_bfloat16* y;             // [T, ld_out]
     int k;
   };
+  __device__ static int* list_of(uint8_t* smem) { return reinterpret_cast<int*>(smem + kTileElems * 2); }
+  __device__ static void init_smem(uint8_t* smem, int etid) {
+    if (etid == 0) list_of(smem)[0] = 0;
+  }
+
   __device__ static void run(const Params& p, const GpTile& ti, int quad, int lane, int rank, int grp,
-                             uint32_t taddr, int tok0, int ncols, uint8_t* smem, uint32_t& seq) {
+                             uint32_t taddr, int tok0, int ncols, uint8_t* smem, uint32_t&) {
     const int r = quad * 32 + lane;
-    const int etid = r;
     const int fbase = ti.f0 + rank * 128;
-    const int fb = fbase >> 7;
-    const int nfb = p.ld_out >> 7;
-    const int row_base = ti.b_row + tok0;
     if (fbase >= p.ld_out) return;   // CTA 1 of a last pair tile past H (H % 256 == 128): no features
+    const int row_base = ti.b_row + tok0;
+    __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem);
 #pragma unroll 1
-    for (int c0 = 32 * grp; c0 < ncols; c0 += 64, ++seq) {
-      __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + (seq & 1u) * kTileElems;
-      int* list = reinterpret_cast<int*>(smem + 2 * kTileElems * 2) + (seq & 1u) * kListInts;
+    for (int c0 = 32 * grp; c0 < ncols; c0 += 64) {
       const int n = min(32, ncols - c0);
       const float my_scale = lane < n ? __ldg(p.row_scale + row_base + c0 + lane) : 1.0f;
       uint32_t v[32];
@@ -240,61 +250,90 @@ struct ScaleCombineGpEpi {
         const float sc = __shfl_sync(0xffffffffu, my_scale, i);
         tile[i * 128 + r] = __float2bfloat16_rn(__uint_as_float(v[i]) * sc);
       }
-      if (etid == 0) list[0] = 0;
       epi_bar_sync(grp);
-      epi_copy_out<128>(tile, n, p.out, p.ld_out, row_base + c0, fbase, p.ld_out, true, etid);
-      __threadfence();
-      epi_bar_sync(grp);
-      if (etid < n) {
-        const int tok = __ldg(p.perm_slot + row_base + c0 + etid) / p.k;
+      epi_copy_out<128>(tile, n, p.out, p.ld_out, row_base + c0, fbase, p.ld_out, true, r);
+      epi_bar_sync(grp);   // the tile buffer is free again
+    }
+  }
+
+  // After the accumulator slot is released: count this group's rows of the slot, merge the blocks they
+  // complete, then clear the list.
+  __device__ static void after_release(const Params& p, const GpTile& ti, int quad, int lane, int rank, int grp,
+                                       uint8_t* smem, int tok0, int ncols) {
+    const int etid = quad * 32 + lane;
+    const int fbase = ti.f0 + rank * 128;
+    if (fbase >= p.ld_out) return;
+    const int nfb = p.ld_out >> 7;
+    const int fb = fbase >> 7;
+    int* list = list_of(smem);
+    __threadfence();         // this thread's slot-row stores, before any arrival of the group
+    epi_bar_sync(grp);
+    {
+      // the group's rows: chunks c0 = 32 * grp + 64 * i (i < 4), thread etid takes row (etid & 31) of chunk etid / 32
+      const int c = 32 * grp + 64 * (etid >> 5) + (etid & 31);
+      if (c < ncols) {
+        const int tok = __ldg(p.perm_slot + ti.b_row + tok0 + c) / p.k;
         const int old = atomicAdd(p.arrivals + static_cast<long long>(tok) * nfb + fb, 1);
         if (old == p.k - 1) {
-          __threadfence();
+          __threadfence();   // acquire: the other tiles' rows of this block are visible from here on
           list[1 + atomicAdd(list, 1)] = tok;
         }
       }
-      epi_bar_sync(grp);
-      const int nm = list[0];
-      const int c8 = (etid & 15) * 8;
-#pragma unroll 1
-      for (int m = etid >> 4; m < nm; m += 8) {
-        const int tok = list[1 + m];
-        float acc[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-#pragma unroll 1
-        for (int j = 0; j < p.k; ++j) {
-          const int pos = __ldg(p.slot_pos + static_cast<long long>(tok) * p.k + j);
-          if (pos < 0) continue;
-          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.out + static_cast<long long>(pos) * p.ld_out +
-                                                                fbase + c8));
-          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(b[q]);
-            acc[2 * q] += f.x;
-            acc[2 * q + 1] += f.y;
-          }
-        }
-        if (p.yshared) {
-          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.yshared + static_cast<long long>(tok) * p.ld_out +
-                                                                fbase + c8));
-          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(b[q]);
-            acc[2 * q] += f.x;
-            acc[2 * q + 1] += f.y;
-          }
-        }
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(p.y + static_cast<long long>(tok) * p.ld_out + fbase + c8) = o;
-      }
     }
+    epi_bar_sync(grp);
+    const int nm = list[0];
+    const int c8 = (etid & 15) * 8;
+#pragma unroll 1
+    for (int m = etid >> 4; m < nm; m += 8) {
+      const int tok = list[1 + m];
+      const int* sp = p.slot_pos + static_cast<long long>(tok) * p.k;
+      float acc[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 1
+      for (int j0 = 0; j0 < p.k; j0 += 8) {
+        const int nj = min(8, p.k - j0);
+        int pos[8];
+        uint4 u[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pos[j] = j < nj ? __ldg(sp + j0 + j) : -1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)   // all loads of the group in flight before any add
+          u[j] = pos[j] >= 0 ? __ldcg(reinterpret_cast<const uint4*>(p.out + static_cast<long long>(pos[j]) * p.ld_out +
+                                                                     fbase + c8))
+                             : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (pos[j] < 0) continue;
+          const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(b[q]);
+            acc[2 * q] += f.x;
+            acc[2 * q + 1] += f.y;
+          }
+        }
+      }
+      if (p.yshared) {
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.yshared + static_cast<long long>(tok) * p.ld_out +
+                                                              fbase + c8));
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(b[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(p.y + static_cast<long long>(tok) * p.ld_out + fbase + c8) = o;
+    }
+    epi_bar_sync(grp);   // every thread has read the list
+    if (etid == 0) list[0] = 0;
   }
 };
 
