@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define KDB200_ABI_VERSION 1
+#define KDB200_ABI_VERSION 2   /* 2: kdb_moe_w4a16_forward takes pw1 */
 
 /* Tokens of one grouped expert-GEMM tile; the routing plan's mtile_start counts ceil(count / this). */
 #define KDB_MOE_TOKEN_TILE 512
@@ -283,8 +283,9 @@ int kdb_moe_forward(const void* x, const float* router_w, const float* router_bi
  * src/kdev/adapters/okc_problems/muse_moe_w4a16.toml; engines okc-challenge/engines/sc_h.cu:189-467).
  * x bf16 [t, h]; topk_ids int32 / topk_w fp32 [t, k] over e_total experts, of which ids 0..local-1 live
  * here (routes to other ids are skipped); y bf16 [t, h] = sum over local routes j of
- * topk_w * rms_norm(y_j), y_j = (bf16(silu(x.W1^T gs13) * (x.W3^T gs13)) . W2^T) gs2, rms_norm(v) =
- * v * rsqrt(mean(v^2) + 1e-8).  Weights NVFP4 (E2M1 codes two per byte, low nibble first; E4M3 scale per
+ * y_j * topk_w * rsqrt(mean(y_j^2) + 1e-8), y_j = (bf16(silu(x.W1^T gs13) * (x.W3^T gs13)) . W2^T) gs2 pw1
+ * kept in fp32, pw1 fp32 [h] the per-feature output weight of the reference engines' Params.pw1
+ * (okc-challenge/engines/sc_h.cu:51, 346; NULL = 1).  Weights NVFP4 (E2M1 codes two per byte, low nibble first; E4M3 scale per
  * 16 elements; fp32 global scale per expert tensor), as 9216-byte blocks, one per (expert, weight tile,
  * 64-element k chunk), tiles and chunks in order: [part 0 codes 128 x 32 B | part 1 codes | part 0 scales
  * 128 x 4 B | part 1 scales].  w13_blocks [local][i/128][h/64]: tile f's part 0 = gate rows 128f.., part 1
@@ -294,9 +295,9 @@ int kdb_moe_forward(const void* x, const float* router_w, const float* router_bi
  */
 size_t kdb_moe_w4a16_workspace_bytes(int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k);
 int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_blocks,
-                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, void* y, int64_t t,
-                          int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k, void* workspace,
-                          size_t workspace_bytes, void* stream);
+                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, const float* pw1,
+                          void* y, int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

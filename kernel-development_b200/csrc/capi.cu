@@ -264,11 +264,11 @@ size_t kdb_moe_w4a16_workspace_bytes(int64_t t, int64_t h, int64_t i, int64_t lo
 }
 
 int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* topk_w, const void* w13_blocks,
-                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, void* y, int64_t t,
-                          int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k, void* workspace,
-                          size_t workspace_bytes, void* stream) {
-  return kdb::moe_w4a16_forward(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, y, t, h, i, local,
-                                e_total, k, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                          const float* w13_gscale, const void* w2_blocks, const float* w2_gscale, const float* pw1,
+                          void* y, int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  return kdb::moe_w4a16_forward(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1, y, t, h, i,
+                                local, e_total, k, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -40,7 +40,7 @@ int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int gro
 // NVFP4 w4a16 layer of one expert-parallel rank (moe_w4a16.cu).
 size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long long L, long long E, long long k);
 int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_blocks, const float* w13_gscale,
-                      const void* w2_blocks, const float* w2_gscale,
+                      const void* w2_blocks, const float* w2_gscale, const float* pw1,
                       void* y, long long T, long long H, long long I, long long L, long long E, long long k,
                       void* workspace, size_t workspace_bytes, cudaStream_t s);
 

@@ -7,8 +7,8 @@
 //   tile prefix  ceil(count / 64) per local expert (w4_prefix_kernel)
 //   gather     local token rows, converted to f16 (exact for activations inside f16's range)
 //   gate_up    h = bf16(silu(x.W1^T * gs13) * (x.W3^T * gs13)), stored as f16 (gemm_fp4w_sm100.cuh)
-//   down       y = bf16((h.W2^T) * gs2)
-//   combine    out[t] = sum over t's local routes j (in route order) of tw[t, j] * y * rsqrt(mean(y^2) + 1e-8)
+//   down       y = (h.W2^T) * gs2 * pw1, kept in fp32 (pw1: the per-feature output weight, sc_h.cu:51, 346)
+//   combine    out[t] = sum over t's local routes j (in route order) of y * tw[t, j] * rsqrt(mean(y^2) + 1e-8)
 //
 // Weights arrive already tiled by prepare() (a lossless reordering of NVFP4): for each expert, weight tile f
 // (gate_up: the gate rows of 128 features and their up rows; down: 256 output features as two 128-row
@@ -92,28 +92,31 @@ struct SwigluFp4Epi {
 };
 
 // down: accumulator lane r of part a = output feature f0 + 128 a + r; columns = the tile's tokens; times gs2
-// of the expert -> bf16.
+// of the expert and pw1 of the feature, kept in fp32 (the engines' y, sc_h.cu:346; x3_h.cu:529-530).
 struct ScaleFp4Epi {
   struct Params {
-    __nv_bfloat16* out;     // [rows, ld_out]
+    float* out;             // [rows, ld_out]
     const float* gscale;    // [local]: gs2 per expert
+    const float* pw1;       // [ld_out] per-feature output weight, or null (1)
     int ld_out;
   };
   __device__ static void run(const Params& p, const Fp4Tile& ti, int r, uint32_t taddr) {
     const float gs = __ldg(p.gscale + ti.group);
 #pragma unroll 1
     for (int a = 0; a < 2; ++a) {
-      __nv_bfloat16* col = p.out + ti.f0 + a * 128 + r;
+      const int feat = ti.f0 + a * 128 + r;
+      const float mul = p.pw1 ? gs * __ldg(p.pw1 + feat) : gs;
+      float* col = p.out + feat;
 #pragma unroll 1
       for (int c0 = 0; c0 < ti.n_valid; c0 += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(taddr + a * kFp4NB + c0, v);
         tmem_ld_wait();
         const int n = min(32, ti.n_valid - c0);
-        __nv_bfloat16* dst = col + static_cast<long long>(ti.b_row + c0) * p.ld_out;
+        float* dst = col + static_cast<long long>(ti.b_row + c0) * p.ld_out;
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (i < n) dst[static_cast<long long>(i) * p.ld_out] = __float2bfloat16_rn(__uint_as_float(v[i]) * gs);
+          if (i < n) dst[static_cast<long long>(i) * p.ld_out] = __uint_as_float(v[i]) * mul;
       }
     }
   }
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(256)
 constexpr int kW4CombineMax = 32;
 
 __global__ void __launch_bounds__(256)
-    w4_combine_kernel(const __nv_bfloat16* __restrict__ rows, const int* __restrict__ ids, const float* __restrict__ tw,
+    w4_combine_kernel(const float* __restrict__ rows, const int* __restrict__ ids, const float* __restrict__ tw,
                       const int* __restrict__ slot_pos, int local, __nv_bfloat16* __restrict__ out, int H, int k) {
   __shared__ float red[8];
   const int t = blockIdx.x, tid = threadIdx.x;
@@ -174,13 +177,13 @@ __global__ void __launch_bounds__(256)
     const int e = __ldg(ids + static_cast<long long>(t) * k + j);
     if (e < 0 || e >= local) continue;   // a route to another rank's expert
     const int r = __ldg(slot_pos + static_cast<long long>(t) * k + j);
-    const __nv_bfloat16* y = rows + static_cast<long long>(r) * H;
+    const float* y = rows + static_cast<long long>(r) * H;
     float v[kW4CombineMax];
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kW4CombineMax; ++i) {
       const int h = tid + 256 * i;
-      v[i] = (i < per && h < H) ? __bfloat162float(y[h]) : 0.f;
+      v[i] = (i < per && h < H) ? y[h] : 0.f;
       ss = fmaf(v[i], v[i], ss);
     }
 #pragma unroll
@@ -191,9 +194,10 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int w = 0; w < 8; ++w) tot += red[w];
     __syncthreads();
-    const float scale = __ldg(tw + static_cast<long long>(t) * k + j) * rsqrtf(tot / static_cast<float>(H) + 1e-8f);
+    const float wj = __ldg(tw + static_cast<long long>(t) * k + j);
+    const float rr = rsqrtf(tot / static_cast<float>(H) + 1e-8f);
 #pragma unroll
-    for (int i = 0; i < kW4CombineMax; ++i) acc[i] = fmaf(scale, v[i], acc[i]);
+    for (int i = 0; i < kW4CombineMax; ++i) acc[i] = fmaf(v[i] * wj, rr, acc[i]);   // y * tw * rsqrt, as x3_h.cu:654
   }
 #pragma unroll
   for (int i = 0; i < kW4CombineMax; ++i) {
@@ -225,7 +229,7 @@ static W4Carve w4_carve(long long T, long long H, long long I, long long L, long
   c.tile_start = o;    o += up(sizeof(int) * (L + 1));
   c.xf16 = o;          o += up(2 * R * H);
   c.hbuf = o;          o += up(2 * R * I);
-  c.yrows = o;         o += up(2 * R * H);
+  c.yrows = o;         o += up(4 * R * H);   // fp32 y rows
   c.total = o;
   return c;
 }
@@ -266,7 +270,7 @@ static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* block
 }
 
 int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void* w13_blocks, const float* w13_gscale,
-                      const void* w2_blocks, const float* w2_gscale,
+                      const void* w2_blocks, const float* w2_gscale, const float* pw1,
                       void* y, long long T, long long H, long long I, long long L, long long E, long long k,
                       void* workspace, size_t workspace_bytes, cudaStream_t s) {
   int rc = w4_check(T, H, I, L, E, k);
@@ -319,13 +323,14 @@ int moe_w4a16_forward(const void* x, const int* ids, const float* tw, const void
     sp.nkb = Ii / kBK;
     sp.f_step = 256;
     ScaleFp4Epi::Params ep;
-    ep.out = reinterpret_cast<__nv_bfloat16*>(ws + c.yrows);
+    ep.out = reinterpret_cast<float*>(ws + c.yrows);
     ep.gscale = w2_gscale;
+    ep.pw1 = pw1;
     ep.ld_out = Hi;
     rc = launch_fp4w<ScaleFp4Epi>(ws + c.hbuf, R, Ii, static_cast<const uint8_t*>(w2_blocks), sp, ep, s);
     if (rc) return rc;
   }
-  w4_combine_kernel<<<Ti, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(ws + c.yrows), ids, tw, Ip(c.slot_pos),
+  w4_combine_kernel<<<Ti, 256, 0, s>>>(reinterpret_cast<const float*>(ws + c.yrows), ids, tw, Ip(c.slot_pos),
                                        Li, static_cast<__nv_bfloat16*>(y), Hi, ki);
   return cuda_status(cudaGetLastError());
 }

@@ -38,7 +38,7 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_proj_tile_shape": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(ctypes.c_int32)]),
     "kdb_set_sm_budget": (_c_int, [ctypes.c_int32]),
     "kdb_moe_w4a16_workspace_bytes": (_c_size, [_c_i64] * 6),
-    "kdb_moe_w4a16_forward": (_c_int, [_c_vp] * 8 + [_c_i64] * 6 + [_c_vp, _c_size, _c_vp]),
+    "kdb_moe_w4a16_forward": (_c_int, [_c_vp] * 9 + [_c_i64] * 6 + [_c_vp, _c_size, _c_vp]),
     "kdb_sm_budget": (_c_int, []),
     "kdb_proj_split_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "kdb_proj_f32w_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),

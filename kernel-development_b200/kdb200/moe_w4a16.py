@@ -42,12 +42,15 @@ def prepare(weights: dict, device: str | torch.device = "cuda") -> dict:
     w13 = _blocks(weights["w13"].to(device), weights["w13_scale"].to(device), gate_up=True)
     w2 = _blocks(weights["w2"].to(device), weights["w2_scale"].to(device), gate_up=False)
     L, rows13, _ = weights["w13"].shape
+    h = weights["w2"].shape[1]
+    pw1 = weights.get("pw1")
+    pw1 = torch.ones(h, dtype=torch.float32) if pw1 is None else pw1
     return {"w13_blocks": w13, "w13_gscale": weights["w13_gscale"].to(device).float().contiguous(),
             "w2_blocks": w2, "w2_gscale": weights["w2_gscale"].to(device).float().contiguous(),
-            "local": L, "i": rows13 // 2, "h": weights["w2"].shape[1]}
+            "pw1": pw1.to(device).float().contiguous(), "local": L, "i": rows13 // 2, "h": h}
 
 
-def _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_total):
+def _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1, e_total):
     """Shapes, dtypes and devices of kdb200::moe_w4a16's arguments; returns (T, H, I, local, k).  The kernel
     receives raw pointers, so every tensor must be contiguous and on x's CUDA device."""
     if x.dtype != torch.bfloat16 or x.dim() != 2:
@@ -68,9 +71,11 @@ def _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_
         raise ValueError("NVFP4 blocks do not match x's hidden size (use moe_w4a16.prepare)")
     if tuple(w13_gscale.shape) != (local,) or tuple(w2_gscale.shape) != (local,):
         raise ValueError(f"global scales must be [{local}]")
+    if pw1.dtype != torch.float32 or tuple(pw1.shape) != (h,):
+        raise ValueError(f"pw1 must be fp32 [{h}]")
     if not local <= e_total:
         raise ValueError(f"e_total ({e_total}) must be at least the number of local experts ({local})")
-    tensors = (x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale)
+    tensors = (x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1)
     if not x.is_cuda or any(a.device != x.device for a in tensors):
         raise ValueError("all tensors must be on one CUDA device (there is no CPU path)")
     if not all(a.is_contiguous() for a in tensors):
@@ -80,27 +85,29 @@ def _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_
 
 @torch.library.custom_op("kdb200::moe_w4a16", mutates_args=())
 def moe_w4a16(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, w13_blocks: torch.Tensor,
-              w13_gscale: torch.Tensor, w2_blocks: torch.Tensor, w2_gscale: torch.Tensor, e_total: int) -> torch.Tensor:
-    """y bf16 [T, H]: the rank's local routes (ids < local) through NVFP4 experts, RMS-normalised and
-    weighted (kdb_moe_w4a16_forward)."""
-    t, h, i, local, k = _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_total)
+              w13_gscale: torch.Tensor, w2_blocks: torch.Tensor, w2_gscale: torch.Tensor, pw1: torch.Tensor,
+              e_total: int) -> torch.Tensor:
+    """y bf16 [T, H]: the rank's local routes (ids < local) through NVFP4 experts, times the per-feature
+    weight pw1, RMS-normalised and weighted (kdb_moe_w4a16_forward)."""
+    t, h, i, local, k = _check(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1, e_total)
     y = torch.empty((t, h), dtype=torch.bfloat16, device=x.device)
     nbytes = int(_lib.lib().kdb_moe_w4a16_workspace_bytes(t, h, i, local, e_total, k))
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         rc = _lib.lib().kdb_moe_w4a16_forward(
             x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), w13_blocks.data_ptr(),
-            w13_gscale.data_ptr(), w2_blocks.data_ptr(), w2_gscale.data_ptr(), y.data_ptr(), t, h, i, local, e_total,
+            w13_gscale.data_ptr(), w2_blocks.data_ptr(), w2_gscale.data_ptr(), pw1.data_ptr(), y.data_ptr(), t, h, i,
+            local, e_total,
             k, ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream)
     _lib.check("kdb_moe_w4a16_forward", rc)
     return y
 
 
 @moe_w4a16.register_fake
-def _moe_w4a16_fake(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, e_total):
+def _moe_w4a16_fake(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1, e_total):
     return x.new_empty(x.shape)
 
 
 def forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, state: dict, e_total: int) -> torch.Tensor:
     return moe_w4a16(x, topk_ids.contiguous(), topk_w.contiguous(), state["w13_blocks"], state["w13_gscale"],
-                     state["w2_blocks"], state["w2_gscale"], int(e_total))
+                     state["w2_blocks"], state["w2_gscale"], state["pw1"], int(e_total))

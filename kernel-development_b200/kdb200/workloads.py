@@ -282,7 +282,8 @@ def nvfp4_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 
 def w4a16_weights(cfg: W4A16Config, seed: int = 0, experts: list[int] | None = None) -> dict:
     """NVFP4 weights of the local experts (CPU): w13 [L, 2I, H/2] uint8 (rows 0..I-1 gate, I..2I-1 up),
-    w13_scale [L, 2I, H/16] e4m3, w13_gscale [L] fp32, w2 [L, H, I/2], w2_scale [L, H, I/16], w2_gscale [L].
+    w13_scale [L, 2I, H/16] e4m3, w13_gscale [L] fp32, w2 [L, H, I/2], w2_scale [L, H, I/16], w2_gscale [L],
+    pw1 [H] fp32 (the per-feature output weight, shared by the rank's experts).
     `experts` restricts (and orders) the experts drawn; each is the same as in the full set."""
     H, I = cfg.h, cfg.i
     out = {k: [] for k in ("w13", "w13_scale", "w13_gscale", "w2", "w2_scale", "w2_gscale")}
@@ -294,7 +295,10 @@ def w4a16_weights(cfg: W4A16Config, seed: int = 0, experts: list[int] | None = N
             out[name].append(c)
             out[name + "_scale"].append(s)
             out[name + "_gscale"].append(g)
-    return {k: torch.stack(v) for k, v in out.items()}
+    res = {k: torch.stack(v) for k, v in out.items()}
+    # the engines' per-feature output weight pw1 [H] (sc_h.cu:51): seeded, around 1
+    res["pw1"] = 1.0 + 0.25 * _randn((H,), seed * 1000 + _TID_ZIPF + 100, "cpu", 1.0, torch.float32)
+    return res
 
 
 def w4a16_routing(cfg: W4A16Config, seed: int = 0) -> tuple[torch.Tensor, torch.Tensor]:

@@ -8,8 +8,10 @@ routes to this rank's experts (ids < local) computed, and a post-expert RMS norm
   for each local route (t, j), e = ids[t, j] < local:
       W13 = e2m1 * scale (exact in bf16); g, u = x[t] . W1[e]^T * gs13[e], x[t] . W3[e]^T * gs13[e]
       h   = bf16( silu(g) * u )                                   (sc_h.cu:322-340)
-      y   = (h . W2[e]^T) * gs2[e]                                 (sc_h.cu:341-381)
-      out[t] += tw[t, j] * y * rsqrt(mean(y^2) + 1e-8)             (x3_h.cu:496-663, x7_h.cu:438-590)
+      y   = (h . W2[e]^T) * gs2[e] * pw1                           fp32, pw1 [H] a per-feature weight
+                                                                   (sc_h.cu:51, 209, 346; x3_h.cu:110, 345, 529)
+      out[t] += y * tw[t, j] * rsqrt(mean(y^2) + 1e-8)             y stays fp32 through the sum of squares
+                                                                   (sc_h.cu:347-351, 380; x3_h.cu:530-535, 654-656)
   OUT = bf16(out)
 
 The reference's problem package (reference.py, its NVFP4 layout and checks) is not in its tree, so the
@@ -33,13 +35,16 @@ def dequant_expert(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 
 
 def w4a16_ref(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, weights: dict, local: int) -> torch.Tensor:
-    """fp32 [T, H] layer output (before the final bf16 rounding) on the CPU."""
+    """fp32 [T, H] layer output (before the final bf16 rounding) on the CPU.  weights["pw1"] (fp32 [H]) is the
+    engines' per-feature output weight; absent, it is 1."""
     x = x.detach().cpu()
     ids, tw = ids.detach().cpu(), tw.detach().cpu().float()
     T, H = x.shape
     out = torch.zeros((T, H), dtype=torch.float32)
     I = weights["w13"].shape[1] // 2
     xf = x.float()
+    pw1 = weights.get("pw1")
+    pw1 = torch.ones(H) if pw1 is None else pw1.detach().cpu().float()
     for e in range(local):
         rows = (ids == e).nonzero()
         if rows.numel() == 0:
@@ -51,10 +56,9 @@ def w4a16_ref(x: torch.Tensor, ids: torch.Tensor, tw: torch.Tensor, weights: dic
         gu = (xf[tok] @ w13.T) * gs13
         g, u = gu[:, :I], gu[:, I:]
         h = (g / (1.0 + torch.exp(-g)) * u).to(torch.bfloat16).float()
-        y = (h @ w2.T) * gs2
-        y = y.to(torch.bfloat16).float()                     # the down GEMM writes bf16 rows
+        y = (h @ w2.T) * gs2 * pw1                           # fp32, as the engines keep it
         rms = torch.rsqrt((y * y).mean(dim=1, keepdim=True) + RMS_EPS)
-        out.index_add_(0, tok, y * rms * tw[tok, slot].unsqueeze(1))
+        out.index_add_(0, tok, y * tw[tok, slot].unsqueeze(1) * rms)
     return out
 
 

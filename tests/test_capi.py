@@ -35,7 +35,7 @@ def test_python_binding_covers_header():
 
 
 def test_abi_version_and_strerror(lib):
-    assert lib.kdb_abi_version() == 1
+    assert lib.kdb_abi_version() == 2
     assert lib.kdb_strerror(0) == b"ok"
     assert b"timed out" in lib.kdb_strerror(_lib.KDB_ERR_TIMEOUT)
     assert lib.kdb_strerror(999) == b"unknown status"
@@ -82,11 +82,11 @@ def test_w4a16_host_checks(lib):
     assert lib.kdb_moe_w4a16_workspace_bytes(256, 4096, 4000, 32, 256, 8) == 0   # I % 128 != 0
     assert lib.kdb_moe_w4a16_workspace_bytes(256, 4096, 4096, 300, 256, 8) == 0  # local > total experts
     vp = ctypes.c_void_p
-    ptrs = [vp(256)] * 8
+    ptrs = [vp(256)] * 9          # x, ids, tw, w13 blocks, gs13, w2 blocks, gs2, pw1, y
     shape = (16, 4096, 4096, 32, 256, 8)
     need = lib.kdb_moe_w4a16_workspace_bytes(*shape)
     # no tokens: nothing to do, whatever the pointers
-    assert lib.kdb_moe_w4a16_forward(*([None] * 8), 0, 4096, 4096, 32, 256, 8, None, 0, None) == 0
+    assert lib.kdb_moe_w4a16_forward(*([None] * 9), 0, 4096, 4096, 32, 256, 8, None, 0, None) == 0
     # null, misaligned, too small a workspace: rejected before any launch
     assert lib.kdb_moe_w4a16_forward(*([None] + ptrs[1:]), *shape, vp(256), need, None) == _lib.KDB_ERR_INVALID_ARG
     assert lib.kdb_moe_w4a16_forward(*([vp(264)] + ptrs[1:]), *shape, vp(256), need, None) == _lib.KDB_ERR_INVALID_ARG

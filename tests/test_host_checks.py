@@ -15,7 +15,7 @@ def _w4_args(t=5, h=256, i=128, local=4, k=4):
     x = torch.zeros((t, h), dtype=torch.bfloat16)
     ids = torch.zeros((t, k), dtype=torch.int32)
     tw = torch.full((t, k), 1.0 / k)
-    return [x, ids, tw, st["w13_blocks"], st["w13_gscale"], st["w2_blocks"], st["w2_gscale"], 32]
+    return [x, ids, tw, st["w13_blocks"], st["w13_gscale"], st["w2_blocks"], st["w2_gscale"], st["pw1"], 32]
 
 
 def test_w4a16_prepare_shapes_on_cpu():
@@ -35,7 +35,9 @@ def test_w4a16_prepare_shapes_on_cpu():
     (1, torch.zeros((6, 4), dtype=torch.int32), ValueError),            # ids rows != tokens
     (5, torch.zeros((4, 1, 3, 9216), dtype=torch.uint8), ValueError),   # down blocks for another I
     (6, torch.zeros(3, dtype=torch.float32), ValueError),               # one scale per local expert
-    (7, 3, ValueError),                                                 # e_total below the local experts
+    (7, torch.ones(128, dtype=torch.float32), ValueError),              # pw1 is one weight per hidden feature
+    (7, torch.ones(256, dtype=torch.float16), ValueError),              # pw1 not fp32
+    (8, 3, ValueError),                                                 # e_total below the local experts
 ])
 def test_w4a16_rejects_bad_arguments(pos, bad, exc):
     a = _w4_args()

@@ -103,3 +103,22 @@ def test_w4a16_through_submission():
     torch.cuda.synchronize()
     ok, msg = ow.check(y, ow.w4a16_ref(x, ids, tw, wts, cfg.local))
     assert ok, msg
+
+
+def test_w4a16_per_feature_weight_pw1():
+    """The engines' per-feature output weight pw1 (okc-challenge/engines/sc_h.cu:51, 346) multiplies y before
+    its sum of squares: with a non-unit pw1 the output matches the oracle and differs from pw1 = 1."""
+    cfg = W.W4A16Config("pw1", 24, 512, 256, 4, 32, 4)
+    wts = W.w4a16_weights(cfg, 5)
+    assert float((wts["pw1"] - 1).abs().max()) > 0.1
+    ids, tw = W.w4a16_routing(cfg, 5)
+    x = W.moe_input(cfg.t, cfg.h, 5)
+    y = W4.forward(x.cuda(), ids.cuda(), tw.cuda(), W4.prepare(wts), cfg.e_total)
+    ones = dict(wts, pw1=torch.ones(cfg.h))
+    y1 = W4.forward(x.cuda(), ids.cuda(), tw.cuda(), W4.prepare(ones), cfg.e_total)
+    torch.cuda.synchronize()
+    ok, msg = ow.check(y, ow.w4a16_ref(x, ids, tw, wts, cfg.local))
+    assert ok, msg
+    ok1, msg1 = ow.check(y1, ow.w4a16_ref(x, ids, tw, ones, cfg.local))
+    assert ok1, msg1
+    assert float((y.float() - y1.float()).abs().max()) > 0.05
