@@ -230,12 +230,6 @@ def _proj_cfg(name):
     return W.PROJ_CONFIGS[name]
 
 
-def _lib_ws(cfg) -> int:
-    """Workspace bytes of the small-M K split for this shape (0: one launch, no split)."""
-    from kdb200 import _lib
-    return int(_lib.lib().kdb_proj_workspace_bytes(cfg.m, cfg.n, cfg.k))
-
-
 def bench_proj(args, dist: Dist) -> dict | None:
     from kdb200 import proj_into
     from kdb200 import workloads as W
@@ -295,9 +289,8 @@ def bench_proj(args, dist: Dist) -> dict | None:
     from kdb200.proj import tile_shape
     bn, pair = tile_shape(cfg.m, cfg.n)
     if cfg.m <= 128:
-        split = int(_lib_ws(cfg)) > 0
-        roof["kernel"] = ("gemm_swap_kernel<ProjSwapSched> (weights as the M operand"
-                          + (", K split + proj_reduce4_kernel: two launches per step)" if split else "), one launch per step"))
+        roof["kernel"] = ("gemm_splitk_kernel (weights as the M operand, K split over a cluster reduced in "
+                          "distributed shared memory), one launch per step")
     else:
         roof["kernel"] = (f"gemm_tn_pair_kernel<ProjSched<256,{bn}>> (256 x {bn} tiles on 2-CTA clusters)" if pair else
                           f"gemm_tn_kernel<ProjSched<128,{bn}>> (128 x {bn} tiles)") + ", one launch per step"
@@ -311,7 +304,7 @@ def bench_proj(args, dist: Dist) -> dict | None:
                 "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": y.numel() * 2,
                 "path": "submissions/b200_bf16_proj.py kernel_fn (kdev adapter API) -> kdb_proj_bf16",
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps * (2 if cfg.m <= 128 and _lib_ws(cfg) > 0 else 1),
+        "gpu_launches": args.steps,
         "roofline": roof,
         "clocks": sampler.summary() if sampler else None,
         "timed_region_ms": round(region_ms, 2),

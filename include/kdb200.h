@@ -87,13 +87,13 @@ int kdb_selftest_wait_timeout(uint64_t limit_ns, void* stream);
 int kdb_proj_bf16(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                   void* stream);
 
-/* Workspace bytes kdb_proj_bf16_ws can use for this shape (0 when it needs none): fp32 partial sums of
- * the K split that small-M (m <= 128, weight-streaming) shapes use to put every SM on the weights. */
+/* Workspace bytes kdb_proj_bf16_ws can use for this shape: 0 for every shape.  Small-M (m <= 128,
+ * weight-streaming) shapes split K over the CTAs of a thread-block cluster and sum the fp32 partials in
+ * slice order through distributed shared memory inside the one launch, so no workspace is needed. */
 size_t kdb_proj_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
-/* kdb_proj_bf16 with a workspace (16-byte aligned, >= kdb_proj_workspace_bytes) for the small-M K split;
- * the partials are summed in slice order, so results are deterministic.  With a smaller or NULL
- * workspace it runs without the split. */
+/* kdb_proj_bf16 with a workspace argument, kept for callers of the earlier two-launch K split; the
+ * workspace is not used (results are deterministic either way). */
 int kdb_proj_bf16_ws(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t k, int64_t ldy,
                      void* workspace, size_t workspace_bytes, void* stream);
 
@@ -103,8 +103,8 @@ int kdb_proj_bf16_ws(const void* x, const void* w, void* y, int64_t m, int64_t n
  * muse_bf16_proj.toml:371; probe rows exact to 0.1%, :376).  Prepare once with kdb_proj_split_f32:
  * w fp32 [n, k] -> w_split bf16 [n, 2k] = [bf16(W) | bf16(W - bf16(W))] per row (each weight kept to
  * 2^-16 relative).  Then Y fp32 [m, n] (contiguous) = X · W_hiᵀ + X · W_midᵀ with fp32 accumulation;
- * k % 64 == 0, x and w_split 16-byte aligned.  m <= 128 uses a K-split workspace like kdb_proj_bf16_ws
- * (kdb_proj_f32w_workspace_bytes; NULL runs without the split).
+ * k % 64 == 0, x and w_split 16-byte aligned.  m <= 128 runs the in-launch cluster K split of
+ * kdb_proj_bf16; the workspace arguments are not used (kdb_proj_f32w_workspace_bytes is 0).
  */
 int kdb_proj_split_f32(const float* w, void* w_split, int64_t n, int64_t k, void* stream);
 size_t kdb_proj_f32w_workspace_bytes(int64_t m, int64_t n, int64_t k);

@@ -8,8 +8,9 @@ namespace kdb {
 // Automatic tile shape: width *bn (64..256) and *pair (1 = 256-row tiles on CTA pairs).
 void pick_tile(long long M, long long N, long long sms, int* bn, int* pair);
 
-// M <= 128 with automatic shape: weights as the M operand and a K split whose fp32 partials go to
-// `workspace` (proj_workspace_bytes); without enough workspace the K split is 1.
+// M <= 128 with automatic shape: weights as the M operand and a K split over a thread-block cluster,
+// reduced in distributed shared memory in the same launch.  `workspace` is not used (proj_workspace_bytes
+// is 0); the parameters remain for the C ABI's kdb_proj_bf16_ws.
 int proj_bf16(const void* x, const void* w, void* y, long long M, long long N, long long K, long long ldy,
               int force_bn, int cta_pair, cudaStream_t stream, void* workspace = nullptr, size_t ws_bytes = 0);
 size_t proj_workspace_bytes(long long M, long long N, long long K);

@@ -70,10 +70,12 @@ def test_cta_pair_tiles_match_single_cta(m, k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 7168, 7168), (16, 7168, 7168), (128, 7168, 7168), (128, 2048, 2048),
-                                   (37, 520, 1000), (100, 4096, 300)])
+                                   (37, 520, 1000), (100, 4096, 300), (5, 256, 333), (33, 64, 130)])
 def test_small_m_split_k(m, k, n):
-    """Weight-streaming shapes (M <= 128): swapped operands with a K split summed from fp32 partials;
-    deterministic (same result twice) and within tolerance of the oracle."""
+    """Weight-streaming shapes (M <= 128): swapped operands with K split over the CTAs of a cluster, whose
+    fp32 partials are summed in slice order through distributed shared memory in the same launch;
+    deterministic (same result twice) and within tolerance of the oracle.  Odd N exercises the scalar
+    stores, K = 64 a single slice."""
     x, w, gx, gw = _pair(m, k, n, seed=m * 3 + n)
     y1 = proj(gx, gw)
     y2 = proj(gx, gw)
@@ -83,7 +85,7 @@ def test_small_m_split_k(m, k, n):
 
 
 def test_small_m_without_workspace():
-    """The C entry point without a workspace runs the same path with one K slice."""
+    """The C entry point without a workspace runs the same single-launch path (no workspace is needed)."""
     import ctypes
     x, w, gx, gw = _pair(16, 7168, 2048, seed=3)
     y = torch.empty((16, 2048), dtype=torch.bfloat16, device="cuda")
