@@ -229,40 +229,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int per = (items + p.splits - 1) / p.splits;
     const int i0 = rank * per, i1 = min(items, i0 + per);
     const uint32_t base = smem_u32(partial);
-    for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += blockDim.x) {
-      const int tok = it / groups, g = it - tok * groups;
-      const int feat = g * 4;
-      if (feat >= n_feat) continue;
-      const uint32_t off = static_cast<uint32_t>((tok * L::kFeat + feat) * 4);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < p.splits; ++s) {
-        const float4 v = ld_dsmem_f4(mapa_shared(base + off, static_cast<uint32_t>(s)));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    // two items per thread and pass, all their S loads in flight before the first add (the loads are
+    // latency-bound); the adds then run in slice order
+    const int stride = static_cast<int>(blockDim.x);
+    for (int it = i0 + static_cast<int>(threadIdx.x); it < i1; it += 2 * stride) {
+      float4 v[2][8];
+      int tk[2], ft[2];
+      bool live[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int item = it + u * stride;
+        tk[u] = item / groups;
+        ft[u] = (item - tk[u] * groups) * 4;
+        live[u] = item < i1 && ft[u] < n_feat;
+        const uint32_t off = static_cast<uint32_t>((tk[u] * L::kFeat + ft[u]) * 4);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          if (live[u] && s < p.splits) v[u][s] = ld_dsmem_f4(mapa_shared(base + off, static_cast<uint32_t>(s)));
       }
-      const long long row = row0 + tok;
-      const int col = a_row + feat;
-      const float o[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (p.y32) {
-        float* dst = p.y32 + row * p.ldy + col;
-        if (p.vec_ok && feat + 4 <= n_feat) {
-          *reinterpret_cast<float4*>(dst) = acc;
-        } else {
-          for (int e = 0; e < 4; ++e)
-            if (feat + e < n_feat) dst[e] = o[e];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!live[u]) continue;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          if (s < p.splits) {
+            acc.x += v[u][s].x;
+            acc.y += v[u][s].y;
+            acc.z += v[u][s].z;
+            acc.w += v[u][s].w;
+          }
         }
-      } else {
-        __nv_bfloat16* dst = p.y + row * p.ldy + col;
-        if (p.vec_ok && feat + 4 <= n_feat) {
-          uint2 pk;
-          pk.x = pack_bf16x2(acc.x, acc.y);
-          pk.y = pack_bf16x2(acc.z, acc.w);
-          *reinterpret_cast<uint2*>(dst) = pk;
+        const int tok = tk[u], feat = ft[u];
+        const long long row = row0 + tok;
+        const int col = a_row + feat;
+        const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (p.y32) {
+          float* dst = p.y32 + row * p.ldy + col;
+          if (p.vec_ok && feat + 4 <= n_feat) {
+            *reinterpret_cast<float4*>(dst) = acc;
+          } else {
+            for (int e = 0; e < 4; ++e)
+              if (feat + e < n_feat) dst[e] = o[e];
+          }
         } else {
-          for (int e = 0; e < 4; ++e)
-            if (feat + e < n_feat) dst[e] = __float2bfloat16_rn(o[e]);
+          __nv_bfloat16* dst = p.y + row * p.ldy + col;
+          if (p.vec_ok && feat + 4 <= n_feat) {
+            uint2 pk;
+            pk.x = pack_bf16x2(acc.x, acc.y);
+            pk.y = pack_bf16x2(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(dst) = pk;
+          } else {
+            for (int e = 0; e < 4; ++e)
+              if (feat + e < n_feat) dst[e] = __float2bfloat16_rn(o[e]);
+          }
         }
       }
     }
