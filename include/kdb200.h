@@ -242,6 +242,23 @@ int kdb_moe_expert_down(const void* a, int64_t a_rows, const void* w_down, int64
                         void* stream);
 
 /*
+ * Grouped down projection with the weighted combine merged into its epilogue, in one launch: rows_out
+ * receives the scaled per-slot rows as kdb_moe_expert_down writes them (row_scale required), and each
+ * tile, once its accumulator is released, counts one arrival per row on (token, 128-feature block); the
+ * tile completing a block sums that block's k slot rows in slot order (+ shared_rows[t]) into y bf16
+ * [t, h], bitwise as kdb_moe_combine does.  perm_slot / slot_pos from kdb_moe_plan; h % 128 == 0;
+ * workspace >= kdb_moe_expert_down_combine_workspace_bytes(t, h) (arrival counters, zeroed here).
+ * Counterpart of the engines' down stage with its combine (okc-challenge/engines/sc_h.cu:341-381).
+ * kdb_moe_forward does not use it: measured on B200 the layer is faster with the separate combine.
+ */
+size_t kdb_moe_expert_down_combine_workspace_bytes(int64_t t, int64_t h);
+int kdb_moe_expert_down_combine(const void* a, int64_t a_rows, const void* w_down, int64_t groups, int64_t i, int64_t h,
+                                const int32_t* offsets, const int32_t* mtile_start, const float* row_scale,
+                                const int32_t* perm_slot, const int32_t* slot_pos, const void* shared_rows,
+                                void* rows_out, void* y, int64_t t, int64_t k, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/*
  * Weighted combine: y[t] = sum_j (slot_w[t*k+j] or 1) * rows[slot_pos[t*k+j]] (+ shared_rows[t]),
  * summed in fp32 in slot order (deterministic), bf16 out.  slot_w NULL: rows are already scaled.
  * Counterpart: the weighted combine of the reference engines (sc_h.cu:374-381).

@@ -211,6 +211,27 @@ int kdb_moe_expert_gate_up(const void* a, int64_t a_rows, const void* w_gate_up_
                                out, static_cast<cudaStream_t>(stream));
 }
 
+size_t kdb_moe_expert_down_combine_workspace_bytes(int64_t t, int64_t h) {
+  if (t <= 0 || h <= 0 || h % 128 != 0) return 0;
+  return static_cast<size_t>(t) * static_cast<size_t>(h / 128) * sizeof(int);
+}
+
+int kdb_moe_expert_down_combine(const void* a, int64_t a_rows, const void* w_down, int64_t groups, int64_t i, int64_t h,
+                                const int32_t* offsets, const int32_t* mtile_start, const float* row_scale,
+                                const int32_t* perm_slot, const int32_t* slot_pos, const void* shared_rows,
+                                void* rows_out, void* y, int64_t t, int64_t k, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  const int rc = expert_gemm_args(a, a_rows, w_down, groups, i, h, offsets, mtile_start, rows_out);
+  if (rc >= 0) return rc;
+  if (!offsets || !row_scale || !perm_slot || !slot_pos || !y || t <= 0 || k <= 0 || k > 32) return KDB_ERR_INVALID_ARG;
+  if (h % 128 != 0 || t > (1ll << 30) / 32) return KDB_ERR_UNSUPPORTED;
+  if (!workspace || workspace_bytes < kdb_moe_expert_down_combine_workspace_bytes(t, h)) return KDB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 3) != 0) return KDB_ERR_INVALID_ARG;
+  return kdb::moe_gemm_down_combine(a, (int)a_rows, w_down, (int)groups, (int)i, (int)h, offsets, mtile_start,
+                                    row_scale, perm_slot, slot_pos, static_cast<int*>(workspace), shared_rows, rows_out,
+                                    y, (int)t, (int)k, static_cast<cudaStream_t>(stream));
+}
+
 int kdb_moe_expert_down(const void* a, int64_t a_rows, const void* w_down, int64_t groups, int64_t i, int64_t h,
                         const int32_t* offsets, const int32_t* mtile_start, const float* row_scale, void* out,
                         void* stream) {

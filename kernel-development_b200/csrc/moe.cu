@@ -1,6 +1,5 @@
 // moe.cu — the fused MoE layer forward: route -> plan -> gather -> grouped gate_up (SwiGLU) ->
-// [shared expert] -> grouped down (x routing weight) with the weighted combine fused into its epilogue
-// (a separate combine kernel only for decode-size batches or H not a multiple of 128).  Every stage is a kernel launched on
+// [shared expert] -> grouped down (x routing weight) -> combine.  Every stage is a kernel launched on
 // the caller's stream; all scratch is carved from the caller's workspace, so the forward never
 // allocates or synchronises and can be captured in a CUDA graph.
 //
@@ -19,12 +18,8 @@ constexpr int kChunk = 256;   // tokens per plan chunk (moe_route.cu)
 
 struct Carve {
   size_t logits, chunk_counts, chunk_base, counts, offsets, mtile_start, perm_slot, slot_pos, perm_token, perm_w,
-      xy_perm, hbuf, hshared, yshared, arrivals, total;
+      xy_perm, hbuf, hshared, yshared, total;
 };
-
-// The down GEMM merges each token's slot rows in its epilogue (moe_gemm_down_combine) when it runs on the
-// CTA-pair path (some expert may hold more than 64 tokens) and H is a multiple of its 128-feature blocks.
-bool fused_combine(const MoeShape& sh) { return sh.t > 64 && sh.h % 128 == 0; }
 
 Carve carve(const MoeShape& sh) {
   Carve c{};
@@ -46,7 +41,6 @@ Carve carve(const MoeShape& sh) {
   c.hbuf = o;         o += up(2 * R * I);
   c.hshared = o;      o += sh.shared ? up(2 * T * sh.shared_i) : 0;
   c.yshared = o;      o += sh.shared ? up(2 * T * H) : 0;
-  c.arrivals = o;     o += fused_combine(sh) ? up(sizeof(int) * T * (H / 128)) : 0;
   c.total = o;
   return c;
 }
@@ -146,14 +140,9 @@ int moe_forward(const void* x, const float* router_w, const float* router_bias, 
     rc = moe_gemm_down(hs, T, shared_down, 1, Is, H, nullptr, nullptr, nullptr, yshared, s);
     if (rc) return rc;
   }
-  // x_perm is dead once gate_up has run (stream order): its buffer takes the per-slot down output.
-  if (fused_combine(sh)) {
-    int* arrivals = Ip(c.arrivals);
-    rc = cuda_status(cudaMemsetAsync(arrivals, 0, sizeof(int) * static_cast<size_t>(T) * (H / 128), s));
-    if (rc) return rc;
-    return moe_gemm_down_combine(hbuf, R, w_down, E, I, H, Ip(c.offsets), Ip(c.mtile_start), F(c.perm_w),
-                                 Ip(c.perm_slot), Ip(c.slot_pos), arrivals, yshared, xy_perm, y, T, K, s);
-  }
+  // x_perm is dead once gate_up has run (stream order): its buffer takes the per-slot down output.  The
+  // combine runs as its own kernel: the down GEMM with the combine merged into its epilogue
+  // (moe_gemm_down_combine, kdb_moe_expert_down_combine) measured slower on B200 at every layer size tried.
   rc = moe_gemm_down(hbuf, R, w_down, E, I, H, Ip(c.offsets), Ip(c.mtile_start), F(c.perm_w), xy_perm, s, T);
   if (rc) return rc;
   return moe_combine(xy_perm, Ip(c.slot_pos), yshared, y, T, H, K, s);

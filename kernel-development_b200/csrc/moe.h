@@ -30,8 +30,8 @@ int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
                   const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens = 0);
 // Grouped down (CTA-pair path) with the weighted combine fused into its epilogue: rows_out receives the
-// scaled per-slot rows, y[t] the combine of token t's k slot rows (+ yshared[t]); arrivals int32
-// [T, H / 128] must be zero at launch.  H % 128 == 0.
+// scaled per-slot rows, y[t] the combine of token t's k slot rows (+ yshared[t]); arrivals: int32
+// [T, H / 128] scratch, zeroed here.  H % 128 == 0.
 int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int groups, int I, int H,
                           const int* offsets, const int* mtile_start, const float* row_scale, const int* perm_slot,
                           const int* slot_pos, int* arrivals, const void* yshared, void* rows_out, void* y, int T,

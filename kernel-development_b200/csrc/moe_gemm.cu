@@ -207,9 +207,10 @@ struct ScaleGpEpi {
 // order then the shared row, exactly as moe_combine_kernel, so the result does not depend on which tile
 // arrives last.  Running the arrivals and merges after the release overlaps their memory latency (the
 // merge reads other tiles' rows, mostly from HBM) with the next tile's MMAs.  Ordering (the release /
-// acquire pattern of a split-K semaphore): each thread fences its slot-row stores, the group meets at a
-// barrier, then the arrivals; the thread completing a block fences before publishing it to its group, and
-// merge reads bypass L1.  The arrival counters ([T, H / 128] int32) are zeroed before the launch.
+// acquire pattern of a split-K semaphore): the group meets at a barrier after its slot-row stores, its first
+// warp fences (release) and makes the arrivals; a warp that completed a block fences again (acquire) before
+// the barrier that hands the list to the group, and merge reads bypass L1.  The arrival counters
+// ([T, H / 128] int32) are zeroed before the launch.
 struct ScaleCombineGpEpi {
   static constexpr int kTileElems = 32 * 128;
   static constexpr int kListInts = 132;   // [0] count, then the tokens to merge (<= 128 rows per group and slot)
@@ -266,19 +267,32 @@ struct ScaleCombineGpEpi {
     const int nfb = p.ld_out >> 7;
     const int fb = fbase >> 7;
     int* list = list_of(smem);
-    __threadfence();         // this thread's slot-row stores, before any arrival of the group
+    // Arrivals by the group's first warp only (the split-K semaphore pattern): the group barrier orders
+    // every thread's slot-row stores before that warp's fence, which then releases them (cumulatively)
+    // ahead of its relaxed atomics, one fence per group and slot instead of one per thread.
     epi_bar_sync(grp);
-    {
-      // the group's rows: chunks c0 = 32 * grp + 64 * i (i < 4), thread etid takes row (etid & 31) of chunk etid / 32
-      const int c = 32 * grp + 64 * (etid >> 5) + (etid & 31);
-      if (c < ncols) {
-        const int tok = __ldg(p.perm_slot + ti.b_row + tok0 + c) / p.k;
-        const int old = atomicAdd(p.arrivals + static_cast<long long>(tok) * nfb + fb, 1);
-        if (old == p.k - 1) {
-          __threadfence();   // acquire: the other tiles' rows of this block are visible from here on
-          list[1 + atomicAdd(list, 1)] = tok;
+    if (etid < 32) {
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      // the group's rows: chunks c0 = 32 * grp + 64 * i (i < 4); lane l takes row l of each chunk
+      int tok[4], old[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = 32 * grp + 64 * i + etid;
+        tok[i] = c < ncols ? __ldg(p.perm_slot + ti.b_row + tok0 + c) / p.k : -1;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        old[i] = tok[i] >= 0 ? atomicAdd(p.arrivals + static_cast<long long>(tok[i]) * nfb + fb, 1) : -1;
+      bool any_last = false;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (old[i] == p.k - 1) {
+          any_last = true;
+          list[1 + atomicAdd(list, 1)] = tok[i];
         }
       }
+      // acquire: the other tiles' rows of the completed blocks are visible to the group after the barrier
+      if (__any_sync(0xffffffffu, any_last)) asm volatile("fence.acq_rel.gpu;" ::: "memory");
     }
     epi_bar_sync(grp);
     const int nm = list[0];
@@ -608,9 +622,11 @@ int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int gro
                           const int* offsets, const int* mtile_start, const float* row_scale, const int* perm_slot,
                           const int* slot_pos, int* arrivals, const void* yshared, void* rows_out, void* y, int T,
                           int k, cudaStream_t s) {
-  if (a_rows <= 0) return KDB_OK;
+  if (T <= 0 || a_rows <= 0) return KDB_OK;
   if (H % 128 != 0 || !aligned16(rows_out) || !aligned16(y) || (yshared && !aligned16(yshared)))
     return KDB_ERR_UNSUPPORTED;
+  int rc = cuda_status(cudaMemsetAsync(arrivals, 0, sizeof(int) * static_cast<size_t>(T) * (H / 128), s));
+  if (rc) return rc;
   GroupedPairSched::Params sp;
   sp.offsets = offsets;
   sp.tile_start = mtile_start;

@@ -60,6 +60,9 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_moe_expert_down": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp,
                                      _c_vp]),
     "kdb_moe_combine": (_c_int, [_c_vp] * 5 + [_c_i64] * 3 + [_c_vp]),
+    "kdb_moe_expert_down_combine_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
+    "kdb_moe_expert_down_combine": (_c_int, [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64] + [_c_vp] * 8
+                                    + [_c_i64, _c_i64, _c_vp, _c_size, _c_vp]),
     "kdb_moe_ep_regroup_workspace_bytes": (_c_size, [_c_i64, _c_i64]),
     "kdb_moe_ep_regroup": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp,
                                     _c_size, _c_vp]),

@@ -316,6 +316,39 @@ def expert_down(a: torch.Tensor, w_down: torch.Tensor, offsets: Optional[torch.T
     return out
 
 
+def expert_down_combine(a: torch.Tensor, w_down: torch.Tensor, offsets: torch.Tensor, mtile_start: torch.Tensor,
+                        row_scale: torch.Tensor, perm_slot: torch.Tensor, slot_pos: torch.Tensor, t: int, k: int,
+                        shared_rows: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Grouped down with the combine merged into its epilogue (one launch): returns (per-slot rows bf16
+    [R, H], y bf16 [t, H]); y equals combine(rows, slot_pos, t, k, shared_rows=shared_rows) bitwise."""
+    _need("a", a, torch.bfloat16, 2)
+    _need("w_down", w_down, torch.bfloat16, 3)
+    groups, h, i = w_down.shape
+    _check_groups(a, i, groups, offsets, mtile_start)
+    for name, v in (("row_scale", row_scale),):
+        _need(name, v, torch.float32, 1)
+    _need("perm_slot", perm_slot, torch.int32, 1)
+    _need("slot_pos", slot_pos, torch.int32, 1)
+    if row_scale.numel() != a.shape[0] or perm_slot.numel() != a.shape[0] or slot_pos.numel() != t * k:
+        raise ValueError("row_scale and perm_slot need one entry per row, slot_pos t * k entries")
+    if shared_rows is not None:
+        _need("shared_rows", shared_rows, torch.bfloat16, 2)
+        if tuple(shared_rows.shape) != (t, h):
+            raise ValueError(f"shared_rows must be [{t}, {h}]")
+    _same_device(a.device, row_scale=row_scale, perm_slot=perm_slot, slot_pos=slot_pos, shared_rows=shared_rows)
+    rows = torch.empty((a.shape[0], h), dtype=torch.bfloat16, device=a.device)
+    y = torch.empty((t, h), dtype=torch.bfloat16, device=a.device)
+    nbytes = int(_lib.lib().kdb_moe_expert_down_combine_workspace_bytes(t, h))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=a.device)
+    with torch.cuda.device(a.device):
+        rc = _lib.lib().kdb_moe_expert_down_combine(
+            a.data_ptr(), a.shape[0], w_down.data_ptr(), groups, i, h, offsets.data_ptr(), mtile_start.data_ptr(),
+            row_scale.data_ptr(), perm_slot.data_ptr(), slot_pos.data_ptr(), _ptr(shared_rows), rows.data_ptr(),
+            y.data_ptr(), t, k, ws.data_ptr(), ws.numel(), _vp(_stream(a.device)))
+    _lib.check("kdb_moe_expert_down_combine", rc)
+    return rows, y
+
+
 def combine(rows: torch.Tensor, slot_pos: torch.Tensor, t: int, k: int, slot_w: Optional[torch.Tensor] = None,
             shared_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y[t] = sum_j (slot_w or 1) * rows[slot_pos[t*k + j]] (+ shared_rows[t]) in fp32, bf16 out."""

@@ -307,9 +307,10 @@ def test_sm_budget_leaves_results_unchanged():
     W.MoeConfig("fused_h384", 200, 384, 8, 128, 2, shared=1, shared_i=128),   # last pair tile half past H
 ])
 def test_fused_combine_equals_stage_composition(cfg):
-    """The layer's down GEMM merges each token's slot rows in its epilogue (the last of the token's k tiles
-    to arrive sums them in slot order).  Its output must equal, bitwise, the separate stages: grouped down
-    into per-slot rows, then the combine kernel."""
+    """kdb_moe_expert_down_combine merges each token's slot rows in the down GEMM's epilogue (the last of the
+    token's k tiles to arrive sums them in slot order).  Its rows and y must equal, bitwise, the separate
+    stages: grouped down into per-slot rows, then the combine kernel; the layer (which uses the separate
+    stages) agrees too."""
     x = W.moe_input(cfg.t, cfg.h, 21, device="cuda")
     state = M.prepare(W.moe_weights(cfg, 21, device="cuda"), cfg.k)
     y, w, ids = M.forward(x, state)
@@ -325,5 +326,10 @@ def test_fused_combine_equals_stage_composition(cfg):
         hs = M.expert_gate_up(x, state["shared_gate_up_packed"])
         ys = M.expert_down(hs, state["shared_down"])
     y2 = M.combine(rows, p["slot_pos"], cfg.t, cfg.k, shared_rows=ys)
+    rows3, y3 = M.expert_down_combine(h, state["w_down"], p["offsets"], mt, perm_w, p["perm_slot"], p["slot_pos"],
+                                      cfg.t, cfg.k, shared_rows=ys)
+    rows4, y4 = M.expert_down_combine(h, state["w_down"], p["offsets"], mt, perm_w, p["perm_slot"], p["slot_pos"],
+                                      cfg.t, cfg.k, shared_rows=ys)   # counters start from zero again
     torch.cuda.synchronize()
     assert torch.equal(y, y2)
+    assert torch.equal(rows3, rows) and torch.equal(y3, y2) and torch.equal(y4, y2)
