@@ -8,9 +8,20 @@ from __future__ import annotations
 import torch
 
 # Tolerances of the projection check: max-abs and relative Frobenius error against this
-# fp32 reference (the bf16 rounding of Y alone gives a relative error near 2^-9 / sqrt(3)).
+# fp32 reference (the bf16 rounding of Y alone gives a relative error near 2^-9 / sqrt(3)).  The max-abs
+# bound is 2e-2 for outputs of unit scale (the benchmark distributions: X ~ N(0, 1), W ~ N(0, 1/K) give
+# rms(Y) ~ 1) and grows with rms(Y) above that: for heavy-tailed inputs (the reference's "outliers"
+# distribution, rms(Y) ~ 8) the bf16 rounding of the largest outputs alone is half a unit in the last
+# place of |Y| ~ 32, i.e. 0.06.
 MAX_ABS_TOL = 2e-2
 REL_FRO_TOL = 1e-2
+
+
+def max_abs_bound(ref: torch.Tensor) -> float:
+    """MAX_ABS_TOL * max(1, rms(ref))."""
+    r = ref.detach().cpu().float()
+    rms = float(r.pow(2).mean().sqrt()) if r.numel() else 0.0
+    return MAX_ABS_TOL * max(1.0, rms)
 
 
 def proj_ref(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -61,7 +72,8 @@ def check(out: torch.Tensor, ref: torch.Tensor) -> tuple[bool, str]:
     if tuple(out.shape) != tuple(ref.shape):
         return False, f"shape {tuple(out.shape)} != expected {tuple(ref.shape)}"
     c = compare(out, ref)
-    ok = c["nonfinite"] == 0 and c["max_abs"] <= MAX_ABS_TOL and c["rel_fro"] <= REL_FRO_TOL
+    mab = max_abs_bound(ref)
+    ok = c["nonfinite"] == 0 and c["max_abs"] <= mab and c["rel_fro"] <= REL_FRO_TOL
     msg = (f"relative L2 error {c['rel_fro']:.3e} (worst row {c['worst_row']:.3e}) max-abs {c['max_abs']:.3e} "
-           f"[bound {REL_FRO_TOL}: max-abs <= {MAX_ABS_TOL}]")
+           f"[bound {REL_FRO_TOL}: max-abs <= {mab:.3g}]")
     return ok, msg

@@ -1,7 +1,8 @@
 """GPU parity tests of the bf16 projection (libkdb200 kdb_proj_bf16) against the fp32 oracle.
 
-Tolerance (written here, shared with the oracle's check): max-abs <= 2e-2 and relative Frobenius
-<= 1e-2 against x.float() @ w.float().T; the bf16 rounding of Y alone gives ~1.7e-3."""
+Tolerance (written here, shared with the oracle's check): max-abs <= 2e-2 * max(1, rms(Y_ref)) and relative
+Frobenius <= 1e-2 against x.float() @ w.float().T; the bf16 rounding of Y alone gives ~1.7e-3.  The benchmark
+distributions have rms(Y_ref) ~ 1, so the max-abs bound there is 2e-2."""
 from __future__ import annotations
 
 from pathlib import Path
@@ -29,7 +30,7 @@ def _pair(m, k, n, seed=0):
 def _assert_close(y, ref):
     c = op.compare(y, ref)
     assert c["nonfinite"] == 0, c
-    assert c["max_abs"] <= MAX_ABS and c["rel_fro"] <= REL_FRO, c
+    assert c["max_abs"] <= MAX_ABS * max(1.0, float(ref.float().pow(2).mean().sqrt())) and c["rel_fro"] <= REL_FRO, c
 
 
 @pytest.mark.parametrize("m,k,n", [
