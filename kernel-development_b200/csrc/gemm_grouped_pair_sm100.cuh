@@ -53,10 +53,7 @@ struct GpLayout {
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   static constexpr int kBarOffset = kEpiOffset + EPI_BYTES;
   static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;
-  // gathered token rows (row-gather mode): this CTA's source row of every token row of the current tile
-  static constexpr int kGatherInts = 128 + (kGpTokens - kGpSlotCols) / 2;
-  static constexpr int kGatherOffset = (kBarOffset + kBarBytes + 15) / 16 * 16;
-  static constexpr int kSmemBytes = kGatherOffset + kGatherInts * 4 + 1024;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
   static constexpr uint32_t kTmemCols = 2 * kGpSlotCols;
 };
 
@@ -93,10 +90,7 @@ __device__ __forceinline__ void epi_bar_sync(int grp) {
   asm volatile("bar.sync %0, 128;" ::"r"(2 + 2 * grp) : "memory");
 }
 
-// GATHER: the token operand is not laid out in tile order; token row r of a tile is row gather[r] of the
-// tensor in tmB.m[0] (a map whose box is one row high), loaded four rows per TMA gather (tile::gather4).  This
-// reads the layer's input rows in place of a permuted copy of them.
-template <class Sched, class Epi, int ABOXES, int STAGES, bool GATHER = false>
+template <class Sched, class Epi, int ABOXES, int STAGES>
 __global__ void __launch_bounds__(kGpThreads, 1)
     gemm_grouped_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ TokenMaps tmB,
                              const typename Sched::Params sp, const typename Epi::Params ep) {
@@ -165,37 +159,19 @@ __global__ void __launch_bounds__(kGpThreads, 1)
         const int a_row = ti.a_row + static_cast<int>(rank) * ti.a_rank_stride;
         const int b1 = ti.b_row + static_cast<int>(rank) * h1;
         const int b2 = ti.b_row + sp2.m1 + static_cast<int>(rank) * h2;
-        int* gidx = reinterpret_cast<int*>(smem + L::kGatherOffset);
-        if constexpr (GATHER) {
-          // source rows of this CTA's token rows; rows past the tile's tokens repeat its last row (their MMA
-          // columns are never stored).  h1, h2 are multiples of 8, so every gather moves four rows.
-          const int last = ti.b_row + ti.n_valid - 1;
-          for (int j = 0; j < h1; ++j) gidx[j] = __ldg(sp.gather + min(b1 + j, last));
-          for (int j = 0; j < h2; ++j) gidx[128 + j] = __ldg(sp.gather + min(b2 + j, last));
-        }
-        const uint32_t tx_bytes = GATHER ? 2u * (L::kABytes + static_cast<uint32_t>(h1 + h2) * kBK * 2) : bytes;
         for (int kb = 0; kb < ti.nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProdEmpty)) {
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(&full[stage], tx_bytes);
+          if (leader) mbar_arrive_expect_tx(&full[stage], bytes);
           uint8_t* st = smem + stage * L::kStageBytes;
           const uint32_t bar = full_lead + 8u * stage;
 #pragma unroll
           for (int b = 0; b < ABOXES; ++b)
             tma_load_2d_pair(st + b * L::kABoxRows * kBK * 2, &tmA, bar, kb * kBK, a_row + b * ti.a_box_stride, pol);
-          if constexpr (GATHER) {
-            for (int q = 0; q < h1; q += 4)
-              tma_gather4_pair(st + L::kABytes + q * kBK * 2, &tmB.m[0], bar, kb * kBK,
-                               *reinterpret_cast<const int4*>(gidx + q), pol);
-            for (int q = 0; q < h2; q += 4)
-              tma_gather4_pair(st + L::kABytes + L::kBRegion + q * kBK * 2, &tmB.m[0], bar, kb * kBK,
-                               *reinterpret_cast<const int4*>(gidx + 128 + q), pol);
-          } else {
-            tma_load_2d_pair(st + L::kABytes, &tmB.m[bi1], bar, kb * kBK, b1, pol);
-            if (h2 > 0) tma_load_2d_pair(st + L::kABytes + L::kBRegion, &tmB.m[bi2], bar, kb * kBK, b2, pol);
-          }
+          tma_load_2d_pair(st + L::kABytes, &tmB.m[bi1], bar, kb * kBK, b1, pol);
+          if (h2 > 0) tma_load_2d_pair(st + L::kABytes + L::kBRegion, &tmB.m[bi2], bar, kb * kBK, b2, pol);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {

@@ -1,6 +1,5 @@
-// moe.cu — the fused MoE layer forward: route -> plan -> grouped gate_up (SwiGLU; token rows gathered in
-// place by its TMA loads, or by a gather kernel for decode-size batches) -> [shared expert] -> grouped down
-// (x routing weight) -> combine.  Every stage is a kernel launched on
+// moe.cu — the fused MoE layer forward: route -> plan -> gather -> grouped gate_up (SwiGLU) ->
+// [shared expert] -> grouped down (x routing weight) -> combine.  Every stage is a kernel launched on
 // the caller's stream; all scratch is carved from the caller's workspace, so the forward never
 // allocates or synchronises and can be captured in a CUDA graph.
 //
@@ -125,17 +124,10 @@ int moe_forward(const void* x, const float* router_w, const float* router_bias, 
   if (rc) return rc;
   void* xy_perm = ws + c.xy_perm;
   void* hbuf = ws + c.hbuf;
-  // a token picks an expert at most once: no group holds more than T rows.  Above 64 tokens the CTA-pair
-  // gate_up reads each token row of x in place (row gather by perm_token); the weight-streaming path of
-  // decode-size batches reads a permuted copy.
-  if (T > 64) {
-    rc = moe_gemm_gate_up(x, T, w_gate_up_packed, E, I, H, Ip(c.offsets), Ip(c.mtile_start), hbuf, s, T,
-                          Ip(c.perm_token));
-  } else {
-    rc = moe_gather_rows(x, Ip(c.perm_token), xy_perm, R, H, T, s);
-    if (rc) return rc;
-    rc = moe_gemm_gate_up(xy_perm, R, w_gate_up_packed, E, I, H, Ip(c.offsets), Ip(c.mtile_start), hbuf, s, T);
-  }
+  rc = moe_gather_rows(x, Ip(c.perm_token), xy_perm, R, H, T, s);
+  if (rc) return rc;
+  // a token picks an expert at most once: no group holds more than T rows
+  rc = moe_gemm_gate_up(xy_perm, R, w_gate_up_packed, E, I, H, Ip(c.offsets), Ip(c.mtile_start), hbuf, s, T);
   if (rc) return rc;
   // the shared expert first: the routed down's combine reads its rows
   void* yshared = nullptr;

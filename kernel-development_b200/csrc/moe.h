@@ -25,11 +25,8 @@ size_t moe_ep_regroup_scratch_bytes(int P, int Er);
 int moe_pack_gate_up(const void* w, void* packed, int E, int I, int H, cudaStream_t s);
 // Grouped expert GEMMs (moe_gemm.cu).  max_group_tokens: an upper bound on any group's row count that the
 // caller guarantees (0 = none known; a_rows is used); a bound <= 64 selects the weight-streaming variant.
-// gather_rows (CTA-pair path only, grouped): token row r of the grouped order is row gather_rows[r] of `a`
-// ([a_rows, H]), read in place by the GEMM's TMA gathers instead of from a permuted copy.
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
-                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens = 0,
-                     const int* gather_rows = nullptr);
+                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens = 0);
 int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int I, int H, const int* offsets,
                   const int* mtile_start, const float* row_scale, void* out, cudaStream_t s, int max_group_tokens = 0);
 // Grouped down (CTA-pair path) with the weighted combine fused into its epilogue: rows_out receives the

@@ -42,7 +42,6 @@ struct GroupedPairSched {
     int a_box_stride;         // offset of a CTA's second 64-row box (gate_up: gate -> up rows)
     int a_rank_stride;        // offset of CTA 1's rows
     int f_step;               // output features per weight tile
-    const int* gather;        // row-gather mode: source row of each token row (tile order), else null
   };
   Params p;
   int total_tt;
@@ -477,12 +476,12 @@ static int ensure_smem_attr(Kern kern, int bytes, bool* done) {
   return KDB_OK;
 }
 
-template <class Epi, int ABOXES, bool GATHER = false>
+template <class Epi, int ABOXES>
 static int launch_grouped_pair(const void* tokens, int a_rows, const void* weights, uint64_t weight_rows, int K,
                                const GroupedPairSched::Params& sp, const typename Epi::Params& ep, cudaStream_t s) {
   constexpr int kStages = 4;   // 48 KB per stage: 128 weight rows + two 128-row token groups
   using L = GpLayout<ABOXES, kStages, 2 * Epi::kSmemBytes>;
-  auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, kStages, GATHER>;
+  auto kern = gemm_grouped_pair_kernel<GroupedPairSched, Epi, ABOXES, kStages>;
   static bool done[64] = {false};
   int rc = ensure_smem_attr(kern, L::kSmemBytes, done);
   if (rc) return rc;
@@ -490,11 +489,8 @@ static int launch_grouped_pair(const void* tokens, int a_rows, const void* weigh
   TokenMaps tb;
   rc = make_tmap_bf16_2d(&ta, weights, K, weight_rows, K, kBK, L::kABoxRows);
   if (rc) return rc;
-  // row-gather mode reads single rows (a box one row high, four rows per gather); otherwise five boxes
-  rc = GATHER ? make_tmap_bf16_2d(&tb.m[0], tokens, K, a_rows, K, kBK, 1) : make_token_maps(&tb, tokens, a_rows, K);
+  rc = make_token_maps(&tb, tokens, a_rows, K);
   if (rc) return rc;
-  if (GATHER)
-    for (int i = 1; i < 5; ++i) tb.m[i] = tb.m[0];   // every map the kernel prefetches is a valid descriptor
   int pairs = num_sms() / 2;
   if (!sp.tile_start) {
     const int tiles = ((a_rows + kGpTokens - 1) / kGpTokens) * sp.f_tiles;
@@ -537,10 +533,9 @@ static int launch_stream(const void* tokens, int a_rows, const void* weights, ui
 }
 
 int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups, int I, int H, const int* offsets,
-                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens, const int* gather_rows) {
+                     const int* mtile_start, void* out, cudaStream_t s, int max_group_tokens) {
   if (a_rows <= 0) return KDB_OK;
   const int bound = max_group_tokens > 0 && max_group_tokens < a_rows ? max_group_tokens : a_rows;
-  if (gather_rows && (bound <= 64 || !offsets || !mtile_start)) return KDB_ERR_INVALID_ARG;
   if (bound <= 64) {
     StreamSched::Params sp;
     sp.offsets = offsets;
@@ -570,15 +565,11 @@ int moe_gemm_gate_up(const void* a, int a_rows, const void* w_packed, int groups
   sp.a_box_stride = 128;       // gate row r -> its up row r + 128 within the packed block
   sp.a_rank_stride = 64;       // CTA 1 takes features 64..127 of the block
   sp.f_step = 128;
-  sp.gather = gather_rows;
   SwigluGpEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(out);
   ep.ld_out = I;
   ep.n_feat = I;
   ep.vec_ok = aligned16(out) && I % 8 == 0;
-  if (gather_rows)
-    return launch_grouped_pair<SwigluGpEpi, 2, true>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp,
-                                                     ep, s);
   return launch_grouped_pair<SwigluGpEpi, 2>(a, a_rows, w_packed, static_cast<uint64_t>(groups) * 2 * I, H, sp, ep,
                                              s);
 }
@@ -618,7 +609,6 @@ int moe_gemm_down(const void* a, int a_rows, const void* w_down, int groups, int
   sp.a_box_stride = 0;
   sp.a_rank_stride = 128;
   sp.f_step = 256;
-  sp.gather = nullptr;
   ScaleGpEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(out);
   ep.row_scale = row_scale;
@@ -649,7 +639,6 @@ int moe_gemm_down_combine(const void* a, int a_rows, const void* w_down, int gro
   sp.a_box_stride = 0;
   sp.a_rank_stride = 128;
   sp.f_step = 256;
-  sp.gather = nullptr;
   ScaleCombineGpEpi::Params ep;
   ep.out = static_cast<__nv_bfloat16*>(rows_out);
   ep.row_scale = row_scale;

@@ -274,19 +274,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tma
       : "memory");
 }
 
-// Four rows (rows.x .. rows.w) of a 2-D tensor map whose box is 64 columns x 1 row, columns [c0, c0 + 64), into
-// 512 consecutive bytes of shared memory (laid out as four rows of a tile load with the map's swizzle), for the
-// pair: completion on an mbarrier of either CTA (shared::cluster address).  No multicast.
-__device__ __forceinline__ void tma_gather4_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int32_t c0,
-                                                 int4 rows, uint64_t cache_policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.cta_group::2"
-      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(rows.x), "r"(rows.y), "r"(rows.z),
-      "r"(rows.w), "l"(cache_policy)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
