@@ -2,16 +2,19 @@
 //
 // The weights stream from HBM as NVFP4 (E2M1 codes, one E4M3 scale per 16 elements; 4.5 bits per weight)
 // and become f16 tcgen05 operands only on chip:
-//   producer (warp 0, one thread): one bulk copy per raw stage of two k chunks; prepare() stores, for each
+//   producer (warp 0, one thread): per raw stage of two k chunks, one bulk copy of their NVFP4 blocks and
+//       one TMA copy per chunk of the tile's token rows (f16), all completing on the stage's barrier, so a
+//       chunk's tokens arrive RSTAGES stages ahead together with its weights.  prepare() stores, for each
 //       weight tile (two 128-row parts) and 64-element k chunk, both parts' codes (2 x 4 KB) and scales
 //       (2 x 512 B) contiguously and the chunks of a tile one after another, because each TMA operation
-//       carries a fixed cost that dominated when a chunk took four small copies;
+//       carries a fixed cost that dominated when a chunk took four small copies.  (The tokens were once
+//       loaded by the converter at the start of each chunk; the MMA then waited ~1.5 us on every chunk's
+//       token copy with only CSTAGES chunks of slack, which capped each SM at ~16 GB/s of NVFP4.)
 //   converter (warps 6-9): e2m1 x e4m3 -> f16 (cvt.rn.f16x2.e2m1x2, then one f16x2 multiply: both exact,
 //       the product has at most 6 significant bits) written straight into TMEM with tcgen05.st (lane =
-//       weight row, two k elements per 32-bit column), where the MMA takes its A operand; thread 0 also
-//       loads the stage's token rows (f16) into shared memory with TMA.  Staging the f16 weights in TMEM
-//       keeps them out of shared memory, whose bandwidth (32 KB of f16 written and read per 9 KB of NVFP4)
-//       bounded the version that converted into a swizzled shared-memory tile;
+//       weight row, two k elements per 32-bit column), where the MMA takes its A operand.  Staging the f16
+//       weights in TMEM keeps them out of shared memory, whose bandwidth (32 KB of f16 written and read per
+//       9 KB of NVFP4) bounded the version that converted into a swizzled shared-memory tile;
 //   MMA issuer (warp 1, one thread): A = 128 weight rows of each part from TMEM, B = the tile's tokens
 //       (N = tokens rounded up to 16) from shared memory, K = 16 per instruction, double-buffered
 //       accumulators (2 parts x 64 token columns each);
@@ -22,10 +25,11 @@
 // bf16 computation.  Why not tcgen05's block-scaled MMA: it scales fp4/fp6/fp8 operands only, and w4a16
 // keeps the activations in 16 bits.
 //
-// Signalling (all waits bounded): raw_full (TMA tx), raw_empty (converter), conv_full (converter's
-// expect-tx for the tokens + its arrival after its tcgen05.st of the weights completed and was fenced),
-// conv_empty (MMA commit), tfull / tempty (accumulators).  The converter warps vote after each wait so
-// their named barrier is reached by all four or none.
+// Signalling (all waits bounded): raw_full (TMA tx of weights and tokens), raw_empty (two arrivals: the
+// converter once it has read the stage's weights, the MMA commit once the MMAs reading its tokens are done),
+// conv_full (the converter's arrival after its tcgen05.st of the weights completed and was fenced),
+// conv_empty (MMA commit), tfull / tempty (accumulators).  The converter warps vote after each wait so their
+// named barrier is reached by all four or none.
 #pragma once
 
 #include <cuda.h>
@@ -51,9 +55,10 @@ struct Fp4Tile {
 
 template <int RSTAGES, int CSTAGES>
 struct Fp4Layout {
-  static constexpr int kTokBytes = kFp4NB * kBK * 2;           // one stage's token rows (B, 64 x 64 f16 = 8 KB)
-  static constexpr int kRawStage = kFp4RawChunks * kFp4Chunk;
-  static constexpr int kRawOffset = CSTAGES * kTokBytes;
+  static constexpr int kTokBytes = kFp4NB * kBK * 2;           // one chunk's token rows (B, 64 x 64 f16 = 8 KB)
+  static constexpr int kRawWeights = kFp4RawChunks * kFp4Chunk;   // a raw stage: the NVFP4 blocks of two chunks,
+  static constexpr int kRawStage = kRawWeights + kFp4RawChunks * kTokBytes;   // then their token rows
+  static constexpr int kRawOffset = 0;
   static constexpr int kBarOffset = kRawOffset + RSTAGES * kRawStage;
   static constexpr int kBarBytes = (2 * RSTAGES + 2 * CSTAGES + 5) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
@@ -177,10 +182,10 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < RSTAGES; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 1);
+      mbar_init(&raw_empty[s], 2);    // converter (weights read) + MMA commit (tokens read)
     }
     for (int s = 0; s < CSTAGES; ++s) {
-      mbar_init(&conv_full[s], 2);    // converter: expect-tx arrival for the tokens + arrival after writing
+      mbar_init(&conv_full[s], 1);
       mbar_init(&conv_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -211,9 +216,12 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
       // ------------------------------------------------------------------ weight producer
       uint32_t stage = 0, phase = 0, armed_mask = 0, armed_phase = 0;
       bool ok = true;
+      const uint64_t pol_t = l2_policy_evict_normal();
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
         const Fp4Tile ti = sched.tile(t);
         const uint8_t* tile_src = blocks + (static_cast<long long>(ti.group) * sp.f_tiles + ti.f) * nkb * kFp4Chunk;
+        const int bi = box_index(ti.n_valid);
+        const uint32_t tok_bytes = (16u << bi) * kBK * 2;
         for (int kb = 0; kb < nkb; kb += kFp4RawChunks) {
           const int nc = min(kFp4RawChunks, nkb - kb);
           if (!mbar_wait(&raw_empty[stage], phase ^ 1u, abort_flag, kSiteProdEmpty)) {
@@ -221,8 +229,11 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
             break;
           }
           uint8_t* st = raw + stage * L::kRawStage;
-          mbar_arrive_expect_tx(&raw_full[stage], nc * kFp4Chunk);
+          mbar_arrive_expect_tx(&raw_full[stage], nc * (kFp4Chunk + tok_bytes));
           bulk_load(st, tile_src + static_cast<long long>(kb) * kFp4Chunk, nc * kFp4Chunk, &raw_full[stage]);
+          for (int c = 0; c < nc; ++c)
+            tma_load_2d(st + L::kRawWeights + c * L::kTokBytes, &tmB.m[bi], &raw_full[stage], (kb + c) * kBK, ti.b_row,
+                        pol_t);
           armed_mask |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == RSTAGES) {
@@ -237,7 +248,7 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA issuer
-      uint32_t stage = 0, phase = 0;
+      uint32_t stage = 0, phase = 0, rstage = 0, rphase = 0;
       bool issued = false, ok = true;
       int it = 0;
       for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++it) {
@@ -248,12 +259,14 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
         tc_fence_after();
         const uint32_t d_base = tmem_base + acc * L::kAccCols;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&conv_full[stage], phase, abort_flag, kSiteMmaFull)) {
+          const int c = kb % kFp4RawChunks;   // chunk within its raw stage (tiles start on a stage boundary)
+          if (!mbar_wait(&conv_full[stage], phase, abort_flag, kSiteMmaFull) ||
+              (c == 0 && !mbar_wait(&raw_full[rstage], rphase, abort_flag, kSiteMmaFull))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(smem + stage * L::kTokBytes);            // token rows
+          const uint32_t b_addr = smem_u32(raw + rstage * L::kRawStage + L::kRawWeights + c * L::kTokBytes);
           const uint32_t a_col = tmem_base + L::kACol0 + stage * 64;                  // weight parts
 #pragma unroll
           for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
@@ -267,6 +280,13 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
           if (++stage == CSTAGES) {
             stage = 0;
             phase ^= 1u;
+          }
+          if (c == kFp4RawChunks - 1 || kb == nkb - 1) {   // the stage's tokens are read once these MMAs finish
+            mma_commit(&raw_empty[rstage]);
+            if (++rstage == RSTAGES) {
+              rstage = 0;
+              rphase ^= 1u;
+            }
           }
         }
         if (ok) mma_commit(&tfull[acc]);
@@ -282,11 +302,8 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
     const int wrow = (warp & 3) * 32 + static_cast<int>(lane);   // weight row (= TMEM lane) this thread converts
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t rstage = 0, rphase = 0, cstage = 0, cphase = 0;
-    bool live = true, armed = false;
-    uint32_t armed_stage = 0, armed_ph = 0;
+    bool live = true;
     for (int t = blockIdx.x; live && t < ntiles; t += gridDim.x) {
-      const Fp4Tile ti = sched.tile(t);
-      const int bi = box_index(ti.n_valid);
       for (int kb = 0; live && kb < nkb; kb += kFp4RawChunks) {
         const int nc = min(kFp4RawChunks, nkb - kb);
         bool ok = mbar_wait(&raw_full[rstage], rphase, abort_flag, kSiteFp4Conv);
@@ -298,14 +315,6 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
             break;
           }
           tc_fence_after();   // the MMAs that read this TMEM stage completed (conv_empty) before it is rewritten
-          uint8_t* cst = smem + cstage * L::kTokBytes;
-          if (ct == 0) {
-            mbar_arrive_expect_tx(&conv_full[cstage], (16u << bi) * kBK * 2);
-            tma_load_2d(cst, &tmB.m[bi], &conv_full[cstage], (kb + c) * kBK, ti.b_row, l2_policy_evict_normal());
-            armed = true;
-            armed_stage = cstage;
-            armed_ph = cphase;
-          }
           const uint8_t* rch = rst + c * kFp4Chunk;
 #pragma unroll
           for (int a = 0; a < 2; ++a) {
@@ -341,9 +350,6 @@ __global__ void __launch_bounds__(kFp4Threads, 1)
         }
       }
     }
-    // the token copy of the last armed stage must land before this CTA may leave (already complete
-    // unless the MMA side gave up before consuming it)
-    if (ct == 0 && armed) mbar_wait_drain(&conv_full[armed_stage], armed_ph, kSiteDrainTma);
   } else {
     // -------------------------------------------------------------------- epilogue (128 threads)
     const int quad = warp & 3;   // TMEM lanes = weight rows 32 * quad .. + 31 of both parts

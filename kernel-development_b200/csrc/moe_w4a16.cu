@@ -250,7 +250,7 @@ size_t moe_w4a16_workspace_bytes(long long T, long long H, long long I, long lon
 template <class Epi>
 static int launch_fp4w(const void* tokens, int rows, int K, const uint8_t* blocks, const Fp4Sched::Params& sp,
                        const typename Epi::Params& ep, cudaStream_t s) {
-  constexpr int RS = 8, CS = 3;   // 144 KB of NVFP4 in flight, 3 x 8 KB token stages
+  constexpr int RS = 6, CS = 4;   // 6 raw stages of 2 chunks (108 KB of NVFP4 + their 96 KB of tokens), 4 TMEM stages
   using L = Fp4Layout<RS, CS>;
   auto kern = gemm_fp4w_kernel<Fp4Sched, Epi, RS, CS>;
   static bool done[64] = {false};
