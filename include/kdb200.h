@@ -316,6 +316,33 @@ int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* t
                           void* y, int64_t t, int64_t h, int64_t i, int64_t local, int64_t e_total, int64_t k,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- */
+/* FP8-KV paged decode / verify attention                                                          */
+/* ---------------------------------------------------------------------------------------------- */
+
+/*
+ * Replaces the body of kernel_fn(data) for the reference's `muse_attention_decode` problem
+ * (src/kdev/adapters/okc_problems/muse_attention_decode.toml: shapes, tests, [comply] notes).
+ * q bf16 [batch, q_len, q_heads, head_dim]; k_new / v_new bf16 [batch, q_len, kv_heads, head_dim];
+ * k_cache / v_cache float8 e4m3 [slots, kv_heads, head_dim] (value = e4m3 * kv_scale); block_table int32
+ * [batch, max_len], the cache slot of every token (page size 1); seq_lens int32 [batch], tokens per
+ * sequence after the append (the new tokens are positions L - q_len .. L - 1, q_len <= L <= max_len).
+ * First writes the new tokens' K/V into their slots (e4m3 of value / kv_scale, nearest-even, saturating
+ * at +-448), then out bf16 [batch, q_len, q_heads, head_dim] = softmax(q K^T / sqrt(head_dim)) V per
+ * query head over its KV head's keys j <= p (p the query's position), and j > p - window when window > 0
+ * (a sliding layer: window 2048), 0 for the whole context.  head_dim == 128, q_heads % kv_heads == 0,
+ * q_len * q_heads / kv_heads <= 64.  q, caches, k_new, v_new, out 16-byte aligned; workspace >=
+ * kdb_attn_decode_workspace_bytes, 256-byte aligned.  A length or slot out of range is reported in the
+ * device status word (KDB_ERR_DEVICE_BOUNDS).  Graph capturable; no host synchronisation.
+ */
+size_t kdb_attn_decode_workspace_bytes(int64_t batch, int64_t q_len, int64_t q_heads, int64_t kv_heads,
+                                       int64_t max_len, int64_t window);
+int kdb_attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                        const int32_t* block_table, const int32_t* seq_lens, float kv_scale, void* out,
+                        int64_t batch, int64_t q_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t max_len, int64_t slots, int64_t window, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

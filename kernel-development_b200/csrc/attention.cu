@@ -1,0 +1,1018 @@
+// attention.cu — paged decode / verify attention over an FP8 E4M3 KV cache: the `muse_attention_decode` problem
+// of the reference (src/kdev/adapters/okc_problems/muse_attention_decode.toml: batch 1-48, context up to 80k
+// (1M in a test), q_len 1 (decode) or 8 (verify), sliding (2,048 keys) or full layers, page size 1, kv_scale,
+// "kernel_fn writes the new FP8 cache entries into k_cache / v_cache").
+//
+// Tensors: q [B, T, Hq, 128] bf16; k_new / v_new [B, T, Hkv, 128] bf16; k_cache / v_cache [slots, Hkv, 128] e4m3
+// (value = e4m3 x kv_scale); block_table [B, max_len] int32, the cache slot of every token (page = 1);
+// seq_lens [B] int32, tokens after the append (the new ones are positions L - T .. L - 1).  Query row
+// r = t * group + h of KV head g is query head g * group + h of token t (group = Hq / Hkv, R = T * group <= 64).
+//
+// Three launches:
+//   attn_append_kernel   the new tokens' K/V, fp8 of value / kv_scale (round to nearest even, saturating at
+//                        +-448), written into their slots;
+//   attn_fwd_kernel      persistent, warp-specialised: the tiles of 128 keys of every (sequence, KV head) form
+//                        one sequence, split evenly over the CTAs.  A producer warp gathers a tile's K and V rows
+//                        (128 B each) with TMA row gathers (tile::gather4) into a ring of stages; one thread
+//                        issues S^T = K Q^T (tcgen05 kind::f8f6f4, M = 128 keys, N = 16 / 64 query rows,
+//                        K = 128 dims, the fp8 cache read as it is stored); the softmax warps read S^T from tensor
+//                        memory (thread = key), take the tile's row maxima across the 128 keys and write P^T as
+//                        e4m3, and the MMA thread accumulates O^T += V^T P^T (M = 128 dims, V read MN-major
+//                        straight from the cache rows) in tensor memory.  Queries and probabilities go in as two
+//                        e4m3 terms each (x = hi + lo, each the nearest e4m3; the residual is about 2^-8 of x), so
+//                        the products carry about bf16 precision while both MMAs read the fp8 cache directly.  The
+//                        running maximum is raised lazily (only when a tile's maximum exceeds it by more than 2^4),
+//                        which bounds every probability by 2^8 in e4m3 and rescales O^T in tensor memory rarely.
+//                        At the end of a CTA's stretch of one (sequence, KV head) the unnormalised O, row sums and
+//                        maxima go to a partial slot;
+//   attn_merge_kernel    per query row, the partials of the CTAs that covered its keys, merged exactly.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include "gemm_sm100.cuh"
+#include "host_util.h"
+#include "sm100_common.cuh"
+
+namespace kdb {
+
+constexpr int kAttnD = 128;          // head dim
+constexpr int kAttnTile = 128;       // keys per tile = TMEM lanes of S^T
+constexpr int kAttnMaxCtas = 1024;   // partial slots reserved for CTAs (workspace bound)
+constexpr int kAttnMaxRows = 64;     // T * group
+
+enum : unsigned int {
+  kSiteAttnProdEmpty = 0x1A1,
+  kSiteAttnMmaFull = 0x1A2,
+  kSiteAttnMmaQ = 0x1A3,
+  kSiteAttnMmaSFree = 0x1A4,
+  kSiteAttnMmaP = 0x1A5,
+  kSiteAttnMmaOFree = 0x1A6,
+  kSiteAttnSoftS = 0x1A7,
+  kSiteAttnSoftPv = 0x1A8,
+  kSiteAttnDrainTma = 0x1A9,
+  kSiteAttnDrainMma = 0x1AA,
+  kSiteAttnLen = 0x1AB,
+  kSiteAttnSlot = 0x1AC,
+  kSiteAttnAppend = 0x1AD,
+  kSiteAttnMeta = 0x1AE,
+};
+
+struct AttnParams {
+  const __nv_bfloat16* q;   // [B, T, Hq, 128]
+  const int* block_table;   // [B, max_len]
+  const int* seq_lens;      // [B]
+  float score_scale;        // kv_scale / sqrt(128) * log2(e)
+  int B, T, Hq, Hkv, group, R, max_len, window;
+  long long slots;          // cache slots
+  float* part_m;            // [slot][R]  running maximum (log2 units)
+  float* part_l;            // [slot][R]  sum of probabilities
+  float* part_o;            // [slot][R][128] unnormalised output (x 1 / kv_scale)
+  int* meta;                // [B * Hkv][2]: first and last CTA of every (sequence, KV head)
+};
+
+// Length of sequence b, clamped into [T, max_len] (a length outside is reported: its attention is undefined).
+__device__ __forceinline__ int attn_len(const AttnParams& p, int b) {
+  int L = __ldg(p.seq_lens + b);
+  if (L < p.T || L > p.max_len) {
+    report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnLen);
+    L = L < p.T ? p.T : p.max_len;
+  }
+  return L;
+}
+// First key of sequence b's window union (the lowest key any of its T query rows attends).
+__device__ __forceinline__ int attn_lo(const AttnParams& p, int L) {
+  return p.window > 0 ? max(0, L - p.T - p.window + 1) : 0;
+}
+__device__ __forceinline__ int attn_tiles_of(const AttnParams& p, int L) {
+  return (L - attn_lo(p, L) + kAttnTile - 1) / kAttnTile;
+}
+
+// Walks this CTA's tiles: (sequence b, KV head g, tile) in b-major, g, tile order.
+struct AttnCursor {
+  int b, g, tile, ntiles, L, lo;
+  int remaining;   // tiles left, the current one included
+  int seg;         // segment (one (b, g) stretch) index within the CTA
+  bool seg_start, seg_end;
+
+  __device__ void load_b(const AttnParams& p) {
+    L = attn_len(p, b);
+    lo = attn_lo(p, L);
+    ntiles = (L - lo + kAttnTile - 1) / kAttnTile;
+  }
+  __device__ void init(const AttnParams& p, int b0, int g0, int t0, int count) {
+    b = b0;
+    g = g0;
+    tile = t0;
+    remaining = count;
+    seg = 0;
+    load_b(p);
+    seg_start = true;
+    seg_end = remaining == 1 || tile == ntiles - 1;
+  }
+  __device__ void next(const AttnParams& p) {
+    --remaining;
+    if (remaining <= 0) return;
+    if (++tile == ntiles) {
+      tile = 0;
+      if (++g == p.Hkv) {
+        g = 0;
+        ++b;
+        load_b(p);
+      }
+      ++seg;
+    }
+    seg_start = tile == 0;
+    seg_end = remaining == 1 || tile == ntiles - 1;
+  }
+  // Jump to the first tile of the next segment; false when this was the CTA's last segment.
+  __device__ bool next_segment(const AttnParams& p) {
+    const int left_in_seg = ntiles - tile;
+    if (remaining <= left_in_seg) return false;
+    remaining -= left_in_seg - 1;
+    tile = ntiles - 1;
+    next(p);
+    return true;
+  }
+};
+
+template <int NQ, int SPLIT, int STAGES>
+struct AttnLayout {
+  static constexpr int kSoftThreads = 128 * SPLIT;
+  static constexpr int kThreads = kSoftThreads + 64;   // + producer warp + MMA warp
+  static constexpr int kRpt = NQ / SPLIT;              // query rows per softmax thread
+  static constexpr int kKvBytes = kAttnTile * kAttnD;  // 16 KB: 128 rows of 128 B
+  static constexpr int kStageBytes = 2 * kKvBytes;     // K tile, then V tile
+  static constexpr int kQBytes = NQ * kAttnD;          // one e4m3 term of Q (or of P^T)
+  static constexpr int kQOffset = STAGES * kStageBytes;         // Q[buffer][hi, lo]
+  static constexpr int kPOffset = kQOffset + 4 * kQBytes;       // P^T[buffer][hi, lo]
+  static constexpr int kXchOffset = kPOffset + 4 * kQBytes;     // row maxima [2][NQ][4]
+  static constexpr int kLsumOffset = kXchOffset + 2 * NQ * 4 * 4;   // row sums [NQ][4]
+  static constexpr int kQcOffset = kLsumOffset + NQ * 4 * 4;        // score scale per row [2][NQ]
+  static constexpr int kBarOffset = kQcOffset + 2 * NQ * 4;
+  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2], o_free, drain
+  static constexpr int kNumBars = 2 * STAGES + 12;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;   // tmem slot, abort flag, scan scratch
+  static constexpr int kMiscInts = 48;
+  static constexpr int kSmemBytes = kMiscOffset + kMiscInts * 4 + 1024;
+  static constexpr uint32_t kTmemCols = 3 * NQ <= 64 ? 64 : (3 * NQ <= 128 ? 128 : 256);
+  // TMEM columns: S^T buffers [0, NQ) and [NQ, 2 NQ); O^T [2 NQ, 3 NQ)
+};
+
+// kind::f8f6f4, e4m3 x e4m3 -> f32, M = m, N = n; A K-major (scores) or MN-major (values), B K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n, bool a_mn_major) {
+  return (1u << 4)                                   // D format: f32
+         | (0u << 7)                                 // A format: e4m3
+         | (0u << 10)                                // B format: e4m3
+         | (a_mn_major ? (1u << 15) : 0u)            // A major
+         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+}
+
+// Descriptor of an MN-major operand stored as rows of 128 B (one row per K index, 128 e4m3 along M) with the
+// 128-byte swizzle: K groups of 8 rows 1024 B apart; M spans one 128-byte atom.
+__device__ __forceinline__ uint64_t sdesc_sw128_mnmajor(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);   // start address
+  d |= static_cast<uint64_t>(8192u >> 4) << 16;              // leading byte offset: next 128-byte M atom (unused)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;              // stride byte offset: next 8 K rows
+  d |= static_cast<uint64_t>(1u) << 46;                       // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                       // layout: 128-byte swizzle
+  return d;
+}
+
+__device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Four rows of a 2-D tensor map whose box is one row high, into 512 consecutive bytes of shared memory (the map's
+// swizzle applied as for a tile load); completion on this CTA's mbarrier.  No multicast.
+__device__ __forceinline__ void tma_gather4(void* smem_dst, const void* tmap, uint64_t* bar, int4 rows,
+                                            uint64_t cache_policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(0), "r"(rows.x), "r"(rows.y), "r"(rows.z),
+      "r"(rows.w), "l"(cache_policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void soft_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+// Named barrier of the softmax warps that also ANDs a predicate over them.
+__device__ __forceinline__ bool soft_bar_and(int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
+      : "memory");
+  return r != 0u;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float warp_max_f32(float x) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld_32x32b_x32(taddr, r);
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_st_cols<16>(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_cols<32>(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32])
+      : "memory");
+}
+
+__device__ __forceinline__ uint8_t e4m3_of(float x) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ float f32_of_e4m3(uint8_t v) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Byte offset of element (row, col) of a [rows][128 B] tile with the 128-byte swizzle (1024-byte aligned base).
+__device__ __forceinline__ int sw128_offset(int row, int col) {
+  return (row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 4) ^ row) & 7) << 4) + (col & 15);
+}
+
+// Block-wide inclusive scan over every thread of the CTA (blockDim.x a multiple of 32, at most 32 warps);
+// *total = the sum over the block.
+__device__ __forceinline__ int block_incl_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  int before = 0, all = 0;
+  for (int w = 0; w < nwarps; ++w) {
+    const int s = warp_sums[w];
+    if (w < warp) before += s;
+    all += s;
+  }
+  __syncthreads();
+  *total = all;
+  return x + before;
+}
+
+// The CTA's stretch of the global tile sequence: [t_begin, t_end) of N tiles split evenly over gridDim.x CTAs.
+// Returns the tile count; (b0, g0, t0) locate the first tile.  Every thread of the CTA takes part.
+__device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, int* t0) {
+  int* warp_sums = scratch;   // [32]
+  int* found = scratch + 32;  // [3]
+  const int tid = threadIdx.x;
+  int total = 0;
+  for (int base = 0; base < p.B; base += blockDim.x) {
+    const int b = base + tid;
+    const int v = b < p.B ? attn_tiles_of(p, attn_len(p, b)) * p.Hkv : 0;
+    int chunk;
+    block_incl_scan(v, warp_sums, &chunk);
+    total += chunk;
+  }
+  const long long n = total, c = blockIdx.x, C = gridDim.x;
+  const int t_begin = static_cast<int>(c * n / C), t_end = static_cast<int>((c + 1) * n / C);
+  if (t_end <= t_begin) return 0;
+  if (tid == 0) found[0] = -1;
+  __syncthreads();
+  int running = 0;
+  for (int base = 0; base < p.B; base += blockDim.x) {
+    const int b = base + tid;
+    const int tiles = b < p.B ? attn_tiles_of(p, attn_len(p, b)) : 0;
+    const int v = tiles * p.Hkv;
+    int chunk;
+    const int incl = block_incl_scan(v, warp_sums, &chunk);
+    const int excl = incl - v;
+    if (v > 0 && running + excl <= t_begin && t_begin < running + incl) {
+      const int off = t_begin - running - excl;
+      found[0] = b;
+      found[1] = off / tiles;
+      found[2] = off % tiles;
+    }
+    running += chunk;
+    __syncthreads();
+    if (found[0] >= 0) break;
+  }
+  *b0 = found[0];
+  *g0 = found[1];
+  *t0 = found[2];
+  return found[0] >= 0 ? t_end - t_begin : 0;
+}
+
+// Q rows of (b, g) as two e4m3 terms, scaled per row by a power of two s so that the largest |q| lands in
+// [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; qc[r] = score_scale / s.
+// Run by the softmax threads; each fences its writes for the tensor cores.
+template <int SOFT_THREADS>
+__device__ void attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* qc) {
+  const int tid = threadIdx.x;
+  const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
+  for (int base = 0; base < items; base += SOFT_THREADS) {
+    const int item = base + tid;
+    const bool active = item < items;
+    const int r = item >> 4, piece = item & 15;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = 0.f;
+    if (active) {
+      const int t = r / p.group, h = r - t * p.group;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+          p.q + ((static_cast<long long>(b) * p.T + t) * p.Hq + g * p.group + h) * kAttnD + piece * 8));
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(v2[e]);
+        x[2 * e] = f.x;
+        x[2 * e + 1] = f.y;
+      }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[e]));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (active) {
+      // power-of-two scale: amax * s in [128, 256); exponent clamped so s stays a finite normal float
+      int e2 = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
+      e2 = max(-100, min(100, e2));
+      const float s = __uint_as_float(static_cast<uint32_t>(127 + 7 - e2) << 23);
+      uint8_t hb[8], lb[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xs = x[e] * s;
+        hb[e] = e4m3_of(xs);
+        lb[e] = e4m3_of(xs - f32_of_e4m3(hb[e]));
+      }
+      const int off = sw128_offset(r, piece * 8);
+      *reinterpret_cast<uint2*>(qhi + off) = *reinterpret_cast<const uint2*>(hb);
+      *reinterpret_cast<uint2*>(qlo + off) = *reinterpret_cast<const uint2*>(lb);
+      if (piece == 0) qc[r] = p.score_scale / s;
+    }
+  }
+  fence_proxy_async_smem();
+}
+
+template <int NQ, int SPLIT, int STAGES>
+__global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                    const AttnParams p) {
+  using L = AttnLayout<NQ, SPLIT, STAGES>;
+  constexpr int RPT = L::kRpt;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* kv_empty = kv_full + STAGES;
+  uint64_t* s_full = kv_empty + STAGES;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_full = pv_done + 2;
+  uint64_t* o_free = q_full + 2;
+  uint64_t* drain = o_free + 1;
+  int* misc = reinterpret_cast<int*>(smem + L::kMiscOffset);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
+  volatile int* abort_flag = misc + 1;
+  int* scratch = misc + 8;   // 40 ints
+  float* xch = reinterpret_cast<float*>(smem + L::kXchOffset);
+  float* lsum = reinterpret_cast<float*>(smem + L::kLsumOffset);
+  float* qc = reinterpret_cast<float*>(smem + L::kQcOffset);
+  uint8_t* qtile = smem + L::kQOffset;   // [buffer][hi, lo][NQ][128]
+  uint8_t* ptile = smem + L::kPOffset;   // [buffer][hi, lo][NQ][128]
+
+  const int warp = warp_id_uniform();
+  const uint32_t lane = lane_id();
+  const int tid = threadIdx.x;
+  constexpr int kProducerWarp = L::kSoftThreads / 32;
+  constexpr int kMmaWarp = kProducerWarp + 1;
+
+  int b0 = 0, g0 = 0, t0 = 0;
+  const int count = attn_locate(p, scratch, &b0, &g0, &t0);
+  if (count == 0) return;   // uniform over the CTA: no tiles
+
+  // Q and P tiles start zero (rows R..NQ-1 stay zero); barriers; tensor memory
+  for (int i = tid; i < 8 * L::kQBytes / 16; i += L::kThreads)
+    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int u = 0; u < 2; ++u) {
+      mbar_init(&s_full[u], 1);
+      mbar_init(&s_free[u], L::kSoftThreads);
+      mbar_init(&p_full[u], L::kSoftThreads);
+      mbar_init(&pv_done[u], 1);
+      mbar_init(&q_full[u], L::kSoftThreads);
+    }
+    mbar_init(o_free, L::kSoftThreads);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------------ producer: K/V row gathers
+    const uint64_t pol = l2_policy_evict_first();
+    AttnCursor cur;
+    cur.init(p, b0, g0, t0, count);
+    uint32_t armed_mask = 0, armed_phase = 0;
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      const bool ok = mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag, kSiteAttnProdEmpty);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      // cache rows of keys k0 + 4 lane .. + 3; keys past the sequence read its last key (masked later)
+      const int k0 = cur.lo + cur.tile * kAttnTile;
+      const long long bt = static_cast<long long>(cur.b) * p.max_len;
+      const int last_slot = __ldg(p.block_table + bt + cur.L - 1);
+      int rows[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int pos = k0 + 4 * static_cast<int>(lane) + j;
+        int slot = pos < cur.L ? __ldg(p.block_table + bt + pos) : last_slot;
+        if (slot < 0 || slot >= p.slots) {
+          report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnSlot);
+          slot = 0;
+        }
+        rows[j] = slot * p.Hkv + cur.g;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
+      __syncwarp();
+      uint8_t* st = smem + s * L::kStageBytes;
+      const int4 r4 = make_int4(rows[0], rows[1], rows[2], rows[3]);
+      tma_gather4(st + lane * 512, &tm_k, &kv_full[s], r4, pol);
+      tma_gather4(st + L::kKvBytes + lane * 512, &tm_v, &kv_full[s], r4, pol);
+      armed_mask |= 1u << s;
+      armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
+    }
+    if (lane == 0)
+      for (int s = 0; s < STAGES; ++s)
+        if (armed_mask & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, kSiteAttnDrainTma);
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, NQ, false);
+      constexpr uint32_t kIdPV = idesc_e4m3_f32(128, NQ, true);
+      const uint32_t o_tmem = tmem_base + 2 * NQ;
+      AttnCursor cur;
+      cur.init(p, b0, g0, t0, count);
+      bool ok = true, issued = false;
+      int prev_i = -1, prev_seg = 0;
+      bool prev_start = false;
+      // O^T (+)= V^T P^T for tile j (after the softmax wrote P^T[j & 1]); frees the K/V stage and P buffer
+      auto issue_pv = [&](int j, int seg, bool start) -> bool {
+        const int uj = j & 1, sj = j % STAGES;
+        if (!mbar_wait(&p_full[uj], (j >> 1) & 1, abort_flag, kSiteAttnMmaP)) return false;
+        if (start && seg > 0 && !mbar_wait(o_free, (seg - 1) & 1, abort_flag, kSiteAttnMmaOFree)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + sj * L::kStageBytes + L::kKvBytes);
+        const uint32_t ph_addr = smem_u32(ptile + (2 * uj) * L::kQBytes);
+        const uint32_t pl_addr = ph_addr + L::kQBytes;
+#pragma unroll
+        for (int ks = 0; ks < kAttnTile / 32; ++ks)
+          mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(ph_addr + ks * 32), kIdPV,
+                   (start && ks == 0) ? 0u : 1u);
+#pragma unroll
+        for (int ks = 0; ks < kAttnTile / 32; ++ks)
+          mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(pl_addr + ks * 32), kIdPV,
+                   1u);
+        mma_commit(&kv_empty[sj]);
+        mma_commit(&pv_done[uj]);
+        return true;
+      };
+      for (int i = 0; ok && cur.remaining > 0; ++i, cur.next(p)) {
+        const int s = i % STAGES, u = i & 1;
+        if (!mbar_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
+        if (cur.seg_start && !mbar_wait(&q_full[cur.seg & 1], (cur.seg >> 1) & 1, abort_flag, kSiteAttnMmaQ)) break;
+        if (!mbar_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + s * L::kStageBytes);
+        const uint32_t qh_addr = smem_u32(qtile + (2 * (cur.seg & 1)) * L::kQBytes);
+        const uint32_t ql_addr = qh_addr + L::kQBytes;
+        const uint32_t s_tmem = tmem_base + u * NQ;
+#pragma unroll
+        for (int ks = 0; ks < kAttnD / 32; ++ks)
+          mma_e4m3(s_tmem, sdesc_sw128_kmajor(k_addr + ks * 32), sdesc_sw128_kmajor(qh_addr + ks * 32), kIdQK,
+                   ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < kAttnD / 32; ++ks)
+          mma_e4m3(s_tmem, sdesc_sw128_kmajor(k_addr + ks * 32), sdesc_sw128_kmajor(ql_addr + ks * 32), kIdQK, 1u);
+        mma_commit(&s_full[u]);
+        issued = true;
+        if (prev_i >= 0 && !issue_pv(prev_i, prev_seg, prev_start)) {
+          ok = false;
+          break;
+        }
+        prev_i = i;
+        prev_seg = cur.seg;
+        prev_start = cur.seg_start;
+      }
+      if (ok && prev_i >= 0 && !*abort_flag) issue_pv(prev_i, prev_seg, prev_start);
+      if (issued) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, kSiteAttnDrainMma);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax / epilogue warps
+    const int quad = warp & 3, rs = warp >> 2;   // TMEM lanes [32 quad, +32); rows [rs RPT, +RPT)
+    const int key = quad * 32 + static_cast<int>(lane);   // S^T lane = key of the tile; O^T lane = dim
+    const int r0 = rs * RPT;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    constexpr float kTau = 4.f;     // raise the running maximum only past +2^4
+    constexpr float kPShift = 4.f;  // probabilities scaled by 2^(8 - tau): at most 2^8 in e4m3
+
+    AttnCursor qcur;
+    qcur.init(p, b0, g0, t0, count);
+    attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile, qtile + L::kQBytes, qc);
+    mbar_arrive(&q_full[0]);
+    bool q_more = qcur.next_segment(p);
+    if (q_more) {
+      attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile + 2 * L::kQBytes, qtile + 3 * L::kQBytes, qc + NQ);
+      mbar_arrive(&q_full[1]);
+    }
+
+    AttnCursor cur;
+    cur.init(p, b0, g0, t0, count);
+    float m_used[RPT], l_lane[RPT];
+#pragma unroll
+    for (int j = 0; j < RPT; ++j) {
+      m_used[j] = -INFINITY;
+      l_lane[j] = 0.f;
+    }
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int u = i & 1;
+      const int bg = cur.b * p.Hkv + cur.g;
+      if (cur.seg_start) {
+        // segment j >= 1 begins: the Q buffer of segment j - 1 is free (its score MMAs completed), so prepare
+        // segment j + 1's queries there
+        if (cur.seg >= 1 && q_more) {
+          q_more = qcur.next_segment(p);
+          if (q_more) {
+            const int qb = (cur.seg + 1) & 1;
+            attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile + 2 * qb * L::kQBytes,
+                                            qtile + (2 * qb + 1) * L::kQBytes, qc + qb * NQ);
+            mbar_arrive(&q_full[qb]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) {
+          m_used[j] = -INFINITY;
+          l_lane[j] = 0.f;
+        }
+        if (tid == 0 && cur.tile == 0) p.meta[bg * 2] = blockIdx.x;
+      }
+      // ---- scores of this thread's key for its rows (log2 units), masked
+      bool ok = mbar_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS);
+      if (!soft_bar_and(L::kSoftThreads, ok)) break;
+      tc_fence_after();
+      uint32_t acc[RPT];
+      tmem_ld_cols<RPT>(lane_addr + u * NQ + r0, acc);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_free[u]);
+      const float* qcs = qc + (cur.seg & 1) * NQ;
+      const int pos = cur.lo + cur.tile * kAttnTile + key;
+      const int new0 = cur.L - p.T;
+      float x[RPT];
+#pragma unroll
+      for (int j = 0; j < RPT; ++j) {
+        const int r = r0 + j;
+        float v = -INFINITY;
+        if (r < p.R) {
+          const int qpos = new0 + r / p.group;
+          const bool keep = pos <= qpos && (p.window == 0 || pos > qpos - p.window);
+          if (keep) v = __uint_as_float(acc[j]) * qcs[r];
+        }
+        x[j] = v;
+      }
+      // ---- tile maxima over the 128 keys: warp redux, then the four quads through shared memory
+      float* xc = xch + (i & 1) * NQ * 4;
+#pragma unroll
+      for (int j = 0; j < RPT; ++j) {
+        const float wm = warp_max_f32(x[j]);
+        if (static_cast<int>(lane) == (j & 31)) xc[(r0 + j) * 4 + quad] = wm;
+      }
+      soft_bar_sync(L::kSoftThreads);
+      float f[RPT];
+      bool rescale = false;
+#pragma unroll
+      for (int j = 0; j < RPT; ++j) {
+        const float4 t4 = *reinterpret_cast<const float4*>(xc + (r0 + j) * 4);
+        const float tmax = fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w));
+        f[j] = 1.f;
+        if (m_used[j] == -INFINITY) {
+          m_used[j] = tmax;   // first keys of this row in the segment: its O^T column is still zero
+        } else if (tmax > m_used[j] + kTau) {
+          f[j] = fast_exp2(m_used[j] - tmax);
+          m_used[j] = tmax;
+          rescale = true;
+        }
+      }
+      // every softmax thread saw the same maxima; with SPLIT = 2 the two row halves decide apart, so agree here
+      if (SPLIT > 1) rescale = !soft_bar_and(L::kSoftThreads, !rescale);
+      if (rescale) {
+        // O^T of the tiles so far (PV of tile i - 1 included) times f, per row
+        const int j1 = i - 1;
+        ok = mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag, kSiteAttnSoftPv);
+        if (!soft_bar_and(L::kSoftThreads, ok)) break;
+        tc_fence_after();
+        uint32_t o[RPT];
+        tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
+        tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+        tmem_st_wait();
+      }
+      // ---- probabilities (x 2^(8 - tau)) as two e4m3 terms into P^T[u]; rows >= R stay zero
+      if (i >= 2) {
+        const int j2 = i - 2;
+        ok = mbar_wait(&pv_done[u], (j2 >> 1) & 1, abort_flag, kSiteAttnSoftPv);
+        if (!soft_bar_and(L::kSoftThreads, ok)) break;
+      }
+      uint8_t* ph = ptile + (2 * u) * L::kQBytes;
+      uint8_t* pl = ph + L::kQBytes;
+#pragma unroll
+      for (int j = 0; j < RPT; ++j) {
+        const int r = r0 + j;
+        if (r < p.R) {
+          l_lane[j] *= f[j];
+          float pv = 0.f;
+          if (x[j] != -INFINITY) pv = fast_exp2(x[j] - m_used[j] + kPShift);
+          const uint8_t hb = e4m3_of(pv);
+          const float hf = f32_of_e4m3(hb);
+          const uint8_t lb = e4m3_of(pv - hf);
+          l_lane[j] += hf + f32_of_e4m3(lb);
+          const int off = sw128_offset(r, key);
+          ph[off] = hb;
+          pl[off] = lb;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[u]);
+
+      if (cur.seg_end) {
+        // ---- this segment's partial: O^T columns (thread = dim), row sums, maxima
+        ok = mbar_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv);
+        if (!soft_bar_and(L::kSoftThreads, ok)) break;
+        tc_fence_after();
+        uint32_t o[RPT];
+        tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(o_free);
+        const long long slot = static_cast<long long>(blockIdx.x) + bg;
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) {
+          const int r = r0 + j;
+          float ls = l_lane[j];
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+          if (r < p.R) {
+            p.part_o[(slot * p.R + r) * kAttnD + key] = __uint_as_float(o[j]);
+            if (lane == 0) lsum[r * 4 + quad] = ls;
+          }
+        }
+        soft_bar_sync(L::kSoftThreads);
+        if (quad == 0) {
+#pragma unroll
+          for (int j = 0; j < RPT; ++j) {
+            const int r = r0 + j;
+            if (r < p.R && static_cast<int>(lane) == (j & 31)) {
+              const float4 l4 = *reinterpret_cast<const float4*>(lsum + r * 4);
+              p.part_l[slot * p.R + r] = (l4.x + l4.y) + (l4.z + l4.w);
+              p.part_m[slot * p.R + r] = m_used[j];
+            }
+          }
+        }
+        if (tid == 0 && cur.tile == cur.ntiles - 1) p.meta[bg * 2 + 1] = blockIdx.x;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// append: one warp per new (sequence, token, KV head) row, four values per lane
+// ---------------------------------------------------------------------------------------------
+struct AttnAppendParams {
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  const int* block_table;
+  const int* seq_lens;
+  float kv_scale;
+  int B, T, Hkv, max_len;
+  long long slots;
+};
+
+__global__ void __launch_bounds__(128) attn_append_kernel(const AttnAppendParams a) {
+  const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= static_cast<long long>(a.B) * a.T * a.Hkv) return;
+  const int g = static_cast<int>(row % a.Hkv);
+  const long long bt = row / a.Hkv;
+  const int t = static_cast<int>(bt % a.T), b = static_cast<int>(bt / a.T);
+  int L = __ldg(a.seq_lens + b);
+  L = L < a.T ? a.T : (L > a.max_len ? a.max_len : L);   // an out-of-range length is reported by attn_fwd_kernel
+  const int slot = __ldg(a.block_table + static_cast<long long>(b) * a.max_len + L - a.T + t);
+  if (slot < 0 || slot >= a.slots) {
+    if (lane == 0) report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnAppend);
+    return;
+  }
+  const long long src = row * kAttnD + lane * 4;
+  const long long dst = (static_cast<long long>(slot) * a.Hkv + g) * kAttnD + lane * 4;
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const __nv_bfloat16* x = (w == 0 ? a.k_new : a.v_new) + src;
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(x));
+    const __nv_bfloat16* xv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      packed |= static_cast<uint32_t>(e4m3_of(__fdiv_rn(__bfloat162float(xv[e]), a.kv_scale))) << (8 * e);
+    *reinterpret_cast<uint32_t*>((w == 0 ? a.k_cache : a.v_cache) + dst) = packed;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// merge: one CTA (8 warps) per (sequence, KV head, query row); warp w takes the partials of CTAs c0 + w, + 8, ...
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    attn_merge_kernel(const AttnParams p, int ctas, float kv_scale, __nv_bfloat16* __restrict__ out) {
+  __shared__ float sm_m[8], sm_l[8];
+  __shared__ __align__(16) float sm_o[8][kAttnD];
+  const int r = blockIdx.x % p.R;
+  const int bg = blockIdx.x / p.R;
+  const int g = bg % p.Hkv, b = bg / p.Hkv;
+  const int t = r / p.group, h = r - t * p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int c0 = p.meta[bg * 2], c1 = p.meta[bg * 2 + 1];
+  if (c0 < 0 || c1 >= ctas || c0 > c1) {
+    if (threadIdx.x == 0) report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnMeta);
+    c0 = 0;
+    c1 = -1;
+  }
+  float m = -INFINITY, l = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = c0 + warp; c <= c1; c += 8) {
+    const long long slot = static_cast<long long>(c) + bg;
+    const float mk = p.part_m[slot * p.R + r];
+    if (mk == -INFINITY) continue;
+    const float lk = p.part_l[slot * p.R + r];
+    const float4 ok = *reinterpret_cast<const float4*>(p.part_o + (slot * p.R + r) * kAttnD + lane * 4);
+    const float mn = fmaxf(m, mk);
+    const float a = fast_exp2(m - mn), w = fast_exp2(mk - mn);
+    l = l * a + lk * w;
+    acc.x = acc.x * a + ok.x * w;
+    acc.y = acc.y * a + ok.y * w;
+    acc.z = acc.z * a + ok.z * w;
+    acc.w = acc.w * a + ok.w * w;
+    m = mn;
+  }
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = l;
+  }
+  *reinterpret_cast<float4*>(&sm_o[warp][lane * 4]) = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, sm_m[w]);
+    float lt = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        if (sm_m[w] == -INFINITY) continue;
+        const float s = fast_exp2(sm_m[w] - M);
+        lt += sm_l[w] * s;
+        const float4 ow = *reinterpret_cast<const float4*>(&sm_o[w][lane * 4]);
+        o.x += ow.x * s;
+        o.y += ow.y * s;
+        o.z += ow.z * s;
+        o.w += ow.w * s;
+      }
+    }
+    const float k = lt > 0.f ? kv_scale / lt : 0.f;
+    __nv_bfloat16* dst = out + ((static_cast<long long>(b) * p.T + t) * p.Hq + g * p.group + h) * kAttnD + lane * 4;
+    const __nv_bfloat162 lo2 = __floats2bfloat162_rn(o.x * k, o.y * k);
+    const __nv_bfloat162 hi2 = __floats2bfloat162_rn(o.z * k, o.w * k);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo2);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi2);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------------------------
+static long long attn_max_tiles(long long B, long long T, long long Hkv, long long max_len, long long window) {
+  const long long span = window > 0 ? (window + T - 1 < max_len ? window + T - 1 : max_len) : max_len;
+  return B * Hkv * ((span + kAttnTile - 1) / kAttnTile);
+}
+
+int attn_check(long long B, long long T, long long Hq, long long Hkv, long long D, long long max_len, long long slots,
+               long long window) {
+  if (B < 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || max_len < 0 || slots < 0 || window < 0) return KDB_ERR_INVALID_ARG;
+  if (D != kAttnD || Hq % Hkv != 0 || T * (Hq / Hkv) > kAttnMaxRows) return KDB_ERR_UNSUPPORTED;
+  if (B > 0 && (max_len < T || slots <= 0)) return KDB_ERR_INVALID_ARG;
+  if (B > (1ll << 24) || window > (1ll << 30) || max_len >= (1ll << 31) ||
+      attn_max_tiles(B, T, Hkv, max_len, window) >= (1ll << 30) || slots * Hkv >= (1ll << 31))
+    return KDB_ERR_UNSUPPORTED;
+  return KDB_OK;
+}
+
+static int attn_ctas_bound(long long B, long long T, long long Hkv, long long max_len, long long window) {
+  const long long n = attn_max_tiles(B, T, Hkv, max_len, window);
+  return static_cast<int>(n < kAttnMaxCtas ? n : kAttnMaxCtas);
+}
+
+size_t attn_workspace_bytes(long long B, long long T, long long Hq, long long Hkv, long long max_len,
+                            long long window) {
+  if (attn_check(B, T, Hq, Hkv, kAttnD, max_len, 1, window) != KDB_OK || B == 0) return 0;
+  const long long R = T * (Hq / Hkv);
+  const long long nslots = attn_ctas_bound(B, T, Hkv, max_len, window) + B * Hkv;
+  const size_t fbytes = (static_cast<size_t>(nslots) * R * (2 + kAttnD) * sizeof(float) + 255) / 256 * 256;
+  return fbytes + static_cast<size_t>(B * Hkv * 2) * sizeof(int);
+}
+
+template <int NQ, int SPLIT, int STAGES>
+static int attn_launch_fwd(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, long long max_tiles,
+                           int* ctas_out, cudaStream_t s) {
+  using L = AttnLayout<NQ, SPLIT, STAGES>;
+  auto kern = attn_fwd_kernel<NQ, SPLIT, STAGES>;
+  static int occ[64] = {0};
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev));
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return KDB_ERR_UNSUPPORTED;
+  if (occ[dev] == 0) {
+    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes));
+    if (rc) return rc;
+    int o = 0;
+    rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, L::kThreads, L::kSmemBytes));
+    if (rc) return rc;
+    occ[dev] = o > 0 ? o : 1;
+  }
+  // small jobs: one tile per CTA; larger ones: at least four tiles per CTA, at most one wave of resident CTAs
+  const long long resident = static_cast<long long>(num_sms()) * occ[dev];
+  long long c = max_tiles <= 32 ? max_tiles : (max_tiles + 3) / 4;
+  if (max_tiles > 32 && c < 32) c = 32;
+  if (c > resident) c = resident;
+  if (c > kAttnMaxCtas) c = kAttnMaxCtas;
+  if (c < 1) c = 1;
+  *ctas_out = static_cast<int>(c);
+  kern<<<static_cast<unsigned int>(c), L::kThreads, L::kSmemBytes, s>>>(tk, tv, p);
+  return cuda_status(cudaGetLastError());
+}
+
+int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                    const int* block_table, const int* seq_lens, float kv_scale, void* out, long long B, long long T,
+                    long long Hq, long long Hkv, long long D, long long max_len, long long slots, long long window,
+                    void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  int rc = attn_check(B, T, Hq, Hkv, D, max_len, slots, window);
+  if (rc) return rc;
+  if (B == 0) return KDB_OK;
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !block_table || !seq_lens || !out) return KDB_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(k_new) || !aligned16(v_new) ||
+      !aligned16(out) || (reinterpret_cast<uintptr_t>(block_table) & 3u) || (reinterpret_cast<uintptr_t>(seq_lens) & 3u))
+    return KDB_ERR_INVALID_ARG;
+  if (!(kv_scale > 0.f) || !(kv_scale < INFINITY)) return KDB_ERR_INVALID_ARG;
+  const size_t need = attn_workspace_bytes(B, T, Hq, Hkv, max_len, window);
+  if (!workspace || workspace_bytes < need) return KDB_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return KDB_ERR_INVALID_ARG;
+
+  const long long group = Hq / Hkv, R = T * group;
+  const long long max_tiles = attn_max_tiles(B, T, Hkv, max_len, window);
+  const long long nslots = attn_ctas_bound(B, T, Hkv, max_len, window) + B * Hkv;
+  AttnParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.score_scale = kv_scale * (1.0f / sqrtf(static_cast<float>(kAttnD))) * 1.4426950408889634f;
+  p.B = static_cast<int>(B);
+  p.T = static_cast<int>(T);
+  p.Hq = static_cast<int>(Hq);
+  p.Hkv = static_cast<int>(Hkv);
+  p.group = static_cast<int>(group);
+  p.R = static_cast<int>(R);
+  p.max_len = static_cast<int>(max_len);
+  p.window = static_cast<int>(window);
+  p.slots = slots;
+  float* f = static_cast<float*>(workspace);
+  p.part_m = f;
+  p.part_l = f + nslots * R;
+  p.part_o = f + 2 * nslots * R;
+  const size_t fbytes = (static_cast<size_t>(nslots) * R * (2 + kAttnD) * sizeof(float) + 255) / 256 * 256;
+  p.meta = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + fbytes);
+
+  CUtensorMap tk, tv;   // the caches as [slots * Hkv] rows of 128 B (a bf16 view of 64 elements), one-row boxes
+  rc = make_tmap_bf16_2d(&tk, k_cache, 64, static_cast<uint64_t>(slots * Hkv), 64, 64, 1);
+  if (rc) return rc;
+  rc = make_tmap_bf16_2d(&tv, v_cache, 64, static_cast<uint64_t>(slots * Hkv), 64, 64, 1);
+  if (rc) return rc;
+
+  AttnAppendParams a;
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.k_cache = static_cast<uint8_t*>(k_cache);
+  a.v_cache = static_cast<uint8_t*>(v_cache);
+  a.block_table = block_table;
+  a.seq_lens = seq_lens;
+  a.kv_scale = kv_scale;
+  a.B = p.B;
+  a.T = p.T;
+  a.Hkv = p.Hkv;
+  a.max_len = p.max_len;
+  a.slots = slots;
+  const long long rows = B * T * Hkv;
+  attn_append_kernel<<<static_cast<unsigned int>((rows + 3) / 4), 128, 0, s>>>(a);
+  rc = cuda_status(cudaGetLastError());
+  if (rc) return rc;
+
+  int ctas = 0;
+  rc = R <= 16 ? attn_launch_fwd<16, 1, 6>(tk, tv, p, max_tiles, &ctas, s)
+               : attn_launch_fwd<64, 2, 4>(tk, tv, p, max_tiles, &ctas, s);
+  if (rc) return rc;
+  attn_merge_kernel<<<static_cast<unsigned int>(B * Hkv * R), 256, 0, s>>>(p, ctas, kv_scale,
+                                                                           static_cast<__nv_bfloat16*>(out));
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace kdb

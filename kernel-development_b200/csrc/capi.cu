@@ -11,6 +11,12 @@
 namespace kdb {
 cudaError_t last_cuda_error();
 int selftest_wait_timeout(unsigned long long limit_ns, cudaStream_t s);
+size_t attn_workspace_bytes(long long B, long long T, long long Hq, long long Hkv, long long max_len,
+                            long long window);
+int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                    const int* block_table, const int* seq_lens, float kv_scale, void* out, long long B, long long T,
+                    long long Hq, long long Hkv, long long D, long long max_len, long long slots, long long window,
+                    void* workspace, size_t workspace_bytes, cudaStream_t s);
 }  // namespace kdb
 
 extern "C" {
@@ -290,6 +296,21 @@ int kdb_moe_w4a16_forward(const void* x, const int32_t* topk_ids, const float* t
                           void* workspace, size_t workspace_bytes, void* stream) {
   return kdb::moe_w4a16_forward(x, topk_ids, topk_w, w13_blocks, w13_gscale, w2_blocks, w2_gscale, pw1, y, t, h, i,
                                 local, e_total, k, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t kdb_attn_decode_workspace_bytes(int64_t batch, int64_t q_len, int64_t q_heads, int64_t kv_heads,
+                                       int64_t max_len, int64_t window) {
+  return kdb::attn_workspace_bytes(batch, q_len, q_heads, kv_heads, max_len, window);
+}
+
+int kdb_attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                        const int32_t* block_table, const int32_t* seq_lens, float kv_scale, void* out,
+                        int64_t batch, int64_t q_len, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t max_len, int64_t slots, int64_t window, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  return kdb::attn_decode_fp8(q, k_new, v_new, k_cache, v_cache, block_table, seq_lens, kv_scale, out, batch, q_len,
+                              q_heads, kv_heads, head_dim, max_len, slots, window, workspace, workspace_bytes,
+                              static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -85,10 +85,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
                : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // All 128 converter threads agree on `ok` (named barrier 5).
 __device__ __forceinline__ bool conv_vote_all(bool ok) {
   uint32_t bad = ok ? 0u : 1u, any;
@@ -136,8 +132,6 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
-
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // D[tmem] (+)= A[tmem] * B[smem]: A is M = 128 lanes x K = 16 (eight 32-bit columns of packed f16 pairs).
 __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,

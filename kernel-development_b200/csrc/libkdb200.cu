@@ -10,4 +10,5 @@
 #include "moe_noalloc.cu"
 #include "moe_w4a16.cu"
 #include "selftest.cu"
+#include "attention.cu"
 #include "capi.cu"

@@ -39,6 +39,8 @@ SIGNATURES: dict[str, tuple] = {
     "kdb_set_sm_budget": (_c_int, [ctypes.c_int32]),
     "kdb_moe_w4a16_workspace_bytes": (_c_size, [_c_i64] * 6),
     "kdb_moe_w4a16_forward": (_c_int, [_c_vp] * 9 + [_c_i64] * 6 + [_c_vp, _c_size, _c_vp]),
+    "kdb_attn_decode_workspace_bytes": (_c_size, [_c_i64] * 6),
+    "kdb_attn_decode_fp8": (_c_int, [_c_vp] * 7 + [ctypes.c_float, _c_vp] + [_c_i64] * 8 + [_c_vp, _c_size, _c_vp]),
     "kdb_sm_budget": (_c_int, []),
     "kdb_proj_split_f32": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_vp]),
     "kdb_proj_f32w_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64]),

@@ -95,7 +95,7 @@ def test_w4a16_forward_passes_checks(fake_device):
     y = W4.forward(W.moe_input(cfg.t, cfg.h, 1), ids.t().contiguous().t(), tw, state, cfg.e_total)
     assert y.shape == (cfg.t, cfg.h)
     name, args = fake_device.calls[-1]
-    assert name == "kdb_moe_w4a16_forward" and args[8:14] == (cfg.t, cfg.h, cfg.i, cfg.local, cfg.e_total, cfg.k)
+    assert name == "kdb_moe_w4a16_forward" and args[9:15] == (cfg.t, cfg.h, cfg.i, cfg.local, cfg.e_total, cfg.k)
 
 
 def test_projection_ops_pass_checks(fake_device):
@@ -107,3 +107,35 @@ def test_projection_ops_pass_checks(fake_device):
     y32 = P.proj_f32w(x, split)
     assert y32.shape == (16, 64) and y32.dtype == torch.float32
     assert _names(fake_device)[-1] == "kdb_proj_f32w"
+
+
+@pytest.mark.parametrize("case", [dict(batch=2, ctx=300, heads="tp8", layer="sliding"),
+                                  dict(batch=3, ctx=200, heads="dp", layer="full", q_len=8)])
+def test_attention_decode_passes_checks(fake_device, case):
+    from kdb200 import attention as A
+    from oracle import attention as OA
+    d = OA.generate_input(case, 3)
+    out = A.decode(d["q"], d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], d["block_table"], d["seq_lens"],
+                   d["kv_scale"], A.window_of(case["layer"]))
+    assert out.shape == d["q"].shape and out.dtype == torch.bfloat16
+    name, args = fake_device.calls[-1]
+    B, T, Hq, _ = d["q"].shape
+    assert name == "kdb_attn_decode_fp8"
+    assert args[7] == d["kv_scale"] and args[9:17] == (B, T, Hq, d["k_cache"].shape[1], 128,
+                                                       d["block_table"].shape[1], d["k_cache"].shape[0],
+                                                       A.window_of(case["layer"]))
+
+
+def test_attention_decode_rejects_bad_arguments(fake_device):
+    from kdb200 import attention as A
+    from oracle import attention as OA
+    d = OA.generate_input(dict(batch=1, ctx=50), 1)
+    args = [d["q"], d["k_new"], d["v_new"], d["k_cache"], d["v_cache"], d["block_table"], d["seq_lens"]]
+    with pytest.raises(TypeError):
+        A.decode(d["q"].float(), *args[1:])
+    with pytest.raises(TypeError):
+        A.decode(*args[:3], d["k_cache"].view(torch.uint8), *args[4:])
+    with pytest.raises(ValueError):
+        A.decode(*args[:5], d["block_table"].repeat(2, 1), d["seq_lens"])
+    with pytest.raises(ValueError):
+        A.window_of("local")

@@ -110,3 +110,40 @@ def test_moe_problem_check_through_kdev(okc, tmp_path, monkeypatch):
     ids[0, 0] = (ids[0, 0] + 1) % small.e
     res2 = a.check(data, (ref["y"], ref["w"], ids))
     assert not res2.ok and "mismatched 1" in res2.message
+
+
+CPU_ATTN_SUB = textwrap.dedent('''\
+    # CPU stand-in with the submission's entry point (the real one launches libkdb200 kernels)
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import attention as oa
+    def kernel_fn(data):
+        kc, vc = oa.append_kv(data)
+        data["k_cache"].copy_(kc)
+        data["v_cache"].copy_(vc)
+        return oa.attention_ref(data).to(data["q"].dtype)
+    ''')
+
+
+def test_attention_problem_through_kdev(okc, tmp_path):
+    """The attention problem (kernel_fn(data), check through collect): an oracle stand-in passes, an output
+    off by 10 % fails, and a cache without the appended entries fails."""
+    a = okc.OkcAdapter(str(PROBLEMS / "b200_attention_decode"), str(PROBLEMS / "b200_attention_decode.toml"))
+    assert a.problem == "b200_attention_decode" and a.kernel_fn_args() == 1
+    assert [s.shape_id for s in a.tests()][:3] == ["t0", "t1", "t2"]
+    sub = tmp_path / "cpu_attn_sub.py"
+    sub.write_text(CPU_ATTN_SUB.replace("ROOT", repr(str(ROOT))))
+    mod = a.load(str(sub), "cpu_attn")
+    shape = a.tests()[0]
+    data = a.make_inputs(shape, seed=5)
+    if data["q"].is_cuda:
+        pytest.skip("CPU-only test")
+    out = a.call(mod, None, data)
+    res = a.check(data, out)
+    assert res.ok, res.message
+    assert not a.check(data, out * 1.1).ok
+    fresh = a.make_inputs(shape, seed=5)
+    bad = a.check(fresh, out)           # caches without the new entries
+    assert not bad.ok and "k_cache" in bad.message
+    real = a.load(str(SUBS / "b200_attention_decode.py"), "real_attn")
+    assert callable(real.kernel_fn)

@@ -90,3 +90,9 @@ def test_w4a16_submission_passes_kdev_check(kdev, monkeypatch):
              shapes=lambda a: [s for s in a.tests() if s.case.get("bs", 0) <= 64])
     _fresh_references()
     torch.cuda.synchronize()
+
+
+def test_attention_submission_passes_kdev_check(kdev):
+    okc, check = kdev
+    _run_all(okc, check, "b200_attention_decode", "b200_attention_decode.py",
+             shapes=lambda a: [s for s in a.tests() if s.case["ctx"] <= 9000 and s.case["batch"] <= 8])
