@@ -573,6 +573,14 @@ def run_reference(args, dist) -> dict | None:
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": _proj_config(cfg, world, args.workload),
             "cpu_baseline": b, "e2e": {"value": b["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                                        "d2h_bytes_per_step": 0}}
+    if args.workload.startswith("attn"):
+        b = cpu_baseline_attn(args.workload, steps=n)
+        case, _ = W.ATTN_CONFIGS[args.workload]
+        return {"impl": "reference", "metric": ATTN_METRIC, "value": b["value"], "unit": "keys/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.workload, **case}, "cpu_baseline": b,
+                "e2e": {"value": b["value"], "unit": "keys/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if args.workload.startswith("w4a16"):
         b = cpu_baseline_w4a16(args.workload, steps=n)
         config = {"workload": args.workload}
@@ -683,6 +691,111 @@ def cpu_baseline_w4a16(workload: str, steps: int = 3) -> dict:
                       f"oracle/moe_w4a16.py, median of {len(rates)}"}
 
 
+# ------------------------------------------------------------------------------------------------ attention
+ATTN_METRIC = "cached keys attended per second (keys x KV heads / s)"
+
+
+def _attn_inputs(workload: str, device):
+    from kdb200 import attention as A
+    from kdb200 import workloads as W
+    from oracle import attention as OA
+    case, seed = W.ATTN_CONFIGS[workload]
+    data = OA.generate_input(case, seed)
+    window = A.window_of(case["layer"])
+    return case, data, window, W.attn_keys(data, window)
+
+
+def cpu_baseline_attn(workload: str, steps: int = 3) -> dict:
+    """The oracle (oracle/attention.py: fp32 einsum over the appended cache) on the host cores, on the first
+    sequence of the workload's batch (a bounded sample), in the same unit."""
+    from kdb200 import workloads as W
+    from oracle import attention as OA
+    cores = _cpu_threads()
+    case, data, window, _ = _attn_inputs(workload, "cpu")
+    one = {k: (v[:1] if isinstance(v, torch.Tensor) and k not in ("k_cache", "v_cache") else v)
+           for k, v in data.items()}
+    one["k_cache"], one["v_cache"] = data["k_cache"], data["v_cache"]
+    keys = W.attn_keys(one, window)
+    rates = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        OA.attention_ref(one)
+        rates.append(keys / (time.perf_counter() - t0))
+    return {"value": round(statistics.median(rates), 1), "unit": "keys/s", "cores": cores, "kind": "port",
+            "sample": f"sequence 0 of {case['batch']} ({keys} keys x KV heads), oracle/attention.py attention_ref "
+                      f"(append + fp32 einsum softmax), median of {len(rates)}"}
+
+
+def bench_attn(args, dist: Dist) -> dict | None:
+    """FP8-KV paged decode / verify attention, one call per step (append + attention + merge), one GPU."""
+    from kdb200 import attention as A
+    if dist.world > 1:
+        raise SystemExit("attention workloads run on one GPU (replicas only): use --gpus 1")
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    case, data, window, keys = _attn_inputs(args.workload, dev)
+    g = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in data.items()}
+    flush = _flusher(dev)
+    holder = {}
+    sampler = ClockSampler(_physical_index(dist.local))
+
+    def call(q, kn, vn, bt, sl):
+        return A.decode(q, kn, vn, g["k_cache"], g["v_cache"], bt, sl, data["kv_scale"], window)
+
+    def step():
+        holder["out"] = call(g["q"], g["k_new"], g["v_new"], g["block_table"], g["seq_lens"])
+
+    run_step = _capture(step).replay
+    per_step, region_ms = timed_steps(run_step, args.steps, args.warmup, flush, dist, sampler)
+    ms = statistics.mean(per_step)
+    # the attention kernel alone, on the same stream (events around it inside an eager call are not possible
+    # without splitting the op, so time the whole call and report the kernel share from the ncu launch list)
+    T = data["q"].shape[1]
+    small = data["q"].numel() * 2 * 2 + data["k_new"].numel() * 2 * 2 + data["k_new"].numel() * 2
+    nbytes = keys * 256 + small + data["block_table"].numel() * 4
+    host = {k: g[k].cpu().pin_memory() for k in ("q", "k_new", "v_new", "block_table", "seq_lens")}
+    devbuf = {k: torch.empty_like(g[k]) for k in host}
+    out_host = torch.empty(tuple(data["q"].shape), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for k in host:
+            devbuf[k].copy_(host[k], non_blocking=True)
+        out_host.copy_(call(devbuf["q"], devbuf["k_new"], devbuf["v_new"], devbuf["block_table"],
+                            devbuf["seq_lens"]), non_blocking=True)
+
+    e2e_steps, _ = timed_steps(e2e_step, max(3, args.steps // 4), 3, flush, dist, None)
+    e2e_ms = statistics.mean(e2e_steps)
+    h2d = sum(int(v.numel() * v.element_size()) for v in host.values())
+    peaks = _peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": ATTN_METRIC, "value": round(keys / (ms * 1e-3), 1), "unit": "keys/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 cache x (q, p as two e4m3 terms), fp32 acc",
+        "data": "synthetic (seeded oracle/attention.py generator; the reference problem's case and seed)",
+        "config": {"workload": args.workload, **case, "window": window, "keys_x_kv_heads": keys,
+                   "parallelism": "1 GPU (replicas only)",
+                   "l2": "flushed before every timed step (512 MiB device write then read, untimed)",
+                   "graph": "CUDA graph replay per step"},
+        "e2e": {"value": round(keys / (e2e_ms * 1e-3), 1), "unit": "keys/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": int(out_host.numel() * 2), "ms_per_step": round(e2e_ms, 5),
+                "path": "kdb200.attention.decode -> kdb_attn_decode_fp8 (q, k_new, v_new, block_table, seq_lens "
+                        "copied in; the cache stays resident)"},
+        "gpu_launches": 3 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": f"{peaks['source']} (burst)",
+                     "kernel": "whole call (append, attention, merge); bytes = 256 B per cached key and KV head "
+                               "+ q, k_new, v_new, out, block table"},
+        "clocks": sampler.summary(),
+        "timed_region_ms": round(region_ms, 3),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_attn(args.workload)
+    return line
+
+
 # ------------------------------------------------------------------------------------------------ main
 def bench_w4a16(args, dist: Dist) -> dict | None:
     """NVFP4 w4a16 MoE layer of one ep8 rank (1 GPU; the layer is one rank's slice by definition)."""
@@ -786,6 +899,8 @@ def main() -> int:
                     line["projection"] = pline
         elif args.workload.startswith("w4a16"):
             line = bench_w4a16(args, dist)
+        elif args.workload.startswith("attn"):
+            line = bench_attn(args, dist)
         else:
             raise SystemExit(f"unknown workload {args.workload}")
         if line is not None and dist.rank == 0:

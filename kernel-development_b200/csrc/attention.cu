@@ -309,7 +309,8 @@ __device__ __forceinline__ int block_incl_scan(int v, int* warp_sums, int* total
   return x + before;
 }
 
-// The CTA's stretch of the global tile sequence: [t_begin, t_end) of N tiles split evenly over gridDim.x CTAs.
+// The CTA's stretch of the global tile sequence: [t_begin, t_end) of N tiles split evenly over min(gridDim.x, N)
+// CTAs.
 // Returns the tile count; (b0, g0, t0) locate the first tile.  Every thread of the CTA takes part.
 __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, int* t0) {
   int* warp_sums = scratch;   // [32]
@@ -323,9 +324,11 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
     block_incl_scan(v, warp_sums, &chunk);
     total += chunk;
   }
-  const long long n = total, c = blockIdx.x, C = gridDim.x;
+  // the first min(grid, N) CTAs take the work, so every working CTA has at least one tile and the CTAs that
+  // cover one (sequence, KV head) form a gapless range (the merge reads one partial from each)
+  const long long n = total, c = blockIdx.x, C = gridDim.x < n ? gridDim.x : n;
+  if (c >= C) return 0;
   const int t_begin = static_cast<int>(c * n / C), t_end = static_cast<int>((c + 1) * n / C);
-  if (t_end <= t_begin) return 0;
   if (tid == 0) found[0] = -1;
   __syncthreads();
   int running = 0;

@@ -314,3 +314,36 @@ def w4a16_routing(cfg: W4A16Config, seed: int = 0) -> tuple[torch.Tensor, torch.
     logits = torch.randn((cfg.t, cfg.k), generator=g)
     w = torch.softmax(logits, dim=-1)
     return ids.to(torch.int32), w.to(torch.float32)
+
+
+# ------------------------------------------------------------------------------------------------ attention
+# The scored shapes of the reference's muse_attention_decode problem (okc_problems/muse_attention_decode.toml
+# [[shapes]]: case and seed), named attn_<id> with "/" -> "_".
+ATTN_CONFIGS = {
+    "attn_d1_sliding": (dict(batch=1, ctx=80000, heads="tp8", layer="sliding", dist="soft"), 601),
+    "attn_d1_full": (dict(batch=1, ctx=80000, heads="tp8", layer="full", dist="coherent"), 602),
+    "attn_d16_sliding": (dict(batch=16, ctx=80000, heads="tp8", layer="sliding", spread="agentic", dist="soft"), 603),
+    "attn_d16_full": (dict(batch=16, ctx=80000, heads="tp8", layer="full", spread="agentic", dist="coherent"), 604),
+    "attn_d32_sliding": (dict(batch=32, ctx=80000, heads="tp8", layer="sliding", spread="agentic", dist="soft"), 605),
+    "attn_d32_full": (dict(batch=32, ctx=80000, heads="tp8", layer="full", spread="agentic", dist="coherent"), 606),
+    "attn_v1_sliding": (dict(batch=1, ctx=80000, heads="tp8", layer="sliding", q_len=8, dist="soft"), 607),
+    "attn_v1_full": (dict(batch=1, ctx=80000, heads="tp8", layer="full", q_len=8, dist="coherent"), 608),
+    "attn_v16_sliding": (dict(batch=16, ctx=80000, heads="tp8", layer="sliding", q_len=8, spread="agentic",
+                              dist="soft"), 609),
+    "attn_v16_full": (dict(batch=16, ctx=80000, heads="tp8", layer="full", q_len=8, spread="agentic",
+                           dist="coherent"), 610),
+    "attn_v32_sliding": (dict(batch=32, ctx=80000, heads="tp8", layer="sliding", q_len=8, spread="agentic",
+                              dist="soft"), 611),
+    "attn_v32_full": (dict(batch=32, ctx=80000, heads="tp8", layer="full", q_len=8, spread="agentic",
+                           dist="coherent"), 612),
+}
+
+
+def attn_keys(data: dict, window: int) -> int:
+    """Cached keys one call reads, summed over sequences and KV heads (each 256 B: K and V, one byte each)."""
+    T = data["q"].shape[1]
+    Hkv = data["k_cache"].shape[1]
+    total = 0
+    for L in data["seq_lens"].tolist():
+        total += min(int(L), window + T - 1) if window > 0 else int(L)
+    return total * Hkv
