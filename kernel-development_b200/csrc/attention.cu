@@ -12,19 +12,19 @@
 //   attn_append_kernel   the new tokens' K/V, fp8 of value / kv_scale (round to nearest even, saturating at
 //                        +-448), written into their slots;
 //   attn_fwd_kernel      persistent, warp-specialised: the tiles of 128 keys of every (sequence, KV head) form
-//                        one sequence, split evenly over the CTAs.  A producer warp gathers a tile's K and V rows
-//                        (128 B each) with TMA row gathers (tile::gather4) into a ring of stages; one thread
-//                        issues S^T = K Q^T (tcgen05 kind::f8f6f4, M = 128 keys, N = 16 / 64 query rows,
-//                        K = 128 dims, the fp8 cache read as it is stored); the softmax warps read S^T from tensor
-//                        memory (thread = key), take the tile's row maxima across the 128 keys and write P^T as
-//                        e4m3, and the MMA thread accumulates O^T += V^T P^T (M = 128 dims, V read MN-major
-//                        straight from the cache rows) in tensor memory.  Queries and probabilities go in as two
-//                        e4m3 terms each (x = hi + lo, each the nearest e4m3; the residual is about 2^-8 of x), so
-//                        the products carry about bf16 precision while both MMAs read the fp8 cache directly.  The
-//                        running maximum is raised lazily (only when a tile's maximum exceeds it by more than 2^4),
-//                        which bounds every probability by 2^8 in e4m3 and rescales O^T in tensor memory rarely.
-//                        At the end of a CTA's stretch of one (sequence, KV head) the unnormalised O, row sums and
-//                        maxima go to a partial slot;
+//                        one sequence, split evenly over the CTAs.  A producer warp copies a tile's K and V rows
+//                        (128 B each, found through the block table) into a ring of stages with 16-byte cp.async
+//                        copies, laid out with the 128-byte swizzle; one thread issues S^T = K Q^T (tcgen05
+//                        kind::f8f6f4, M = 128 keys, N = 16 / 64 query rows, K = 128 dims, the fp8 cache read as
+//                        it is stored); 16 softmax warps read S^T from tensor memory (thread = key), take the
+//                        tile's row maxima across the 128 keys and write P^T as e4m3, and the MMA thread
+//                        accumulates O^T += V^T P^T (M = 128 dims; V and P^T both MN-major, V straight from the
+//                        cache rows) in tensor memory.  Queries and probabilities go in as two e4m3 terms each
+//                        (x = hi + lo, the residual about 2^-8 of x), so the products carry about bf16 precision
+//                        while both MMAs read the fp8 cache directly.  The running maximum is raised lazily (only
+//                        when a tile's maximum exceeds it by more than 2^4), which bounds every probability by
+//                        2^8 in e4m3 and rescales O^T in tensor memory rarely.  At the end of a CTA's stretch of
+//                        one (sequence, KV head) the unnormalised O, row sums and maxima go to a partial slot;
 //   attn_merge_kernel    per query row, the partials of the CTAs that covered its keys, merged exactly.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -40,6 +40,7 @@ constexpr int kAttnD = 128;          // head dim
 constexpr int kAttnTile = 128;       // keys per tile = TMEM lanes of S^T
 constexpr int kAttnMaxCtas = 1024;   // partial slots reserved for CTAs (workspace bound)
 constexpr int kAttnMaxRows = 64;     // T * group
+constexpr int kAttnMaxReg = 96;      // registers per thread: 18 warps, at most 5 on one SM sub-partition (16K registers)
 
 enum : unsigned int {
   kSiteAttnProdEmpty = 0x1A1,
@@ -50,7 +51,6 @@ enum : unsigned int {
   kSiteAttnMmaOFree = 0x1A6,
   kSiteAttnSoftS = 0x1A7,
   kSiteAttnSoftPv = 0x1A8,
-  kSiteAttnDrainTma = 0x1A9,
   kSiteAttnDrainMma = 0x1AA,
   kSiteAttnLen = 0x1AB,
   kSiteAttnSlot = 0x1AC,
@@ -60,6 +60,8 @@ enum : unsigned int {
 
 struct AttnParams {
   const __nv_bfloat16* q;   // [B, T, Hq, 128]
+  const uint8_t* k_cache;   // [slots, Hkv, 128] e4m3
+  const uint8_t* v_cache;
   const int* block_table;   // [B, max_len]
   const int* seq_lens;      // [B]
   float score_scale;        // kv_scale / sqrt(128) * log2(e)
@@ -136,20 +138,25 @@ struct AttnCursor {
   }
 };
 
-template <int NQ, int SPLIT, int STAGES>
+// NQ: MMA N (query-row columns, 16 or 64); ROWS: query rows the softmax threads handle (R <= ROWS <= NQ);
+// SPLIT: softmax warp groups, each taking ROWS / SPLIT rows of every key; STAGES: K/V ring depth.
+template <int NQ, int ROWS, int SPLIT, int STAGES>
 struct AttnLayout {
   static constexpr int kSoftThreads = 128 * SPLIT;
   static constexpr int kThreads = kSoftThreads + 64;   // + producer warp + MMA warp
-  static constexpr int kRpt = NQ / SPLIT;              // query rows per softmax thread
+  static constexpr int kRpt = ROWS / SPLIT;            // query rows per softmax thread
+  static constexpr int kPf = STAGES - 2;               // tiles of copies in flight
   static constexpr int kKvBytes = kAttnTile * kAttnD;  // 16 KB: 128 rows of 128 B
   static constexpr int kStageBytes = 2 * kKvBytes;     // K tile, then V tile
-  static constexpr int kQBytes = NQ * kAttnD;          // one e4m3 term of Q (or of P^T)
-  static constexpr int kQOffset = STAGES * kStageBytes;         // Q[buffer][hi, lo]
-  static constexpr int kPOffset = kQOffset + 4 * kQBytes;       // P^T[buffer][hi, lo]
-  static constexpr int kXchOffset = kPOffset + 4 * kQBytes;     // row maxima [2][NQ][4]
-  static constexpr int kLsumOffset = kXchOffset + 2 * NQ * 4 * 4;   // row sums [NQ][4]
-  static constexpr int kQcOffset = kLsumOffset + NQ * 4 * 4;        // score scale per row [2][NQ]
-  static constexpr int kBarOffset = kQcOffset + 2 * NQ * 4;
+  static constexpr int kQBytes = NQ * kAttnD;          // one e4m3 term of Q (or of P^T: NQ rows x 128 keys)
+  static constexpr int kQOffset = STAGES * kStageBytes;             // Q[buffer][hi, lo]
+  static constexpr int kPOffset = kQOffset + 4 * kQBytes;           // P^T[buffer][hi, lo]
+  static constexpr int kXchOffset = kPOffset + 4 * kQBytes;         // row maxima [2][ROWS][4]
+  static constexpr int kLsumOffset = kXchOffset + 2 * ROWS * 4 * 4;   // row sums [ROWS][4]
+  static constexpr int kRowmaxOffset = kLsumOffset + ROWS * 4 * 4;    // |q| maximum per row [2][ROWS]
+  static constexpr int kRowtOffset = kRowmaxOffset + 2 * ROWS * 4;    // token of each row [ROWS]
+  static constexpr int kBtOffset = kRowtOffset + ROWS * 4;            // block-table ring [kPf][128]
+  static constexpr int kBarOffset = kBtOffset + kPf * kAttnTile * 4;
   // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2], o_free, drain
   static constexpr int kNumBars = 2 * STAGES + 12;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;   // tmem slot, abort flag, scan scratch
@@ -157,14 +164,17 @@ struct AttnLayout {
   static constexpr int kSmemBytes = kMiscOffset + kMiscInts * 4 + 1024;
   static constexpr uint32_t kTmemCols = 3 * NQ <= 64 ? 64 : (3 * NQ <= 128 ? 128 : 256);
   // TMEM columns: S^T buffers [0, NQ) and [NQ, 2 NQ); O^T [2 NQ, 3 NQ)
+  static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 16), "rows per thread");
+  static_assert(kThreads <= 1024 && kPf >= 1, "launch shape");
 };
 
-// kind::f8f6f4, e4m3 x e4m3 -> f32, M = m, N = n; A K-major (scores) or MN-major (values), B K-major.
-__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n, bool a_mn_major) {
+// kind::f8f6f4, e4m3 x e4m3 -> f32, M = m, N = n; A K-major (scores) or MN-major (values: V^T), B K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                                   // D format: f32
          | (0u << 7)                                 // A format: e4m3
          | (0u << 10)                                // B format: e4m3
          | (a_mn_major ? (1u << 15) : 0u)            // A major
+         | (b_mn_major ? (1u << 16) : 0u)            // B major
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
@@ -188,18 +198,6 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Four rows of a 2-D tensor map whose box is one row high, into 512 consecutive bytes of shared memory (the map's
-// swizzle applied as for a tile load); completion on this CTA's mbarrier.  No multicast.
-__device__ __forceinline__ void tma_gather4(void* smem_dst, const void* tmap, uint64_t* bar, int4 rows,
-                                            uint64_t cache_policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(0), "r"(rows.x), "r"(rows.y), "r"(rows.z),
-      "r"(rows.w), "l"(cache_policy)
       : "memory");
 }
 
@@ -232,8 +230,38 @@ __device__ __forceinline__ float warp_max_f32(float x) {
   return r;
 }
 
+// 4 x 4 byte transpose across the four lanes of an aligned lane quad: lane e holds bytes x[e][0..3] and receives
+// x[0..3][e] (byte k of the result from lane k).
+__device__ __forceinline__ uint32_t quad_transpose(uint32_t x, int e) {
+  const uint32_t p1 = __shfl_xor_sync(0xffffffffu, x, 1);
+  const uint32_t y = (e & 1) ? __byte_perm(x, p1, 0x3715) : __byte_perm(x, p1, 0x6240);
+  const uint32_t p2 = __shfl_xor_sync(0xffffffffu, y, 2);
+  return (e & 2) ? __byte_perm(y, p2, 0x3276) : __byte_perm(y, p2, 0x5410);
+}
+
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// tcgen05.ld / st of N consecutive 32-bit columns of this warp's 32 lanes (shape 32x32b): thread i has lane
+// (lane base + i), columns [col, col + N).
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[N]);
+template <int N>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_cols<2>(uint32_t taddr, uint32_t (&r)[2]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr) : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<4>(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr)
+               : "memory");
+}
 template <>
 __device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -245,12 +273,15 @@ __device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[1
       : "memory");
 }
 template <>
-__device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
-  tmem_ld_32x32b_x32(taddr, r);
+__device__ __forceinline__ void tmem_st_cols<2>(uint32_t taddr, const uint32_t (&r)[2]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(r[0]), "r"(r[1]) : "memory");
 }
-
-template <int N>
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_st_cols<4>(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
 template <>
 __device__ __forceinline__ void tmem_st_cols<16>(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -260,17 +291,19 @@ __device__ __forceinline__ void tmem_st_cols<16>(uint32_t taddr, const uint32_t 
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
-template <>
-__device__ __forceinline__ void tmem_st_cols<32>(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32])
-      : "memory");
+
+// 16-byte asynchronous global -> shared copy, L1 bypassed (cp.async groups).
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+// 4-byte asynchronous global -> shared copy (cp.async groups).
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ uint8_t e4m3_of(float x) {
@@ -310,8 +343,7 @@ __device__ __forceinline__ int block_incl_scan(int v, int* warp_sums, int* total
 }
 
 // The CTA's stretch of the global tile sequence: [t_begin, t_end) of N tiles split evenly over min(gridDim.x, N)
-// CTAs.
-// Returns the tile count; (b0, g0, t0) locate the first tile.  Every thread of the CTA takes part.
+// CTAs.  Returns the tile count; (b0, g0, t0) locate the first tile.  Every thread of the CTA takes part.
 __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, int* t0) {
   int* warp_sums = scratch;   // [32]
   int* found = scratch + 32;  // [3]
@@ -355,20 +387,23 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
   return found[0] >= 0 ? t_end - t_begin : 0;
 }
 
-// Q rows of (b, g) as two e4m3 terms, scaled per row by a power of two s so that the largest |q| lands in
-// [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; qc[r] = score_scale / s.
-// Run by the softmax threads; each fences its writes for the tensor cores.
-template <int SOFT_THREADS>
-__device__ void attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* qc) {
+// Q rows of (b, g) as two e4m3 terms with one power-of-two scale s for the segment, chosen so the largest |q| of its
+// rows lands in [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; returns
+// score_scale / s (the same in every thread).  Run by all softmax threads (one named barrier); each fences its
+// writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.
+template <int SOFT_THREADS, int ROWS>
+__device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* rowmax) {
+  constexpr int kIt = (ROWS * 16 + SOFT_THREADS - 1) / SOFT_THREADS;   // items of 8 dims per thread
   const int tid = threadIdx.x;
   const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
-  for (int base = 0; base < items; base += SOFT_THREADS) {
-    const int item = base + tid;
+  float x[kIt][8];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int item = it * SOFT_THREADS + tid;
     const bool active = item < items;
     const int r = item >> 4, piece = item & 15;
-    float x[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = 0.f;
+    for (int e = 0; e < 8; ++e) x[it][e] = 0.f;
     if (active) {
       const int t = r / p.group, h = r - t * p.group;
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
@@ -377,41 +412,48 @@ __device__ void attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(v2[e]);
-        x[2 * e] = f.x;
-        x[2 * e + 1] = f.y;
+        x[it][2 * e] = f.x;
+        x[it][2 * e + 1] = f.y;
       }
     }
     float amax = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[e]));
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[it][e]));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (active) {
-      // power-of-two scale: amax * s in [128, 256); exponent clamped so s stays a finite normal float
-      int e2 = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
-      e2 = max(-100, min(100, e2));
-      const float s = __uint_as_float(static_cast<uint32_t>(127 + 7 - e2) << 23);
+    if (active && piece == 0) rowmax[r] = amax;
+  }
+  soft_bar_sync(SOFT_THREADS);
+  float amax = 0.f;
+  for (int r = 0; r < p.R; ++r) amax = fmaxf(amax, rowmax[r]);
+  // power-of-two scale: amax * s in [128, 256); exponent clamped so s stays a finite normal float
+  int e2 = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
+  e2 = max(-100, min(100, e2));
+  const float sc = __uint_as_float(static_cast<uint32_t>(127 + 7 - e2) << 23);
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int item = it * SOFT_THREADS + tid;
+    if (item < items) {
+      const int r = item >> 4, piece = item & 15;
       uint8_t hb[8], lb[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float xs = x[e] * s;
+        const float xs = x[it][e] * sc;
         hb[e] = e4m3_of(xs);
         lb[e] = e4m3_of(xs - f32_of_e4m3(hb[e]));
       }
       const int off = sw128_offset(r, piece * 8);
       *reinterpret_cast<uint2*>(qhi + off) = *reinterpret_cast<const uint2*>(hb);
       *reinterpret_cast<uint2*>(qlo + off) = *reinterpret_cast<const uint2*>(lb);
-      if (piece == 0) qc[r] = p.score_scale / s;
     }
   }
   fence_proxy_async_smem();
+  return p.score_scale / sc;
 }
 
-template <int NQ, int SPLIT, int STAGES>
-__global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                    const AttnParams p) {
-  using L = AttnLayout<NQ, SPLIT, STAGES>;
+template <int NQ, int ROWS, int SPLIT, int STAGES>
+__global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
+  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES>;
   constexpr int RPT = L::kRpt;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -430,9 +472,11 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
   int* scratch = misc + 8;   // 40 ints
   float* xch = reinterpret_cast<float*>(smem + L::kXchOffset);
   float* lsum = reinterpret_cast<float*>(smem + L::kLsumOffset);
-  float* qc = reinterpret_cast<float*>(smem + L::kQcOffset);
+  float* rowmax = reinterpret_cast<float*>(smem + L::kRowmaxOffset);   // [2][ROWS]
+  int* rowt = reinterpret_cast<int*>(smem + L::kRowtOffset);
+  int* bt_ring = reinterpret_cast<int*>(smem + L::kBtOffset);
   uint8_t* qtile = smem + L::kQOffset;   // [buffer][hi, lo][NQ][128]
-  uint8_t* ptile = smem + L::kPOffset;   // [buffer][hi, lo][NQ][128]
+  uint8_t* ptile = smem + L::kPOffset;   // [buffer][hi, lo][128 keys x NQ rows]
 
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
@@ -444,9 +488,10 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
   const int count = attn_locate(p, scratch, &b0, &g0, &t0);
   if (count == 0) return;   // uniform over the CTA: no tiles
 
-  // Q and P tiles start zero (rows R..NQ-1 stay zero); barriers; tensor memory
+  // Q and P tiles start zero (rows R..NQ-1 stay zero); row -> token table; barriers; tensor memory
   for (int i = tid; i < 8 * L::kQBytes / 16; i += L::kThreads)
     reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid < ROWS) rowt[tid] = tid / p.group;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -463,8 +508,6 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, L::kTmemCols);
@@ -477,48 +520,82 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer: K/V row gathers
-    const uint64_t pol = l2_policy_evict_first();
-    AttnCursor cur;
+    // ------------------------------------------------------------------ producer: K/V row copies
+    // Lane l copies 16-byte chunk (l & 7) of keys 4j + (l >> 3), j = 0..31, of K and V (cp.async, L1 bypassed) into
+    // the stage with the 128-byte swizzle.  Tile i's copies and the block-table entries of tile i + kPf form one
+    // cp.async group; at the start of iteration i the groups up to i - kPf have landed, so tile i - kPf is
+    // signalled (after a proxy fence: the tensor cores read it) and tile i's entries are in the ring.
+    constexpr int kPf = L::kPf;
+    const int chunk = static_cast<int>(lane & 7), ksub = static_cast<int>(lane >> 3);
+    AttnCursor cur, pf;
     cur.init(p, b0, g0, t0, count);
-    uint32_t armed_mask = 0, armed_phase = 0;
-    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1;
-      const bool ok = mbar_wait(&kv_empty[s], ph ^ 1u, abort_flag, kSiteAttnProdEmpty);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      // cache rows of keys k0 + 4 lane .. + 3; keys past the sequence read its last key (masked later)
-      const int k0 = cur.lo + cur.tile * kAttnTile;
-      const long long bt = static_cast<long long>(cur.b) * p.max_len;
-      const int last_slot = __ldg(p.block_table + bt + cur.L - 1);
-      int rows[4];
+    pf.init(p, b0, g0, t0, count);
+    auto prefetch = [&](int buf) {
+      const int k0 = pf.lo + pf.tile * kAttnTile;
+      const int* src = p.block_table + static_cast<long long>(pf.b) * p.max_len;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int pos = k0 + 4 * static_cast<int>(lane) + j;
-        int slot = pos < cur.L ? __ldg(p.block_table + bt + pos) : last_slot;
+        const int idx = 4 * static_cast<int>(lane) + j;
+        if (k0 + idx < pf.L) cp_async_4(bt_ring + buf * kAttnTile + idx, src + k0 + idx);
+      }
+    };
+#pragma unroll 1
+    for (int d = 0; d < kPf; ++d) {
+      if (pf.remaining > 0) {
+        prefetch(d);
+        pf.next(p);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    int issued = 0;
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int s = i % STAGES;
+      if (i >= kPf) {
+        cp_async_wait<kPf - 1>();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kv_full[(i - kPf) % STAGES]);
+      }
+      const bool ok = mbar_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int* rt = bt_ring + (i % kPf) * kAttnTile;
+      const int nvalid = cur.L - (cur.lo + cur.tile * kAttnTile);   // keys of this tile inside the sequence
+      const uint8_t* kbase = p.k_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
+      const uint8_t* vbase = p.v_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
+      uint8_t* st = smem + s * L::kStageBytes;
+#pragma unroll 8
+      for (int j = 0; j < kAttnTile / 4; ++j) {
+        const int key = 4 * j + ksub;
+        int slot = rt[key < nvalid ? key : nvalid - 1];   // keys past the sequence read its last key (masked)
         if (slot < 0 || slot >= p.slots) {
           report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnSlot);
           slot = 0;
         }
-        rows[j] = slot * p.Hkv + cur.g;
+        const long long off = static_cast<long long>(slot) * p.Hkv * kAttnD;
+        const int dst = key * 128 + ((chunk ^ (key & 7)) << 4);
+        cp_async_16(st + dst, kbase + off);
+        cp_async_16(st + L::kKvBytes + dst, vbase + off);
       }
-      if (lane == 0) mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
-      __syncwarp();
-      uint8_t* st = smem + s * L::kStageBytes;
-      const int4 r4 = make_int4(rows[0], rows[1], rows[2], rows[3]);
-      tma_gather4(st + lane * 512, &tm_k, &kv_full[s], r4, pol);
-      tma_gather4(st + L::kKvBytes + lane * 512, &tm_v, &kv_full[s], r4, pol);
-      armed_mask |= 1u << s;
-      armed_phase = (armed_phase & ~(1u << s)) | (ph << s);
+      __syncwarp();   // every lane has read tile i's entries before the ring slot is refilled
+      if (pf.remaining > 0) {
+        prefetch(i % kPf);
+        pf.next(p);
+      }
+      cp_async_commit();
+      issued = i + 1;
     }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    __syncwarp();
     if (lane == 0)
-      for (int s = 0; s < STAGES; ++s)
-        if (armed_mask & (1u << s)) mbar_wait_drain(&kv_full[s], (armed_phase >> s) & 1u, kSiteAttnDrainTma);
+      for (int t = issued > kPf ? issued - kPf : 0; t < issued; ++t) mbar_arrive(&kv_full[t % STAGES]);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, NQ, false);
-      constexpr uint32_t kIdPV = idesc_e4m3_f32(128, NQ, true);
+      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, NQ, false, false);
+      constexpr uint32_t kIdPV = idesc_e4m3_f32(128, NQ, true, false);
       const uint32_t o_tmem = tmem_base + 2 * NQ;
       AttnCursor cur;
       cur.init(p, b0, g0, t0, count);
@@ -581,8 +658,9 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax / epilogue warps
-    const int quad = warp & 3, rs = warp >> 2;   // TMEM lanes [32 quad, +32); rows [rs RPT, +RPT)
-    const int key = quad * 32 + static_cast<int>(lane);   // S^T lane = key of the tile; O^T lane = dim
+    // warp (quad, rs): TMEM lanes [32 quad, +32) = keys of the tile (S^T) and dims (O^T); rows [rs RPT, +RPT).
+    const int quad = warp & 3, rs = warp >> 2;
+    const int key = quad * 32 + static_cast<int>(lane);
     const int r0 = rs * RPT;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     constexpr float kTau = 4.f;     // raise the running maximum only past +2^4
@@ -590,11 +668,13 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
 
     AttnCursor qcur;
     qcur.init(p, b0, g0, t0, count);
-    attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile, qtile + L::kQBytes, qc);
+    float qsc0 = attn_prepare_q<L::kSoftThreads, ROWS>(p, qcur.b, qcur.g, qtile, qtile + L::kQBytes, rowmax);
+    float qsc1 = 0.f;   // score scales of the segments in Q buffers 0 and 1
     mbar_arrive(&q_full[0]);
     bool q_more = qcur.next_segment(p);
     if (q_more) {
-      attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile + 2 * L::kQBytes, qtile + 3 * L::kQBytes, qc + NQ);
+      qsc1 = attn_prepare_q<L::kSoftThreads, ROWS>(p, qcur.b, qcur.g, qtile + 2 * L::kQBytes,
+                                                   qtile + 3 * L::kQBytes, rowmax + ROWS);
       mbar_arrive(&q_full[1]);
     }
 
@@ -606,6 +686,7 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
       m_used[j] = -INFINITY;
       l_lane[j] = 0.f;
     }
+    bool ok = true;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int u = i & 1;
       const int bg = cur.b * p.Hkv + cur.g;
@@ -616,8 +697,13 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
           q_more = qcur.next_segment(p);
           if (q_more) {
             const int qb = (cur.seg + 1) & 1;
-            attn_prepare_q<L::kSoftThreads>(p, qcur.b, qcur.g, qtile + 2 * qb * L::kQBytes,
-                                            qtile + (2 * qb + 1) * L::kQBytes, qc + qb * NQ);
+            const float sc = attn_prepare_q<L::kSoftThreads, ROWS>(
+                p, qcur.b, qcur.g, qtile + 2 * qb * L::kQBytes, qtile + (2 * qb + 1) * L::kQBytes, rowmax + qb * ROWS);
+            if (qb == 0) {
+              qsc0 = sc;
+            } else {
+              qsc1 = sc;
+            }
             mbar_arrive(&q_full[qb]);
           }
         }
@@ -629,39 +715,47 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
         if (tid == 0 && cur.tile == 0) p.meta[bg * 2] = blockIdx.x;
       }
       // ---- scores of this thread's key for its rows (log2 units), masked
-      bool ok = mbar_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS);
-      if (!soft_bar_and(L::kSoftThreads, ok)) break;
-      tc_fence_after();
-      uint32_t acc[RPT];
-      tmem_ld_cols<RPT>(lane_addr + u * NQ + r0, acc);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_free[u]);
-      const float* qcs = qc + (cur.seg & 1) * NQ;
-      const int pos = cur.lo + cur.tile * kAttnTile + key;
-      const int new0 = cur.L - p.T;
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
+      ok = ok && got;
       float x[RPT];
-#pragma unroll
-      for (int j = 0; j < RPT; ++j) {
-        const int r = r0 + j;
-        float v = -INFINITY;
-        if (r < p.R) {
-          const int qpos = new0 + r / p.group;
-          const bool keep = pos <= qpos && (p.window == 0 || pos > qpos - p.window);
-          if (keep) v = __uint_as_float(acc[j]) * qcs[r];
+      {
+        uint32_t acc[RPT];
+        if (got) {
+          tc_fence_after();
+          tmem_ld_cols<RPT>(lane_addr + u * NQ + r0, acc);
+          tmem_ld_wait();
         }
-        x[j] = v;
+        tc_fence_before();
+        mbar_arrive(&s_free[u]);
+        const float qcs = (cur.seg & 1) ? qsc1 : qsc0;
+        const int k0 = cur.lo + cur.tile * kAttnTile;
+        const int pos = k0 + key;
+        const int new0 = cur.L - p.T;
+        // every row sees every key of an interior tile: before the first query and inside every window
+        const bool interior = k0 + kAttnTile - 1 <= new0 && (p.window == 0 || k0 > cur.L - 1 - p.window);
+#pragma unroll
+        for (int j = 0; j < RPT; ++j) {
+          const int r = r0 + j;
+          float v = got ? __uint_as_float(acc[j]) * qcs : -INFINITY;
+          if (r >= p.R) {
+            v = -INFINITY;
+          } else if (!interior) {
+            const int qpos = new0 + rowt[r];
+            if (pos > qpos || (p.window > 0 && pos <= qpos - p.window)) v = -INFINITY;
+          }
+          x[j] = v;
+        }
       }
       // ---- tile maxima over the 128 keys: warp redux, then the four quads through shared memory
-      float* xc = xch + (i & 1) * NQ * 4;
+      float* xc = xch + (i & 1) * ROWS * 4;
 #pragma unroll
       for (int j = 0; j < RPT; ++j) {
         const float wm = warp_max_f32(x[j]);
-        if (static_cast<int>(lane) == (j & 31)) xc[(r0 + j) * 4 + quad] = wm;
+        if (static_cast<int>(lane) == j) xc[(r0 + j) * 4 + quad] = wm;
       }
-      soft_bar_sync(L::kSoftThreads);
+      if (!soft_bar_and(L::kSoftThreads, ok)) break;
       float f[RPT];
-      bool rescale = false;
+      bool rescale = false;   // the same in every lane of the warp (same rows, same maxima)
 #pragma unroll
       for (int j = 0; j < RPT; ++j) {
         const float4 t4 = *reinterpret_cast<const float4*>(xc + (r0 + j) * 4);
@@ -675,44 +769,61 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
           rescale = true;
         }
       }
-      // every softmax thread saw the same maxima; with SPLIT = 2 the two row halves decide apart, so agree here
-      if (SPLIT > 1) rescale = !soft_bar_and(L::kSoftThreads, !rescale);
       if (rescale) {
-        // O^T of the tiles so far (PV of tile i - 1 included) times f, per row
+        // this warp's O^T columns (its rows, its 32 dims), PV of tile i - 1 included, times f
         const int j1 = i - 1;
-        ok = mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag, kSiteAttnSoftPv);
-        if (!soft_bar_and(L::kSoftThreads, ok)) break;
-        tc_fence_after();
-        uint32_t o[RPT];
-        tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
-        tmem_ld_wait();
+        const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
+                                                          kSiteAttnSoftPv));
+        ok = ok && pv;
+        if (pv) {
+          tc_fence_after();
+          uint32_t o[RPT];
+          tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
-        tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
-        tmem_st_wait();
+          for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
+          tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+          tmem_st_wait();
+        }
       }
-      // ---- probabilities (x 2^(8 - tau)) as two e4m3 terms into P^T[u]; rows >= R stay zero
-      if (i >= 2) {
-        const int j2 = i - 2;
-        ok = mbar_wait(&pv_done[u], (j2 >> 1) & 1, abort_flag, kSiteAttnSoftPv);
-        if (!soft_bar_and(L::kSoftThreads, ok)) break;
-      }
-      uint8_t* ph = ptile + (2 * u) * L::kQBytes;
-      uint8_t* pl = ph + L::kQBytes;
+      // ---- probabilities (x 2^(8 - tau)) as two e4m3 terms into P^T[u] ([rows][128 keys], 128-byte swizzle);
+      // pairs of rows: f16x2 of p, its nearest e4m3 pair (hi), then the e4m3 pair of the exact f16 residual (lo).
+      // The four lanes of a quad (keys 4m..4m+3) transpose their bytes so each stores whole 4-key words of one
+      // row.  Rows >= R get zero.
+      if (i >= 2) ok = mbar_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
+      uint32_t hw[(RPT + 3) / 4], lw[(RPT + 3) / 4];
 #pragma unroll
-      for (int j = 0; j < RPT; ++j) {
-        const int r = r0 + j;
-        if (r < p.R) {
-          l_lane[j] *= f[j];
-          float pv = 0.f;
-          if (x[j] != -INFINITY) pv = fast_exp2(x[j] - m_used[j] + kPShift);
-          const uint8_t hb = e4m3_of(pv);
-          const float hf = f32_of_e4m3(hb);
-          const uint8_t lb = e4m3_of(pv - hf);
-          l_lane[j] += hf + f32_of_e4m3(lb);
-          const int off = sw128_offset(r, key);
-          ph[off] = hb;
-          pl[off] = lb;
+      for (int w = 0; w < (RPT + 3) / 4; ++w) hw[w] = lw[w] = 0u;
+#pragma unroll
+      for (int j = 0; j < RPT; j += 2) {
+        float pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          l_lane[j + e] *= f[j + e];
+          pv[e] = x[j + e] != -INFINITY ? fast_exp2(x[j + e] - m_used[j + e] + kPShift) : 0.f;
+          l_lane[j + e] += pv[e];
+        }
+        const __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
+        const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
+        const __half2 hb = __half2(__nv_cvt_fp8x2_to_halfraw2(hi, __NV_E4M3));
+        const __nv_fp8x2_storage_t lo =
+            __nv_cvt_halfraw2_to_fp8x2(__half2_raw(__hsub2(h2, hb)), __NV_SATFINITE, __NV_E4M3);
+        hw[j >> 2] |= static_cast<uint32_t>(hi) << (8 * (j & 3));
+        lw[j >> 2] |= static_cast<uint32_t>(lo) << (8 * (j & 3));
+      }
+      {
+        uint8_t* ph = ptile + (2 * u) * L::kQBytes;
+        uint8_t* pl = ph + L::kQBytes;
+        const int e = static_cast<int>(lane & 3);
+        const int kb = key & ~3;
+#pragma unroll
+        for (int w = 0; w < (RPT + 3) / 4; ++w) {
+          const uint32_t th = quad_transpose(hw[w], e), tl = quad_transpose(lw[w], e);
+          if (RPT >= 4 || e < RPT) {   // RPT = 2: bytes 2, 3 of the word are the next warp group's rows
+            const int off = sw128_offset(r0 + 4 * w + e, kb);
+            *reinterpret_cast<uint32_t*>(ph + off) = th;
+            *reinterpret_cast<uint32_t*>(pl + off) = tl;
+          }
         }
       }
       fence_proxy_async_smem();
@@ -721,32 +832,32 @@ __global__ void __launch_bounds__(AttnLayout<NQ, SPLIT, STAGES>::kThreads, 1)
 
       if (cur.seg_end) {
         // ---- this segment's partial: O^T columns (thread = dim), row sums, maxima
-        ok = mbar_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv);
-        if (!soft_bar_and(L::kSoftThreads, ok)) break;
-        tc_fence_after();
+        const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
+        ok = ok && pv;
         uint32_t o[RPT];
-        tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
-        tmem_ld_wait();
+        if (pv) {
+          tc_fence_after();
+          tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+          tmem_ld_wait();
+        }
         tc_fence_before();
         mbar_arrive(o_free);
         const long long slot = static_cast<long long>(blockIdx.x) + bg;
 #pragma unroll
         for (int j = 0; j < RPT; ++j) {
           const int r = r0 + j;
-          float ls = l_lane[j];
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+          const float ls = warp_sum_f32(l_lane[j]);
           if (r < p.R) {
-            p.part_o[(slot * p.R + r) * kAttnD + key] = __uint_as_float(o[j]);
+            if (pv) p.part_o[(slot * p.R + r) * kAttnD + key] = __uint_as_float(o[j]);
             if (lane == 0) lsum[r * 4 + quad] = ls;
           }
         }
-        soft_bar_sync(L::kSoftThreads);
+        if (!soft_bar_and(L::kSoftThreads, ok)) break;
         if (quad == 0) {
 #pragma unroll
           for (int j = 0; j < RPT; ++j) {
             const int r = r0 + j;
-            if (r < p.R && static_cast<int>(lane) == (j & 31)) {
+            if (r < p.R && static_cast<int>(lane) == j) {
               const float4 l4 = *reinterpret_cast<const float4*>(lsum + r * 4);
               p.part_l[slot * p.R + r] = (l4.x + l4.y) + (l4.z + l4.w);
               p.part_m[slot * p.R + r] = m_used[j];
@@ -812,12 +923,16 @@ __global__ void __launch_bounds__(128) attn_append_kernel(const AttnAppendParams
 }
 
 // ---------------------------------------------------------------------------------------------
-// merge: one CTA (8 warps) per (sequence, KV head, query row); warp w takes the partials of CTAs c0 + w, + 8, ...
+// merge: one CTA (16 warps) per (sequence, KV head, query row).  Pass 1: the largest partial maximum M; pass 2:
+// warp w sums the partials of CTAs c0 + w, + 16, ... weighted by 2^(m - M) (independent loads, no running
+// rescale), then the 16 warps' sums are added through shared memory.
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+constexpr int kMergeWarps = 16;
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
     attn_merge_kernel(const AttnParams p, int ctas, float kv_scale, __nv_bfloat16* __restrict__ out) {
-  __shared__ float sm_m[8], sm_l[8];
-  __shared__ __align__(16) float sm_o[8][kAttnD];
+  __shared__ float red[kMergeWarps], sm_l[kMergeWarps];
+  __shared__ __align__(16) float sm_o[kMergeWarps][kAttnD];
   const int r = blockIdx.x % p.R;
   const int bg = blockIdx.x / p.R;
   const int g = bg % p.Hkv, b = bg / p.Hkv;
@@ -829,47 +944,47 @@ __global__ void __launch_bounds__(256)
     c0 = 0;
     c1 = -1;
   }
-  float m = -INFINITY, l = 0.f;
+  const int n = c1 - c0 + 1;
+  const long long base = static_cast<long long>(c0) + bg;   // the partial slot of CTA c0 + k is base + k
+  float mx = -INFINITY;
+  for (int k = threadIdx.x; k < n; k += kMergeWarps * 32) mx = fmaxf(mx, p.part_m[(base + k) * p.R + r]);
+  mx = warp_max_f32(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, red[w]);
+  float l = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c = c0 + warp; c <= c1; c += 8) {
-    const long long slot = static_cast<long long>(c) + bg;
-    const float mk = p.part_m[slot * p.R + r];
-    if (mk == -INFINITY) continue;
-    const float lk = p.part_l[slot * p.R + r];
-    const float4 ok = *reinterpret_cast<const float4*>(p.part_o + (slot * p.R + r) * kAttnD + lane * 4);
-    const float mn = fmaxf(m, mk);
-    const float a = fast_exp2(m - mn), w = fast_exp2(mk - mn);
-    l = l * a + lk * w;
-    acc.x = acc.x * a + ok.x * w;
-    acc.y = acc.y * a + ok.y * w;
-    acc.z = acc.z * a + ok.z * w;
-    acc.w = acc.w * a + ok.w * w;
-    m = mn;
+  if (M != -INFINITY) {
+#pragma unroll 4
+    for (int k = warp; k < n; k += kMergeWarps) {
+      const long long row = (base + k) * p.R + r;
+      const float mk = p.part_m[row];
+      const float lk = p.part_l[row];
+      const float4 ok = *reinterpret_cast<const float4*>(p.part_o + row * kAttnD + lane * 4);
+      const float w = mk != -INFINITY ? fast_exp2(mk - M) : 0.f;
+      l = fmaf(w, lk, l);
+      acc.x = fmaf(w, ok.x, acc.x);
+      acc.y = fmaf(w, ok.y, acc.y);
+      acc.z = fmaf(w, ok.z, acc.z);
+      acc.w = fmaf(w, ok.w, acc.w);
+    }
   }
-  if (lane == 0) {
-    sm_m[warp] = m;
-    sm_l[warp] = l;
-  }
+  if (lane == 0) sm_l[warp] = l;
   *reinterpret_cast<float4*>(&sm_o[warp][lane * 4]) = acc;
   __syncthreads();
   if (warp == 0) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, sm_m[w]);
     float lt = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        if (sm_m[w] == -INFINITY) continue;
-        const float s = fast_exp2(sm_m[w] - M);
-        lt += sm_l[w] * s;
-        const float4 ow = *reinterpret_cast<const float4*>(&sm_o[w][lane * 4]);
-        o.x += ow.x * s;
-        o.y += ow.y * s;
-        o.z += ow.z * s;
-        o.w += ow.w * s;
-      }
+    for (int w = 0; w < kMergeWarps; ++w) {
+      lt += sm_l[w];
+      const float4 ow = *reinterpret_cast<const float4*>(&sm_o[w][lane * 4]);
+      o.x += ow.x;
+      o.y += ow.y;
+      o.z += ow.z;
+      o.w += ow.w;
     }
     const float k = lt > 0.f ? kv_scale / lt : 0.f;
     __nv_bfloat16* dst = out + ((static_cast<long long>(b) * p.T + t) * p.Hq + g * p.group + h) * kAttnD + lane * 4;
@@ -915,11 +1030,10 @@ size_t attn_workspace_bytes(long long B, long long T, long long Hq, long long Hk
   return fbytes + static_cast<size_t>(B * Hkv * 2) * sizeof(int);
 }
 
-template <int NQ, int SPLIT, int STAGES>
-static int attn_launch_fwd(const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, long long max_tiles,
-                           int* ctas_out, cudaStream_t s) {
-  using L = AttnLayout<NQ, SPLIT, STAGES>;
-  auto kern = attn_fwd_kernel<NQ, SPLIT, STAGES>;
+template <int NQ, int ROWS, int SPLIT, int STAGES>
+static int attn_launch_fwd(const AttnParams& p, long long max_tiles, int* ctas_out, cudaStream_t s) {
+  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES>;
+  auto kern = attn_fwd_kernel<NQ, ROWS, SPLIT, STAGES>;
   static int occ[64] = {0};
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev));
@@ -941,7 +1055,7 @@ static int attn_launch_fwd(const CUtensorMap& tk, const CUtensorMap& tv, const A
   if (c > kAttnMaxCtas) c = kAttnMaxCtas;
   if (c < 1) c = 1;
   *ctas_out = static_cast<int>(c);
-  kern<<<static_cast<unsigned int>(c), L::kThreads, L::kSmemBytes, s>>>(tk, tv, p);
+  kern<<<static_cast<unsigned int>(c), L::kThreads, L::kSmemBytes, s>>>(p);
   return cuda_status(cudaGetLastError());
 }
 
@@ -985,11 +1099,8 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
   const size_t fbytes = (static_cast<size_t>(nslots) * R * (2 + kAttnD) * sizeof(float) + 255) / 256 * 256;
   p.meta = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + fbytes);
 
-  CUtensorMap tk, tv;   // the caches as [slots * Hkv] rows of 128 B (a bf16 view of 64 elements), one-row boxes
-  rc = make_tmap_bf16_2d(&tk, k_cache, 64, static_cast<uint64_t>(slots * Hkv), 64, 64, 1);
-  if (rc) return rc;
-  rc = make_tmap_bf16_2d(&tv, v_cache, 64, static_cast<uint64_t>(slots * Hkv), 64, 64, 1);
-  if (rc) return rc;
+  p.k_cache = static_cast<const uint8_t*>(k_cache);
+  p.v_cache = static_cast<const uint8_t*>(v_cache);
 
   AttnAppendParams a;
   a.k_new = static_cast<const __nv_bfloat16*>(k_new);
@@ -1010,11 +1121,12 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
   if (rc) return rc;
 
   int ctas = 0;
-  rc = R <= 16 ? attn_launch_fwd<16, 1, 6>(tk, tv, p, max_tiles, &ctas, s)
-               : attn_launch_fwd<64, 2, 4>(tk, tv, p, max_tiles, &ctas, s);
+  rc = R <= 8    ? attn_launch_fwd<16, 8, 4, 6>(p, max_tiles, &ctas, s)
+       : R <= 16 ? attn_launch_fwd<16, 16, 4, 6>(p, max_tiles, &ctas, s)
+                 : attn_launch_fwd<64, 64, 4, 4>(p, max_tiles, &ctas, s);
   if (rc) return rc;
-  attn_merge_kernel<<<static_cast<unsigned int>(B * Hkv * R), 256, 0, s>>>(p, ctas, kv_scale,
-                                                                           static_cast<__nv_bfloat16*>(out));
+  attn_merge_kernel<<<static_cast<unsigned int>(B * Hkv * R), kMergeWarps * 32, 0, s>>>(
+      p, ctas, kv_scale, static_cast<__nv_bfloat16*>(out));
   return cuda_status(cudaGetLastError());
 }
 
