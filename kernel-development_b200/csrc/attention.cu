@@ -12,11 +12,11 @@
 //   attn_append_kernel   the new tokens' K/V, fp8 of value / kv_scale (round to nearest even, saturating at
 //                        +-448), written into their slots;
 //   attn_fwd_kernel      persistent, warp-specialised: the tiles of 128 keys of every (sequence, KV head) form
-//                        one sequence, split evenly over the CTAs.  A producer warp copies a tile's K and V rows
+//                        one sequence, split evenly over the CTAs.  Producer warps copy a tile's K and V rows
 //                        (128 B each, found through the block table) into a ring of stages with 16-byte cp.async
 //                        copies, laid out with the 128-byte swizzle; one thread issues S^T = K Q^T (tcgen05
 //                        kind::f8f6f4, M = 128 keys, N = 16 / 64 query rows, K = 128 dims, the fp8 cache read as
-//                        it is stored); 16 softmax warps read S^T from tensor memory (thread = key), take the
+//                        it is stored); 8 or 16 softmax warps read S^T from tensor memory (thread = key), take the
 //                        tile's row maxima across the 128 keys and write P^T as e4m3, and the MMA thread
 //                        accumulates O^T += V^T P^T (M = 128 dims; V and P^T both MN-major, V straight from the
 //                        cache rows) in tensor memory.  Queries and probabilities go in as two e4m3 terms each
@@ -40,7 +40,6 @@ constexpr int kAttnD = 128;          // head dim
 constexpr int kAttnTile = 128;       // keys per tile = TMEM lanes of S^T
 constexpr int kAttnMaxCtas = 1024;   // partial slots reserved for CTAs (workspace bound)
 constexpr int kAttnMaxRows = 64;     // T * group
-constexpr int kAttnMaxReg = 96;      // registers per thread: 18 warps, at most 5 on one SM sub-partition (16K registers)
 
 enum : unsigned int {
   kSiteAttnProdEmpty = 0x1A1,
@@ -139,11 +138,12 @@ struct AttnCursor {
 };
 
 // NQ: MMA N (query-row columns, 16 or 64); ROWS: query rows the softmax threads handle (R <= ROWS <= NQ);
-// SPLIT: softmax warp groups, each taking ROWS / SPLIT rows of every key; STAGES: K/V ring depth.
-template <int NQ, int ROWS, int SPLIT, int STAGES>
+// SPLIT: softmax warp groups, each taking ROWS / SPLIT rows of every key; STAGES: K/V ring depth; NPROD: producer
+// warps (one warp's cp.async stream reaches about 1.4 TB/s of random 128-byte rows over 148 SMs; four, about 3).
+template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
 struct AttnLayout {
   static constexpr int kSoftThreads = 128 * SPLIT;
-  static constexpr int kThreads = kSoftThreads + 64;   // + producer warp + MMA warp
+  static constexpr int kThreads = kSoftThreads + 32 * (NPROD + 1);   // + producer warps + MMA warp
   static constexpr int kRpt = ROWS / SPLIT;            // query rows per softmax thread
   static constexpr int kPf = STAGES - 2;               // tiles of copies in flight
   static constexpr int kKvBytes = kAttnTile * kAttnD;  // 16 KB: 128 rows of 128 B
@@ -155,8 +155,8 @@ struct AttnLayout {
   static constexpr int kLsumOffset = kXchOffset + 2 * ROWS * 4 * 4;   // row sums [ROWS][4]
   static constexpr int kRowmaxOffset = kLsumOffset + ROWS * 4 * 4;    // |q| maximum per row [2][ROWS]
   static constexpr int kRowtOffset = kRowmaxOffset + 2 * ROWS * 4;    // token of each row [ROWS]
-  static constexpr int kBtOffset = kRowtOffset + ROWS * 4;            // block-table ring [kPf][128]
-  static constexpr int kBarOffset = kBtOffset + kPf * kAttnTile * 4;
+  static constexpr int kBtOffset = kRowtOffset + ROWS * 4;            // block-table rings [NPROD][kPf][128]
+  static constexpr int kBarOffset = kBtOffset + NPROD * kPf * kAttnTile * 4;
   // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2], o_free, drain
   static constexpr int kNumBars = 2 * STAGES + 12;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;   // tmem slot, abort flag, scan scratch
@@ -164,8 +164,9 @@ struct AttnLayout {
   static constexpr int kSmemBytes = kMiscOffset + kMiscInts * 4 + 1024;
   static constexpr uint32_t kTmemCols = 3 * NQ <= 64 ? 64 : (3 * NQ <= 128 ? 128 : 256);
   // TMEM columns: S^T buffers [0, NQ) and [NQ, 2 NQ); O^T [2 NQ, 3 NQ)
-  static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 16), "rows per thread");
-  static_assert(kThreads <= 1024 && kPf >= 1, "launch shape");
+  static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 8 || kRpt == 16),
+                "rows per thread");
+  static_assert(kThreads <= 1024 && kPf >= 1 && 32 % NPROD == 0, "launch shape");
 };
 
 // kind::f8f6f4, e4m3 x e4m3 -> f32, M = m, N = n; A K-major (scores) or MN-major (values: V^T), B K-major.
@@ -263,6 +264,13 @@ __device__ __forceinline__ void tmem_ld_cols<4>(uint32_t taddr, uint32_t (&r)[4]
                : "memory");
 }
 template <>
+__device__ __forceinline__ void tmem_ld_cols<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+template <>
 __device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
@@ -280,6 +288,12 @@ template <>
 __device__ __forceinline__ void tmem_st_cols<4>(uint32_t taddr, const uint32_t (&r)[4]) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
                "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_st_cols<8>(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
 template <>
@@ -451,9 +465,10 @@ __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi,
   return p.score_scale / sc;
 }
 
-template <int NQ, int ROWS, int SPLIT, int STAGES>
-__global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
-  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES>;
+template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
+__global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kThreads, 1)
+    attn_fwd_kernel(const AttnParams p) {
+  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>;
   constexpr int RPT = L::kRpt;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -481,8 +496,8 @@ __global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
   const int tid = threadIdx.x;
-  constexpr int kProducerWarp = L::kSoftThreads / 32;
-  constexpr int kMmaWarp = kProducerWarp + 1;
+  constexpr int kProducerWarp = L::kSoftThreads / 32;   // producer warps kProducerWarp .. + NPROD - 1
+  constexpr int kMmaWarp = kProducerWarp + NPROD;
 
   int b0 = 0, g0 = 0, t0 = 0;
   const int count = attn_locate(p, scratch, &b0, &g0, &t0);
@@ -494,7 +509,7 @@ __global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
   if (tid < ROWS) rowt[tid] = tid / p.group;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_full[s], NPROD);
       mbar_init(&kv_empty[s], 1);
     }
     for (int u = 0; u < 2; ++u) {
@@ -519,13 +534,16 @@ __global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------------ producer: K/V row copies
-    // Lane l copies 16-byte chunk (l & 7) of keys 4j + (l >> 3), j = 0..31, of K and V (cp.async, L1 bypassed) into
-    // the stage with the 128-byte swizzle.  Tile i's copies and the block-table entries of tile i + kPf form one
-    // cp.async group; at the start of iteration i the groups up to i - kPf have landed, so tile i - kPf is
-    // signalled (after a proxy fence: the tensor cores read it) and tile i's entries are in the ring.
+  if (warp >= kProducerWarp && warp < kMmaWarp) {
+    // ------------------------------------------------------------------ producers: K/V row copies
+    // Producer warp wp, lane l copies 16-byte chunk (l & 7) of keys 4j + (l >> 3), j = wp, wp + NPROD, .. < 32, of
+    // K and V (cp.async, L1 bypassed) into the stage with the 128-byte swizzle.  Each producer warp keeps its own
+    // ring of block-table entries.  Tile i's copies and the entries of tile i + kPf form one cp.async group; at
+    // the start of iteration i the groups up to i - kPf have landed, so the warp signals its part of tile i - kPf
+    // (after a proxy fence: the tensor cores read it) and tile i's entries are in its ring.
     constexpr int kPf = L::kPf;
+    const int wp = warp - kProducerWarp;
+    bt_ring += wp * kPf * kAttnTile;
     const int chunk = static_cast<int>(lane & 7), ksub = static_cast<int>(lane >> 3);
     AttnCursor cur, pf;
     cur.init(p, b0, g0, t0, count);
@@ -566,7 +584,7 @@ __global__ void __maxnreg__(kAttnMaxReg) attn_fwd_kernel(const AttnParams p) {
       const uint8_t* vbase = p.v_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
       uint8_t* st = smem + s * L::kStageBytes;
 #pragma unroll 8
-      for (int j = 0; j < kAttnTile / 4; ++j) {
+      for (int j = wp; j < kAttnTile / 4; j += NPROD) {
         const int key = 4 * j + ksub;
         int slot = rt[key < nvalid ? key : nvalid - 1];   // keys past the sequence read its last key (masked)
         if (slot < 0 || slot >= p.slots) {
@@ -1030,10 +1048,10 @@ size_t attn_workspace_bytes(long long B, long long T, long long Hq, long long Hk
   return fbytes + static_cast<size_t>(B * Hkv * 2) * sizeof(int);
 }
 
-template <int NQ, int ROWS, int SPLIT, int STAGES>
+template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
 static int attn_launch_fwd(const AttnParams& p, long long max_tiles, int* ctas_out, cudaStream_t s) {
-  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES>;
-  auto kern = attn_fwd_kernel<NQ, ROWS, SPLIT, STAGES>;
+  using L = AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>;
+  auto kern = attn_fwd_kernel<NQ, ROWS, SPLIT, STAGES, NPROD>;
   static int occ[64] = {0};
   int dev = 0;
   int rc = cuda_status(cudaGetDevice(&dev));
@@ -1121,9 +1139,9 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
   if (rc) return rc;
 
   int ctas = 0;
-  rc = R <= 8    ? attn_launch_fwd<16, 8, 4, 6>(p, max_tiles, &ctas, s)
-       : R <= 16 ? attn_launch_fwd<16, 16, 4, 6>(p, max_tiles, &ctas, s)
-                 : attn_launch_fwd<64, 64, 4, 4>(p, max_tiles, &ctas, s);
+  rc = R <= 8    ? attn_launch_fwd<16, 8, 2, 6, 4>(p, max_tiles, &ctas, s)
+       : R <= 16 ? attn_launch_fwd<16, 16, 2, 6, 4>(p, max_tiles, &ctas, s)
+                 : attn_launch_fwd<64, 64, 4, 4, 2>(p, max_tiles, &ctas, s);
   if (rc) return rc;
   attn_merge_kernel<<<static_cast<unsigned int>(B * Hkv * R), kMergeWarps * 32, 0, s>>>(
       p, ctas, kv_scale, static_cast<__nv_bfloat16*>(out));
