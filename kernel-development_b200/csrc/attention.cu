@@ -202,6 +202,11 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// Programmatic dependent launch: let the next kernel of the stream start its prologue now / wait until the previous
+// kernel's grid has completed and its writes are visible (a no-op when launched without the attribute).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void soft_bar_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
@@ -362,12 +367,13 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
   int* warp_sums = scratch;   // [32]
   int* found = scratch + 32;  // [3]
   const int tid = threadIdx.x;
-  int total = 0;
+  const bool one_chunk = p.B <= static_cast<int>(blockDim.x);   // the first pass's scan can be reused
+  int total = 0, my_tiles = 0, my_incl = 0;
   for (int base = 0; base < p.B; base += blockDim.x) {
     const int b = base + tid;
-    const int v = b < p.B ? attn_tiles_of(p, attn_len(p, b)) * p.Hkv : 0;
+    my_tiles = b < p.B ? attn_tiles_of(p, attn_len(p, b)) : 0;
     int chunk;
-    block_incl_scan(v, warp_sums, &chunk);
+    my_incl = block_incl_scan(my_tiles * p.Hkv, warp_sums, &chunk);
     total += chunk;
   }
   // the first min(grid, N) CTAs take the work, so every working CTA has at least one tile and the CTAs that
@@ -380,10 +386,12 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
   int running = 0;
   for (int base = 0; base < p.B; base += blockDim.x) {
     const int b = base + tid;
-    const int tiles = b < p.B ? attn_tiles_of(p, attn_len(p, b)) : 0;
+    int tiles = my_tiles, incl = my_incl, chunk = total;
+    if (!one_chunk) {
+      tiles = b < p.B ? attn_tiles_of(p, attn_len(p, b)) : 0;
+      incl = block_incl_scan(tiles * p.Hkv, warp_sums, &chunk);
+    }
     const int v = tiles * p.Hkv;
-    int chunk;
-    const int incl = block_incl_scan(v, warp_sums, &chunk);
     const int excl = incl - v;
     if (v > 0 && running + excl <= t_begin && t_begin < running + incl) {
       const int off = t_begin - running - excl;
@@ -567,6 +575,7 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
     cp_async_commit();
     cp_async_wait<0>();
     __syncwarp();
+    pdl_wait();   // the new tokens' rows are written by the append kernel launched just before
     int issued = 0;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int s = i % STAGES;
@@ -912,6 +921,7 @@ struct AttnAppendParams {
 };
 
 __global__ void __launch_bounds__(128) attn_append_kernel(const AttnAppendParams a) {
+  pdl_launch_dependents();   // the attention kernel's prologue may overlap this kernel
   const long long row = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= static_cast<long long>(a.B) * a.T * a.Hkv) return;
@@ -956,6 +966,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
   const int g = bg % p.Hkv, b = bg / p.Hkv;
   const int t = r / p.group, h = r - t * p.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();   // the partials come from the attention kernel launched just before
   int c0 = p.meta[bg * 2], c1 = p.meta[bg * 2 + 1];
   if (c0 < 0 || c1 >= ctas || c0 > c1) {
     if (threadIdx.x == 0) report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnMeta);
@@ -1073,8 +1084,17 @@ static int attn_launch_fwd(const AttnParams& p, long long max_tiles, int* ctas_o
   if (c > kAttnMaxCtas) c = kAttnMaxCtas;
   if (c < 1) c = 1;
   *ctas_out = static_cast<int>(c);
-  kern<<<static_cast<unsigned int>(c), L::kThreads, L::kSmemBytes, s>>>(p);
-  return cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned int>(c), 1, 1);
+  cfg.blockDim = dim3(L::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // overlap the append kernel's tail
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p));
 }
 
 int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
@@ -1143,8 +1163,18 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
        : R <= 16 ? attn_launch_fwd<16, 16, 2, 6, 4>(p, max_tiles, &ctas, s)
                  : attn_launch_fwd<64, 64, 4, 4, 2>(p, max_tiles, &ctas, s);
   if (rc) return rc;
-  attn_merge_kernel<<<static_cast<unsigned int>(B * Hkv * R), kMergeWarps * 32, 0, s>>>(
-      p, ctas, kv_scale, static_cast<__nv_bfloat16*>(out));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned int>(B * Hkv * R), 1, 1);
+  cfg.blockDim = dim3(kMergeWarps * 32, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  rc = cuda_status(cudaLaunchKernelEx(&cfg, attn_merge_kernel, static_cast<const AttnParams>(p), ctas, kv_scale,
+                                      static_cast<__nv_bfloat16*>(out)));
+  if (rc) return rc;
   return cuda_status(cudaGetLastError());
 }
 
