@@ -210,6 +210,19 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void soft_bar_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
+// Named barrier of the softmax warps that also ORs a predicate over them.
+__device__ __forceinline__ bool soft_bar_or(int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(nthreads)
+      : "memory");
+  return r != 0u;
+}
 // Named barrier of the softmax warps that also ANDs a predicate over them.
 __device__ __forceinline__ bool soft_bar_and(int nthreads, bool v) {
   uint32_t r;
@@ -773,44 +786,52 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
           x[j] = v;
         }
       }
-      // ---- tile maxima over the 128 keys: warp redux, then the four quads through shared memory
-      float* xc = xch + (i & 1) * ROWS * 4;
+      // ---- the running maxima change only when some score exceeds its row's maximum by more than 2^tau (and on
+      // a segment's first tile, where they are -inf): one CTA-wide vote; only then the tile's row maxima are
+      // exchanged across the 128 keys (warp redux, then the four quads through shared memory) and O^T rescaled.
+      bool over = false;
 #pragma unroll
-      for (int j = 0; j < RPT; ++j) {
-        const float wm = warp_max_f32(x[j]);
-        if (static_cast<int>(lane) == j) xc[(r0 + j) * 4 + quad] = wm;
-      }
-      if (!soft_bar_and(L::kSoftThreads, ok)) break;
-      float f[RPT];
-      bool rescale = false;   // the same in every lane of the warp (same rows, same maxima)
+      for (int j = 0; j < RPT; ++j) over = over || x[j] > m_used[j] + kTau;
+      if (soft_bar_or(L::kSoftThreads, over || !ok)) {
+        float* xc = xch + (i & 1) * ROWS * 4;
 #pragma unroll
-      for (int j = 0; j < RPT; ++j) {
-        const float4 t4 = *reinterpret_cast<const float4*>(xc + (r0 + j) * 4);
-        const float tmax = fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w));
-        f[j] = 1.f;
-        if (m_used[j] == -INFINITY) {
-          m_used[j] = tmax;   // first keys of this row in the segment: its O^T column is still zero
-        } else if (tmax > m_used[j] + kTau) {
-          f[j] = fast_exp2(m_used[j] - tmax);
-          m_used[j] = tmax;
-          rescale = true;
+        for (int j = 0; j < RPT; ++j) {
+          const float wm = warp_max_f32(x[j]);
+          if (static_cast<int>(lane) == j) xc[(r0 + j) * 4 + quad] = wm;
         }
-      }
-      if (rescale) {
-        // this warp's O^T columns (its rows, its 32 dims), PV of tile i - 1 included, times f
-        const int j1 = i - 1;
-        const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
-                                                          kSiteAttnSoftPv));
-        ok = ok && pv;
-        if (pv) {
-          tc_fence_after();
-          uint32_t o[RPT];
-          tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
-          tmem_ld_wait();
+        if (!soft_bar_and(L::kSoftThreads, ok)) break;
+        float f[RPT];
+        bool rescale = false;   // the same in every lane of the warp (same rows, same maxima)
 #pragma unroll
-          for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
-          tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
-          tmem_st_wait();
+        for (int j = 0; j < RPT; ++j) {
+          const float4 t4 = *reinterpret_cast<const float4*>(xc + (r0 + j) * 4);
+          const float tmax = fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w));
+          f[j] = 1.f;
+          if (m_used[j] == -INFINITY) {
+            m_used[j] = tmax;   // first keys of this row in the segment: its O^T column is still zero
+          } else if (tmax > m_used[j] + kTau) {
+            f[j] = fast_exp2(m_used[j] - tmax);
+            m_used[j] = tmax;
+            l_lane[j] *= f[j];
+            rescale = true;
+          }
+        }
+        if (rescale) {
+          // this warp's O^T columns (its rows, its 32 dims), PV of tile i - 1 included, times f
+          const int j1 = i - 1;
+          const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
+                                                            kSiteAttnSoftPv));
+          ok = ok && pv;
+          if (pv) {
+            tc_fence_after();
+            uint32_t o[RPT];
+            tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
+            tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+            tmem_st_wait();
+          }
         }
       }
       // ---- probabilities (x 2^(8 - tau)) as two e4m3 terms into P^T[u] ([rows][128 keys], 128-byte swizzle);
@@ -826,7 +847,6 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
         float pv[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          l_lane[j + e] *= f[j + e];
           pv[e] = x[j + e] != -INFINITY ? fast_exp2(x[j + e] - m_used[j + e] + kPShift) : 0.f;
           l_lane[j + e] += pv[e];
         }
