@@ -151,7 +151,11 @@ struct AttnLayout {
   static constexpr int kQBytes = NQ * kAttnD;          // one e4m3 term of Q (or of P^T: NQ rows x 128 keys)
   static constexpr int kQOffset = STAGES * kStageBytes;             // Q[buffer][hi, lo]
   static constexpr int kPOffset = kQOffset + 4 * kQBytes;           // P^T[buffer][hi, lo]
-  static constexpr int kXchOffset = kPOffset + 4 * kQBytes;         // row maxima [2][ROWS][4]
+  // kMmaL: the row sums come from the tensor cores (a tile of e4m3 ones times P^T into TMEM columns beside O^T)
+  // and the probabilities are computed in f16 pairs; the conversion / transcendental pipe limits many rows.
+  static constexpr bool kMmaL = ROWS > 16;
+  static constexpr int kOnesOffset = kPOffset + 4 * kQBytes;        // [128][128] e4m3 ones (kMmaL)
+  static constexpr int kXchOffset = kOnesOffset + (kMmaL ? kKvBytes : 0);   // row maxima [2][ROWS][4]
   static constexpr int kLsumOffset = kXchOffset + 2 * ROWS * 4 * 4;   // row sums [ROWS][4]
   static constexpr int kRowmaxOffset = kLsumOffset + ROWS * 4 * 4;    // |q| maximum per row [2][ROWS]
   static constexpr int kRowtOffset = kRowmaxOffset + 2 * ROWS * 4;    // token of each row [ROWS]
@@ -162,9 +166,11 @@ struct AttnLayout {
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;   // tmem slot, abort flag, scan scratch
   static constexpr int kMiscInts = 48;
   static constexpr int kSmemBytes = kMiscOffset + kMiscInts * 4 + 1024;
-  static constexpr uint32_t kTmemCols = 3 * NQ <= 64 ? 64 : (3 * NQ <= 128 ? 128 : 256);
-  // TMEM columns: S^T buffers [0, NQ) and [NQ, 2 NQ); O^T [2 NQ, 3 NQ)
-  static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 8 || kRpt == 16),
+  static constexpr int kCols = (kMmaL ? 4 : 3) * NQ;
+  static constexpr uint32_t kTmemCols = kCols <= 64 ? 64 : (kCols <= 128 ? 128 : 256);
+  // TMEM columns: S^T buffers [0, NQ) and [NQ, 2 NQ); O^T [2 NQ, 3 NQ); row sums [3 NQ, 4 NQ) (kMmaL)
+  static_assert(kCols <= 256, "tensor memory columns");
+  static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 8 || kRpt == 16 || kRpt == 32),
                 "rows per thread");
   static_assert(kThreads <= 1024 && kPf >= 1 && 32 % NPROD == 0, "launch shape");
 };
@@ -200,6 +206,34 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Bounded mbarrier wait whose polls suspend the thread (up to 20 us each, woken when the phase completes), so
+// waiting warps leave the issue slots to the working ones; same contract as mbar_wait (abort flag, 2 s limit,
+// status word on timeout).
+__device__ __forceinline__ bool attn_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0u;
+}
+__device__ __forceinline__ bool attn_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned int site) {
+  if (attn_test(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (attn_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > KDB_WAIT_NS) {
+      report(KDB_ERR_TIMEOUT, site);
+      *abort_flag = 1;
+      return false;
+    }
+  }
 }
 
 // Programmatic dependent launch: let the next kernel of the stream start its prologue now / wait until the previous
@@ -296,6 +330,22 @@ __device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[1
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld_32x32b_x32(taddr, r);
+}
+template <>
+__device__ __forceinline__ void tmem_st_cols<32>(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32])
       : "memory");
 }
 template <>
@@ -428,35 +478,34 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
 // writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.
 template <int SOFT_THREADS, int ROWS>
 __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* rowmax) {
-  constexpr int kIt = (ROWS * 16 + SOFT_THREADS - 1) / SOFT_THREADS;   // items of 8 dims per thread
   const int tid = threadIdx.x;
   const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
-  float x[kIt][8];
-#pragma unroll
-  for (int it = 0; it < kIt; ++it) {
-    const int item = it * SOFT_THREADS + tid;
-    const bool active = item < items;
+  auto load = [&](int item, float (&x)[8]) {
     const int r = item >> 4, piece = item & 15;
+    const int t = r / p.group, h = r - t * p.group;
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
+        p.q + ((static_cast<long long>(b) * p.T + t) * p.Hq + g * p.group + h) * kAttnD + piece * 8));
+    const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[it][e] = 0.f;
-    if (active) {
-      const int t = r / p.group, h = r - t * p.group;
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(
-          p.q + ((static_cast<long long>(b) * p.T + t) * p.Hq + g * p.group + h) * kAttnD + piece * 8));
-      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(v2[e]);
-        x[it][2 * e] = f.x;
-        x[it][2 * e + 1] = f.y;
-      }
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(v2[e]);
+      x[2 * e] = f.x;
+      x[2 * e + 1] = f.y;
     }
+  };
+  // pass 1: the largest |q| of every row (the 16 lanes of a half-warp hold one row)
+  for (int base = 0; base < items; base += SOFT_THREADS) {
+    const int item = base + tid;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = 0.f;
+    if (item < items) load(item, x);
     float amax = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[it][e]));
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(x[e]));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (active && piece == 0) rowmax[r] = amax;
+    if (item < items && (item & 15) == 0) rowmax[item >> 4] = amax;
   }
   soft_bar_sync(SOFT_THREADS);
   float amax = 0.f;
@@ -465,22 +514,20 @@ __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi,
   int e2 = amax > 0.f ? static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127 : 0;
   e2 = max(-100, min(100, e2));
   const float sc = __uint_as_float(static_cast<uint32_t>(127 + 7 - e2) << 23);
+  // pass 2: the two e4m3 terms (q read again: it is in L1/L2)
+  for (int item = tid; item < items; item += SOFT_THREADS) {
+    float x[8];
+    load(item, x);
+    uint8_t hb[8], lb[8];
 #pragma unroll
-  for (int it = 0; it < kIt; ++it) {
-    const int item = it * SOFT_THREADS + tid;
-    if (item < items) {
-      const int r = item >> 4, piece = item & 15;
-      uint8_t hb[8], lb[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float xs = x[it][e] * sc;
-        hb[e] = e4m3_of(xs);
-        lb[e] = e4m3_of(xs - f32_of_e4m3(hb[e]));
-      }
-      const int off = sw128_offset(r, piece * 8);
-      *reinterpret_cast<uint2*>(qhi + off) = *reinterpret_cast<const uint2*>(hb);
-      *reinterpret_cast<uint2*>(qlo + off) = *reinterpret_cast<const uint2*>(lb);
+    for (int e = 0; e < 8; ++e) {
+      const float xs = x[e] * sc;
+      hb[e] = e4m3_of(xs);
+      lb[e] = e4m3_of(xs - f32_of_e4m3(hb[e]));
     }
+    const int off = sw128_offset(item >> 4, (item & 15) * 8);
+    *reinterpret_cast<uint2*>(qhi + off) = *reinterpret_cast<const uint2*>(hb);
+    *reinterpret_cast<uint2*>(qlo + off) = *reinterpret_cast<const uint2*>(lb);
   }
   fence_proxy_async_smem();
   return p.score_scale / sc;
@@ -527,6 +574,9 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
   // Q and P tiles start zero (rows R..NQ-1 stay zero); row -> token table; barriers; tensor memory
   for (int i = tid; i < 8 * L::kQBytes / 16; i += L::kThreads)
     reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if constexpr (L::kMmaL)
+    for (int i = tid; i < L::kKvBytes / 16; i += L::kThreads)   // e4m3 1.0 = 0x38
+      reinterpret_cast<uint4*>(smem + L::kOnesOffset)[i] = make_uint4(0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u);
   if (tid < ROWS) rowt[tid] = tid / p.group;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -598,7 +648,7 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
         __syncwarp();
         if (lane == 0) mbar_arrive(&kv_full[(i - kPf) % STAGES]);
       }
-      const bool ok = mbar_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
+      const bool ok = attn_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
       if (!__all_sync(0xffffffffu, ok)) break;
       const int* rt = bt_ring + (i % kPf) * kAttnTile;
       const int nvalid = cur.L - (cur.lo + cur.tile * kAttnTile);   // keys of this tile inside the sequence
@@ -637,6 +687,8 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
       constexpr uint32_t kIdQK = idesc_e4m3_f32(128, NQ, false, false);
       constexpr uint32_t kIdPV = idesc_e4m3_f32(128, NQ, true, false);
       const uint32_t o_tmem = tmem_base + 2 * NQ;
+      const uint32_t l_tmem = tmem_base + 3 * NQ;
+      (void)l_tmem;
       AttnCursor cur;
       cur.init(p, b0, g0, t0, count);
       bool ok = true, issued = false;
@@ -645,8 +697,8 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
       // O^T (+)= V^T P^T for tile j (after the softmax wrote P^T[j & 1]); frees the K/V stage and P buffer
       auto issue_pv = [&](int j, int seg, bool start) -> bool {
         const int uj = j & 1, sj = j % STAGES;
-        if (!mbar_wait(&p_full[uj], (j >> 1) & 1, abort_flag, kSiteAttnMmaP)) return false;
-        if (start && seg > 0 && !mbar_wait(o_free, (seg - 1) & 1, abort_flag, kSiteAttnMmaOFree)) return false;
+        if (!attn_wait(&p_full[uj], (j >> 1) & 1, abort_flag, kSiteAttnMmaP)) return false;
+        if (start && seg > 0 && !attn_wait(o_free, (seg - 1) & 1, abort_flag, kSiteAttnMmaOFree)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + sj * L::kStageBytes + L::kKvBytes);
         const uint32_t ph_addr = smem_u32(ptile + (2 * uj) * L::kQBytes);
@@ -659,15 +711,27 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
         for (int ks = 0; ks < kAttnTile / 32; ++ks)
           mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(pl_addr + ks * 32), kIdPV,
                    1u);
+        if constexpr (L::kMmaL) {
+          // row sums: ones[128 x keys] P^T, every TMEM lane gets the same sums
+          const uint32_t ones_addr = smem_u32(smem + L::kOnesOffset);
+#pragma unroll
+          for (int ks = 0; ks < kAttnTile / 32; ++ks)
+            mma_e4m3(l_tmem, sdesc_sw128_kmajor(ones_addr + ks * 32), sdesc_sw128_kmajor(ph_addr + ks * 32), kIdQK,
+                     (start && ks == 0) ? 0u : 1u);
+#pragma unroll
+          for (int ks = 0; ks < kAttnTile / 32; ++ks)
+            mma_e4m3(l_tmem, sdesc_sw128_kmajor(ones_addr + ks * 32), sdesc_sw128_kmajor(pl_addr + ks * 32), kIdQK,
+                     1u);
+        }
         mma_commit(&kv_empty[sj]);
         mma_commit(&pv_done[uj]);
         return true;
       };
       for (int i = 0; ok && cur.remaining > 0; ++i, cur.next(p)) {
         const int s = i % STAGES, u = i & 1;
-        if (!mbar_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
-        if (cur.seg_start && !mbar_wait(&q_full[cur.seg & 1], (cur.seg >> 1) & 1, abort_flag, kSiteAttnMmaQ)) break;
-        if (!mbar_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
+        if (!attn_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
+        if (cur.seg_start && !attn_wait(&q_full[cur.seg & 1], (cur.seg >> 1) & 1, abort_flag, kSiteAttnMmaQ)) break;
+        if (!attn_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + s * L::kStageBytes);
         const uint32_t qh_addr = smem_u32(qtile + (2 * (cur.seg & 1)) * L::kQBytes);
@@ -754,50 +818,75 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
         }
         if (tid == 0 && cur.tile == 0) p.meta[bg * 2] = blockIdx.x;
       }
-      // ---- scores of this thread's key for its rows (log2 units), masked
-      const bool got = __all_sync(0xffffffffu, mbar_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
+      // ---- scores of this thread's key for its rows (log2 units), masked, read from S^T in chunks of CH rows.
+      // Up to 8 rows per thread they are read once and kept (S^T[u] is released at once); with more rows they are
+      // read again after the vote rather than kept in registers across it.
+      constexpr bool kHold = RPT <= 8;
+      constexpr int CH = RPT < 8 ? RPT : 8;
+      const bool got = __all_sync(0xffffffffu, attn_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
       ok = ok && got;
-      float x[RPT];
-      {
-        uint32_t acc[RPT];
+      const float qcs = (cur.seg & 1) ? qsc1 : qsc0;
+      const int k0 = cur.lo + cur.tile * kAttnTile;
+      const int pos = k0 + key;
+      const int new0 = cur.L - p.T;
+      // every row sees every key of an interior tile: before the first query and inside every window
+      const bool interior = k0 + kAttnTile - 1 <= new0 && (p.window == 0 || k0 > cur.L - 1 - p.window);
+      auto load_x = [&](int c, float (&xv)[CH]) {
+        uint32_t acc[CH];
         if (got) {
-          tc_fence_after();
-          tmem_ld_cols<RPT>(lane_addr + u * NQ + r0, acc);
+          tmem_ld_cols<CH>(lane_addr + u * NQ + r0 + c * CH, acc);
           tmem_ld_wait();
         }
-        tc_fence_before();
-        mbar_arrive(&s_free[u]);
-        const float qcs = (cur.seg & 1) ? qsc1 : qsc0;
-        const int k0 = cur.lo + cur.tile * kAttnTile;
-        const int pos = k0 + key;
-        const int new0 = cur.L - p.T;
-        // every row sees every key of an interior tile: before the first query and inside every window
-        const bool interior = k0 + kAttnTile - 1 <= new0 && (p.window == 0 || k0 > cur.L - 1 - p.window);
 #pragma unroll
-        for (int j = 0; j < RPT; ++j) {
-          const int r = r0 + j;
-          float v = got ? __uint_as_float(acc[j]) * qcs : -INFINITY;
+        for (int e = 0; e < CH; ++e) {
+          const int r = r0 + c * CH + e;
+          float v = got ? __uint_as_float(acc[e]) * qcs : -INFINITY;
           if (r >= p.R) {
             v = -INFINITY;
           } else if (!interior) {
             const int qpos = new0 + rowt[r];
             if (pos > qpos || (p.window > 0 && pos <= qpos - p.window)) v = -INFINITY;
           }
-          x[j] = v;
+          xv[e] = v;
         }
+      };
+      if (got) tc_fence_after();
+      float xr[CH];
+      if constexpr (kHold) {
+        load_x(0, xr);
+        tc_fence_before();
+        mbar_arrive(&s_free[u]);
       }
+      auto get_x = [&](int c, float (&xv)[CH]) {
+        if constexpr (kHold) {
+#pragma unroll
+          for (int e = 0; e < CH; ++e) xv[e] = xr[e];
+        } else {
+          load_x(c, xv);
+        }
+      };
       // ---- the running maxima change only when some score exceeds its row's maximum by more than 2^tau (and on
       // a segment's first tile, where they are -inf): one CTA-wide vote; only then the tile's row maxima are
       // exchanged across the 128 keys (warp redux, then the four quads through shared memory) and O^T rescaled.
       bool over = false;
 #pragma unroll
-      for (int j = 0; j < RPT; ++j) over = over || x[j] > m_used[j] + kTau;
+      for (int c = 0; c < RPT / CH; ++c) {
+        float xv[CH];
+        get_x(c, xv);
+#pragma unroll
+        for (int e = 0; e < CH; ++e) over = over || xv[e] > m_used[c * CH + e] + kTau;
+      }
       if (soft_bar_or(L::kSoftThreads, over || !ok)) {
         float* xc = xch + (i & 1) * ROWS * 4;
 #pragma unroll
-        for (int j = 0; j < RPT; ++j) {
-          const float wm = warp_max_f32(x[j]);
-          if (static_cast<int>(lane) == j) xc[(r0 + j) * 4 + quad] = wm;
+        for (int c = 0; c < RPT / CH; ++c) {
+          float xv[CH];
+          get_x(c, xv);
+#pragma unroll
+          for (int e = 0; e < CH; ++e) {
+            const float wm = warp_max_f32(xv[e]);
+            if (static_cast<int>(lane) == c * CH + e) xc[(r0 + c * CH + e) * 4 + quad] = wm;
+          }
         }
         if (!soft_bar_and(L::kSoftThreads, ok)) break;
         float f[RPT];
@@ -812,14 +901,14 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
           } else if (tmax > m_used[j] + kTau) {
             f[j] = fast_exp2(m_used[j] - tmax);
             m_used[j] = tmax;
-            l_lane[j] *= f[j];
+            if constexpr (!L::kMmaL) l_lane[j] *= f[j];
             rescale = true;
           }
         }
         if (rescale) {
           // this warp's O^T columns (its rows, its 32 dims), PV of tile i - 1 included, times f
           const int j1 = i - 1;
-          const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
+          const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
                                                             kSiteAttnSoftPv));
           ok = ok && pv;
           if (pv) {
@@ -830,6 +919,13 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
 #pragma unroll
             for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
             tmem_st_cols<RPT>(lane_addr + 2 * NQ + r0, o);
+            if constexpr (L::kMmaL) {
+              tmem_ld_cols<RPT>(lane_addr + 3 * NQ + r0, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < RPT; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f[j]);
+              tmem_st_cols<RPT>(lane_addr + 3 * NQ + r0, o);
+            }
             tmem_st_wait();
           }
         }
@@ -838,65 +934,97 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
       // pairs of rows: f16x2 of p, its nearest e4m3 pair (hi), then the e4m3 pair of the exact f16 residual (lo).
       // The four lanes of a quad (keys 4m..4m+3) transpose their bytes so each stores whole 4-key words of one
       // row.  Rows >= R get zero.
-      if (i >= 2) ok = mbar_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
-      uint32_t hw[(RPT + 3) / 4], lw[(RPT + 3) / 4];
-#pragma unroll
-      for (int w = 0; w < (RPT + 3) / 4; ++w) hw[w] = lw[w] = 0u;
-#pragma unroll
-      for (int j = 0; j < RPT; j += 2) {
-        float pv[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          pv[e] = x[j + e] != -INFINITY ? fast_exp2(x[j + e] - m_used[j + e] + kPShift) : 0.f;
-          l_lane[j + e] += pv[e];
-        }
-        const __half2 h2 = __floats2half2_rn(pv[0], pv[1]);
-        const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
-        const __half2 hb = __half2(__nv_cvt_fp8x2_to_halfraw2(hi, __NV_E4M3));
-        const __nv_fp8x2_storage_t lo =
-            __nv_cvt_halfraw2_to_fp8x2(__half2_raw(__hsub2(h2, hb)), __NV_SATFINITE, __NV_E4M3);
-        hw[j >> 2] |= static_cast<uint32_t>(hi) << (8 * (j & 3));
-        lw[j >> 2] |= static_cast<uint32_t>(lo) << (8 * (j & 3));
-      }
+      if (i >= 2) ok = attn_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
       {
         uint8_t* ph = ptile + (2 * u) * L::kQBytes;
         uint8_t* pl = ph + L::kQBytes;
-        const int e = static_cast<int>(lane & 3);
+        const int e4 = static_cast<int>(lane & 3);
         const int kb = key & ~3;
 #pragma unroll
-        for (int w = 0; w < (RPT + 3) / 4; ++w) {
-          const uint32_t th = quad_transpose(hw[w], e), tl = quad_transpose(lw[w], e);
-          if (RPT >= 4 || e < RPT) {   // RPT = 2: bytes 2, 3 of the word are the next warp group's rows
-            const int off = sw128_offset(r0 + 4 * w + e, kb);
-            *reinterpret_cast<uint32_t*>(ph + off) = th;
-            *reinterpret_cast<uint32_t*>(pl + off) = tl;
+        for (int c = 0; c < RPT / CH; ++c) {
+          float xv[CH];
+          get_x(c, xv);
+          uint32_t hw[(CH + 3) / 4], lw[(CH + 3) / 4];
+#pragma unroll
+          for (int w = 0; w < (CH + 3) / 4; ++w) hw[w] = lw[w] = 0u;
+#pragma unroll
+          for (int e = 0; e < CH; e += 2) {
+            const int j = c * CH + e;
+            __half2 h2;
+            if constexpr (L::kMmaL) {
+              // exponent in f32, 2^x of the pair in one f16x2 instruction; the sums come from the tensor cores
+              float a[2];
+#pragma unroll
+              for (int t = 0; t < 2; ++t)
+                a[t] = xv[e + t] != -INFINITY ? xv[e + t] - m_used[j + t] + kPShift : -INFINITY;
+              const __half2 ha = __floats2half2_rn(a[0], a[1]);
+              uint32_t hv;
+              asm("ex2.approx.f16x2 %0, %1;" : "=r"(hv) : "r"(*reinterpret_cast<const uint32_t*>(&ha)));
+              h2 = *reinterpret_cast<const __half2*>(&hv);
+            } else {
+              float pv[2];
+#pragma unroll
+              for (int t = 0; t < 2; ++t) {
+                pv[t] = xv[e + t] != -INFINITY ? fast_exp2(xv[e + t] - m_used[j + t] + kPShift) : 0.f;
+                l_lane[j + t] += pv[t];
+              }
+              h2 = __floats2half2_rn(pv[0], pv[1]);
+            }
+            const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
+            // hi back in f16 without a conversion: a non-negative e4m3 byte shifted into f16 bits 7..14 is its value
+            // times 2^-8 (normal and subnormal alike), so the residual is h2 - 256 hi, exact in f16
+            const uint32_t hb_bits = __byte_perm(static_cast<uint32_t>(hi), 0u, 0x4140) << 7;
+            const __half2 res = __hfma2(*reinterpret_cast<const __half2*>(&hb_bits), __float2half2_rn(-256.f), h2);
+            const __nv_fp8x2_storage_t lo = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(res), __NV_SATFINITE, __NV_E4M3);
+            hw[e >> 2] |= static_cast<uint32_t>(hi) << (8 * (e & 3));
+            lw[e >> 2] |= static_cast<uint32_t>(lo) << (8 * (e & 3));
+          }
+#pragma unroll
+          for (int w = 0; w < (CH + 3) / 4; ++w) {
+            const uint32_t th = quad_transpose(hw[w], e4), tl = quad_transpose(lw[w], e4);
+            if (CH >= 4 || e4 < CH) {   // CH = 2: bytes 2, 3 of the word are the next warp group's rows
+              const int off = sw128_offset(r0 + c * CH + 4 * w + e4, kb);
+              *reinterpret_cast<uint32_t*>(ph + off) = th;
+              *reinterpret_cast<uint32_t*>(pl + off) = tl;
+            }
           }
         }
       }
-      fence_proxy_async_smem();
       tc_fence_before();
+      if constexpr (!kHold) mbar_arrive(&s_free[u]);   // S^T[u] read for the last time
+      fence_proxy_async_smem();
       mbar_arrive(&p_full[u]);
 
       if (cur.seg_end) {
         // ---- this segment's partial: O^T columns (thread = dim), row sums, maxima
-        const bool pv = __all_sync(0xffffffffu, mbar_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
+        const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
         ok = ok && pv;
-        uint32_t o[RPT];
+        const long long slot = static_cast<long long>(blockIdx.x) + bg;
+        float lrow = 0.f;   // kMmaL: this lane's row sum (row r0 + lane), read from the sum columns
         if (pv) {
           tc_fence_after();
+          uint32_t o[RPT];
           tmem_ld_cols<RPT>(lane_addr + 2 * NQ + r0, o);
           tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < RPT; ++j)
+            if (r0 + j < p.R) p.part_o[(slot * p.R + r0 + j) * kAttnD + key] = __uint_as_float(o[j]);
+          if constexpr (L::kMmaL) {
+            tmem_ld_cols<RPT>(lane_addr + 3 * NQ + r0, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < RPT; ++j)
+              if (static_cast<int>(lane) == j) lrow = __uint_as_float(o[j]);
+          }
         }
         tc_fence_before();
         mbar_arrive(o_free);
-        const long long slot = static_cast<long long>(blockIdx.x) + bg;
+        if constexpr (!L::kMmaL) {
 #pragma unroll
-        for (int j = 0; j < RPT; ++j) {
-          const int r = r0 + j;
-          const float ls = warp_sum_f32(l_lane[j]);
-          if (r < p.R) {
-            if (pv) p.part_o[(slot * p.R + r) * kAttnD + key] = __uint_as_float(o[j]);
-            if (lane == 0) lsum[r * 4 + quad] = ls;
+          for (int j = 0; j < RPT; ++j) {
+            const int r = r0 + j;
+            const float ls = warp_sum_f32(l_lane[j]);
+            if (r < p.R && lane == 0) lsum[r * 4 + quad] = ls;
           }
         }
         if (!soft_bar_and(L::kSoftThreads, ok)) break;
@@ -905,8 +1033,12 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
           for (int j = 0; j < RPT; ++j) {
             const int r = r0 + j;
             if (r < p.R && static_cast<int>(lane) == j) {
-              const float4 l4 = *reinterpret_cast<const float4*>(lsum + r * 4);
-              p.part_l[slot * p.R + r] = (l4.x + l4.y) + (l4.z + l4.w);
+              if constexpr (L::kMmaL) {
+                p.part_l[slot * p.R + r] = lrow;   // every TMEM lane holds the row sums
+              } else {
+                const float4 l4 = *reinterpret_cast<const float4*>(lsum + r * 4);
+                p.part_l[slot * p.R + r] = (l4.x + l4.y) + (l4.z + l4.w);
+              }
               p.part_m[slot * p.R + r] = m_used[j];
             }
           }
