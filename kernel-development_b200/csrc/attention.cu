@@ -244,6 +244,34 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void soft_bar_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
 }
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Named barrier `id` over `nthreads` threads that ORs / ANDs a predicate over them.
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0u;
+}
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0u;
+}
 // Named barrier of the softmax warps that also ORs a predicate over them.
 __device__ __forceinline__ bool soft_bar_or(int nthreads, bool v) {
   uint32_t r;
@@ -475,8 +503,8 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
 // Q rows of (b, g) as two e4m3 terms with one power-of-two scale s for the segment, chosen so the largest |q| of its
 // rows lands in [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; returns
 // score_scale / s (the same in every thread).  Run by all softmax threads (one named barrier); each fences its
-// writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.
-template <int SOFT_THREADS, int ROWS>
+// writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.  BAR: the named barrier used.
+template <int SOFT_THREADS, int ROWS, int BAR = 1>
 __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* rowmax) {
   const int tid = threadIdx.x;
   const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
@@ -507,7 +535,7 @@ __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi,
     for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (item < items && (item & 15) == 0) rowmax[item >> 4] = amax;
   }
-  soft_bar_sync(SOFT_THREADS);
+  named_bar_sync(BAR, SOFT_THREADS);
   float amax = 0.f;
   for (int r = 0; r < p.R; ++r) amax = fmaxf(amax, rowmax[r]);
   // power-of-two scale: amax * s in [128, 256); exponent clamped so s stays a finite normal float
@@ -1058,6 +1086,457 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
 }
 
 // ---------------------------------------------------------------------------------------------
+// Many query rows (verify: T x group up to 64): one thread per query row.  S = Q K^T with the query rows in the
+// TMEM lanes (M = 128, rows 64..127 zero), so a row's 128 scores sit in one thread: its maximum, sum and
+// probabilities need no exchange between threads, and its P^T row (128 keys, K-major) is written as 16-byte
+// chunks.  O^T += V^T P^T as in the decode kernel (TMEM lanes = dims); four correction warps own those lanes:
+// they rescale O^T when a row's running maximum rises and write the partial output at a segment's end.
+// ---------------------------------------------------------------------------------------------
+template <int STAGES, int NPROD>
+struct AttnRowsLayout {
+  static constexpr int kRows = 64;                    // query rows handled (R <= 64)
+  static constexpr int kSoftWarps = 2;                // rows 0..63 = TMEM lanes 0..63
+  static constexpr int kCorrWarps = 4;                // TMEM lanes 0..127 of O^T
+  static constexpr int kSoftThreads = 32 * kSoftWarps;
+  static constexpr int kThreads = 32 * (kSoftWarps + kCorrWarps + NPROD + 1);
+  static constexpr int kPf = STAGES - 2;
+  static constexpr int kKvBytes = kAttnTile * kAttnD;
+  static constexpr int kStageBytes = 2 * kKvBytes;
+  static constexpr int kQBytes = 128 * kAttnD;        // one e4m3 term of Q: 128 rows (64 used) x 128 B
+  static constexpr int kPBytes = kRows * kAttnTile;   // one e4m3 term of P^T: 64 rows x 128 keys
+  static constexpr int kQOffset = STAGES * kStageBytes;          // Q[buffer][hi, lo]
+  static constexpr int kPOffset = kQOffset + 4 * kQBytes;        // P^T[buffer][hi, lo]
+  static constexpr int kFOffset = kPOffset + 4 * kPBytes;        // rescale factors [2][64] + flags [2]
+  static constexpr int kRowmaxOffset = kFOffset + 2 * kRows * 4 + 16;   // |q| maxima [2][64]
+  static constexpr int kBtOffset = kRowmaxOffset + 2 * kRows * 4;        // block-table rings [NPROD][kPf][128]
+  static constexpr int kBarOffset = kBtOffset + NPROD * kPf * kAttnTile * 4;
+  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2], f_ready[2], o_free, drain
+  static constexpr int kNumBars = 2 * STAGES + 14;
+  static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
+  static constexpr int kSmemBytes = kMiscOffset + 48 * 4 + 1024;
+  static constexpr uint32_t kTmemCols = 512;          // S^T... S[2] at [0, 256), O^T at [256, 320)
+  static constexpr int kOCol = 256;
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+template <int STAGES, int NPROD>
+__global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) attn_rows_kernel(const AttnParams p) {
+  using L = AttnRowsLayout<STAGES, NPROD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* kv_empty = kv_full + STAGES;
+  uint64_t* s_full = kv_empty + STAGES;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_full = pv_done + 2;
+  uint64_t* f_ready = q_full + 2;
+  uint64_t* o_free = f_ready + 2;
+  uint64_t* drain = o_free + 1;
+  int* misc = reinterpret_cast<int*>(smem + L::kMiscOffset);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc);
+  volatile int* abort_flag = misc + 1;
+  int* scratch = misc + 8;
+  float* fbuf = reinterpret_cast<float*>(smem + L::kFOffset);                       // [2][64]
+  int* fflag = reinterpret_cast<int*>(smem + L::kFOffset + 2 * L::kRows * 4);       // [2]
+  float* rowmax = reinterpret_cast<float*>(smem + L::kRowmaxOffset);
+  int* bt_ring = reinterpret_cast<int*>(smem + L::kBtOffset);
+  uint8_t* qtile = smem + L::kQOffset;
+  uint8_t* ptile = smem + L::kPOffset;
+
+  const int warp = warp_id_uniform();
+  const uint32_t lane = lane_id();
+  const int tid = threadIdx.x;
+  constexpr int kCorrWarp0 = L::kSoftWarps;
+  constexpr int kProducerWarp = L::kSoftWarps + L::kCorrWarps;
+  constexpr int kMmaWarp = kProducerWarp + NPROD;
+
+  int b0 = 0, g0 = 0, t0 = 0;
+  const int count = attn_locate(p, scratch, &b0, &g0, &t0);
+  if (count == 0) return;
+
+  for (int i = tid; i < (4 * L::kQBytes + 4 * L::kPBytes) / 16; i += L::kThreads)
+    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);   // Q rows 64..127 stay zero
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], NPROD);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int u = 0; u < 2; ++u) {
+      mbar_init(&s_full[u], 1);
+      mbar_init(&s_free[u], L::kSoftThreads);
+      mbar_init(&p_full[u], L::kSoftThreads + 32 * L::kCorrWarps);
+      mbar_init(&pv_done[u], 1);
+      mbar_init(&q_full[u], L::kSoftThreads);
+      mbar_init(&f_ready[u], L::kSoftThreads);
+    }
+    mbar_init(o_free, 32 * L::kCorrWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp >= kProducerWarp && warp < kMmaWarp) {
+    // ------------------------------------------------------------------ producers (as in attn_fwd_kernel)
+    constexpr int kPf = L::kPf;
+    const int wp = warp - kProducerWarp;
+    bt_ring += wp * kPf * kAttnTile;
+    const int chunk = static_cast<int>(lane & 7), ksub = static_cast<int>(lane >> 3);
+    AttnCursor cur, pf;
+    cur.init(p, b0, g0, t0, count);
+    pf.init(p, b0, g0, t0, count);
+    auto prefetch = [&](int buf) {
+      const int k0 = pf.lo + pf.tile * kAttnTile;
+      const int* src = p.block_table + static_cast<long long>(pf.b) * p.max_len;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int idx = 4 * static_cast<int>(lane) + j;
+        if (k0 + idx < pf.L) cp_async_4(bt_ring + buf * kAttnTile + idx, src + k0 + idx);
+      }
+    };
+#pragma unroll 1
+    for (int d = 0; d < kPf; ++d) {
+      if (pf.remaining > 0) {
+        prefetch(d);
+        pf.next(p);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    pdl_wait();   // the new tokens' rows are written by the append kernel launched just before
+    int issued = 0;
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int s = i % STAGES;
+      if (i >= kPf) {
+        cp_async_wait<kPf - 1>();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kv_full[(i - kPf) % STAGES]);
+      }
+      const bool ok = attn_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int* rt = bt_ring + (i % kPf) * kAttnTile;
+      const int nvalid = cur.L - (cur.lo + cur.tile * kAttnTile);
+      const uint8_t* kbase = p.k_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
+      const uint8_t* vbase = p.v_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
+      uint8_t* st = smem + s * L::kStageBytes;
+#pragma unroll 8
+      for (int j = wp; j < kAttnTile / 4; j += NPROD) {
+        const int key = 4 * j + ksub;
+        int slot = rt[key < nvalid ? key : nvalid - 1];
+        if (slot < 0 || slot >= p.slots) {
+          report(KDB_ERR_DEVICE_BOUNDS, kSiteAttnSlot);
+          slot = 0;
+        }
+        const long long off = static_cast<long long>(slot) * p.Hkv * kAttnD;
+        const int dst = key * 128 + ((chunk ^ (key & 7)) << 4);
+        cp_async_16(st + dst, kbase + off);
+        cp_async_16(st + L::kKvBytes + dst, vbase + off);
+      }
+      __syncwarp();
+      if (pf.remaining > 0) {
+        prefetch(i % kPf);
+        pf.next(p);
+      }
+      cp_async_commit();
+      issued = i + 1;
+    }
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0)
+      for (int t = issued > kPf ? issued - kPf : 0; t < issued; ++t) mbar_arrive(&kv_full[t % STAGES]);
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, 128, false, false);   // S[rows x keys]
+      constexpr uint32_t kIdPV = idesc_e4m3_f32(128, 64, true, false);     // O^T[dims x rows]
+      const uint32_t o_tmem = tmem_base + L::kOCol;
+      AttnCursor cur;
+      cur.init(p, b0, g0, t0, count);
+      bool ok = true, issued = false;
+      int prev_i = -1, prev_seg = 0;
+      bool prev_start = false;
+      auto issue_pv = [&](int j, int seg, bool start) -> bool {
+        const int uj = j & 1, sj = j % STAGES;
+        if (!attn_wait(&p_full[uj], (j >> 1) & 1, abort_flag, kSiteAttnMmaP)) return false;
+        if (start && seg > 0 && !attn_wait(o_free, (seg - 1) & 1, abort_flag, kSiteAttnMmaOFree)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + sj * L::kStageBytes + L::kKvBytes);
+        const uint32_t ph_addr = smem_u32(ptile + (2 * uj) * L::kPBytes);
+        const uint32_t pl_addr = ph_addr + L::kPBytes;
+#pragma unroll
+        for (int ks = 0; ks < kAttnTile / 32; ++ks)
+          mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(ph_addr + ks * 32), kIdPV,
+                   (start && ks == 0) ? 0u : 1u);
+#pragma unroll
+        for (int ks = 0; ks < kAttnTile / 32; ++ks)
+          mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(pl_addr + ks * 32), kIdPV,
+                   1u);
+        mma_commit(&kv_empty[sj]);
+        mma_commit(&pv_done[uj]);
+        return true;
+      };
+      for (int i = 0; ok && cur.remaining > 0; ++i, cur.next(p)) {
+        const int s = i % STAGES, u = i & 1;
+        if (!attn_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
+        if (cur.seg_start && !attn_wait(&q_full[cur.seg & 1], (cur.seg >> 1) & 1, abort_flag, kSiteAttnMmaQ)) break;
+        if (!attn_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + s * L::kStageBytes);
+        const uint32_t qh_addr = smem_u32(qtile + (2 * (cur.seg & 1)) * L::kQBytes);
+        const uint32_t ql_addr = qh_addr + L::kQBytes;
+        const uint32_t s_tmem = tmem_base + u * 128;
+#pragma unroll
+        for (int ks = 0; ks < kAttnD / 32; ++ks)
+          mma_e4m3(s_tmem, sdesc_sw128_kmajor(qh_addr + ks * 32), sdesc_sw128_kmajor(k_addr + ks * 32), kIdQK,
+                   ks > 0 ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < kAttnD / 32; ++ks)
+          mma_e4m3(s_tmem, sdesc_sw128_kmajor(ql_addr + ks * 32), sdesc_sw128_kmajor(k_addr + ks * 32), kIdQK, 1u);
+        mma_commit(&s_full[u]);
+        issued = true;
+        if (prev_i >= 0 && !issue_pv(prev_i, prev_seg, prev_start)) {
+          ok = false;
+          break;
+        }
+        prev_i = i;
+        prev_seg = cur.seg;
+        prev_start = cur.seg_start;
+      }
+      if (ok && prev_i >= 0 && !*abort_flag) issue_pv(prev_i, prev_seg, prev_start);
+      if (issued) {
+        mma_commit(drain);
+        mbar_wait_drain(drain, 0, kSiteAttnDrainMma);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax (rows) and correction (dims)
+    const bool soft = warp < kCorrWarp0;
+    const int quad = warp & 3;
+    const int r = warp * 32 + static_cast<int>(lane);   // softmax: this thread's query row (0..63)
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    constexpr float kTau = 4.f;
+    constexpr float kPShift = 4.f;
+
+    // the queries are prepared by the two softmax warps alone (named barrier 2): the correction warps share no
+    // barrier with them and may leave on their own after a timed-out wait
+    AttnCursor qcur;
+    qcur.init(p, b0, g0, t0, count);
+    float qsc0 = 0.f, qsc1 = 0.f;   // score scales of the segments in Q buffers 0 and 1
+    bool q_more = false;
+    if (soft) {
+      qsc0 = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(p, qcur.b, qcur.g, qtile, qtile + L::kQBytes, rowmax);
+      mbar_arrive(&q_full[0]);
+      q_more = qcur.next_segment(p);
+      if (q_more) {
+        qsc1 = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(p, qcur.b, qcur.g, qtile + 2 * L::kQBytes,
+                                                          qtile + 3 * L::kQBytes, rowmax + L::kRows);
+        mbar_arrive(&q_full[1]);
+      }
+    }
+
+    AttnCursor cur;
+    cur.init(p, b0, g0, t0, count);
+    float m_run = -INFINITY, l_run = 0.f;   // softmax: this row's running maximum (log2) and sum
+    const int trow = r / p.group;            // token of the row
+    bool ok = true;
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int u = i & 1;
+      const int bg = cur.b * p.Hkv + cur.g;
+      if (cur.seg_start) {
+        if (soft && cur.seg >= 1 && q_more) {
+          q_more = qcur.next_segment(p);
+          if (q_more) {
+            const int qb = (cur.seg + 1) & 1;
+            const float sc = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(
+                p, qcur.b, qcur.g, qtile + 2 * qb * L::kQBytes, qtile + (2 * qb + 1) * L::kQBytes,
+                rowmax + qb * L::kRows);
+            if (qb == 0) {
+              qsc0 = sc;
+            } else {
+              qsc1 = sc;
+            }
+            mbar_arrive(&q_full[qb]);
+          }
+        }
+        m_run = -INFINITY;
+        l_run = 0.f;
+        if (tid == 0 && cur.tile == 0) p.meta[bg * 2] = blockIdx.x;
+      }
+      const long long slot = static_cast<long long>(blockIdx.x) + bg;
+      if (soft) {
+        // ---- this row's 128 scores: maximum (pass 1), then probabilities into P^T (pass 2)
+        const bool got = __all_sync(0xffffffffu, attn_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
+        ok = ok && got;
+        const float qcs = (cur.seg & 1) ? qsc1 : qsc0;
+        const int k0 = cur.lo + cur.tile * kAttnTile;
+        const int qpos = cur.L - p.T + trow;
+        const bool live = r < p.R;
+        // keys [k0 + klo, k0 + khi) of this tile are this row's (causal and window limits)
+        int khi = qpos - k0 + 1;
+        khi = khi < 0 ? 0 : (khi > kAttnTile ? kAttnTile : khi);
+        int klo = p.window > 0 ? qpos - p.window + 1 - k0 : 0;
+        klo = klo < 0 ? 0 : (klo > kAttnTile ? kAttnTile : klo);
+        if (!live) khi = 0;
+        if (got) tc_fence_after();
+        float tmax = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < kAttnTile / 32; ++c) {
+          uint32_t acc[32];
+          if (got) {
+            tmem_ld_32x32b_x32(lane_addr + u * 128 + 32 * c, acc);
+            tmem_ld_wait();
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int k = 32 * c + e;
+            if (got && k >= klo && k < khi) tmax = fmaxf(tmax, __uint_as_float(acc[e]));
+          }
+        }
+        tmax = tmax == -INFINITY ? tmax : tmax * qcs;
+        float f = 1.f;
+        bool resc = false;
+        if (m_run == -INFINITY) {
+          m_run = tmax;
+        } else if (tmax > m_run + kTau) {
+          f = fast_exp2(m_run - tmax);
+          m_run = tmax;
+          l_run *= f;
+          resc = true;
+        }
+        // tell the correction warps whether (and by how much) to rescale O^T before this tile's PV; the two
+        // softmax warps agree on leaving after a timed-out wait here (named barrier 2)
+        if (!named_bar_and(2, L::kSoftThreads, ok)) break;
+        const bool any = named_bar_or(2, L::kSoftThreads, resc);
+        fbuf[u * L::kRows + r] = f;
+        if (r == 0) fflag[u] = any ? 1 : 0;
+        mbar_arrive(&f_ready[u]);
+        if (i >= 2) ok = attn_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
+        uint8_t* ph = ptile + (2 * u) * L::kPBytes;
+        uint8_t* pl = ph + L::kPBytes;
+        const float shift = kPShift - m_run;
+#pragma unroll 1
+        for (int c = 0; c < kAttnTile / 32; ++c) {
+          uint32_t acc[32];
+          if (got) {
+            tmem_ld_32x32b_x32(lane_addr + u * 128 + 32 * c, acc);
+            tmem_ld_wait();
+          }
+          uint32_t hw[8], lw[8];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float a[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int k = 32 * c + e + t;
+              a[t] = (got && k >= klo && k < khi && m_run != -INFINITY)
+                         ? fmaf(__uint_as_float(acc[e + t]), qcs, shift) : -INFINITY;
+            }
+            const __half2 ha = __floats2half2_rn(a[0], a[1]);
+            uint32_t hv;
+            asm("ex2.approx.f16x2 %0, %1;" : "=r"(hv) : "r"(*reinterpret_cast<const uint32_t*>(&ha)));
+            const __half2 h2 = *reinterpret_cast<const __half2*>(&hv);
+            const float2 pf2 = __half22float2(h2);
+            l_run += pf2.x + pf2.y;
+            const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
+            const uint32_t hb_bits = __byte_perm(static_cast<uint32_t>(hi), 0u, 0x4140) << 7;
+            const __half2 res = __hfma2(*reinterpret_cast<const __half2*>(&hb_bits), __float2half2_rn(-256.f), h2);
+            const __nv_fp8x2_storage_t lo = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(res), __NV_SATFINITE, __NV_E4M3);
+            if ((e & 2) == 0) {
+              hw[e >> 2] = static_cast<uint32_t>(hi);
+              lw[e >> 2] = static_cast<uint32_t>(lo);
+            } else {
+              hw[e >> 2] |= static_cast<uint32_t>(hi) << 16;
+              lw[e >> 2] |= static_cast<uint32_t>(lo) << 16;
+            }
+          }
+          // keys 32c .. 32c+31 of row r: 16-byte chunks 2c and 2c+1 of the swizzled [64][128 B] tile
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int off = sw128_offset(r, 32 * c + 16 * h);
+            *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[4 * h], hw[4 * h + 1], hw[4 * h + 2], hw[4 * h + 3]);
+            *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[4 * h], lw[4 * h + 1], lw[4 * h + 2], lw[4 * h + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s_free[u]);
+        fence_proxy_async_smem();
+        mbar_arrive(&p_full[u]);
+        if (cur.seg_end && live) {
+          p.part_m[slot * p.R + r] = m_run;
+          p.part_l[slot * p.R + r] = l_run;
+        }
+      } else {
+        // ---- correction warps (thread = dim): rescale O^T when asked, then write the partial at a segment end
+        const int dim = quad * 32 + static_cast<int>(lane);
+        ok = __all_sync(0xffffffffu, attn_wait(&f_ready[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv)) && ok;
+        if (ok && fflag[u]) {
+          const int j1 = i - 1;
+          const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
+                                                            kSiteAttnSoftPv));
+          ok = ok && pv;
+          if (pv) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(lane_addr + L::kOCol + 32 * c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fbuf[u * L::kRows + 32 * c + e]);
+              tmem_st_cols<32>(lane_addr + L::kOCol + 32 * c, o);
+            }
+            tmem_st_wait();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&p_full[u]);
+        if (cur.seg_end) {
+          const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
+          ok = ok && pv;
+          if (pv) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld_32x32b_x32(lane_addr + L::kOCol + 32 * c, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (32 * c + e < p.R) p.part_o[(slot * p.R + 32 * c + e) * kAttnD + dim] = __uint_as_float(o[e]);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(o_free);
+        }
+      }
+      if (tid == 0 && cur.seg_end && cur.tile == cur.ntiles - 1) p.meta[bg * 2 + 1] = blockIdx.x;
+      if (!soft && !__all_sync(0xffffffffu, ok)) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // append: one warp per new (sequence, token, KV head) row, four values per lane
 // ---------------------------------------------------------------------------------------------
 struct AttnAppendParams {
@@ -1249,6 +1728,40 @@ static int attn_launch_fwd(const AttnParams& p, long long max_tiles, int* ctas_o
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, p));
 }
 
+template <int STAGES, int NPROD>
+static int attn_launch_rows(const AttnParams& p, long long max_tiles, int* ctas_out, cudaStream_t s) {
+  using L = AttnRowsLayout<STAGES, NPROD>;
+  auto kern = attn_rows_kernel<STAGES, NPROD>;
+  static bool done[64] = {false};
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev));
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return KDB_ERR_UNSUPPORTED;
+  if (!done[dev]) {
+    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes));
+    if (rc) return rc;
+    done[dev] = true;
+  }
+  // one CTA per SM (512 TMEM columns); at least four tiles per CTA once the work covers the GPU
+  long long c = max_tiles <= 32 ? max_tiles : (max_tiles + 3) / 4;
+  if (max_tiles > 32 && c < 32) c = 32;
+  if (c > num_sms()) c = num_sms();
+  if (c > kAttnMaxCtas) c = kAttnMaxCtas;
+  if (c < 1) c = 1;
+  *ctas_out = static_cast<int>(c);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned int>(c), 1, 1);
+  cfg.blockDim = dim3(L::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p));
+}
+
 int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                     const int* block_table, const int* seq_lens, float kv_scale, void* out, long long B, long long T,
                     long long Hq, long long Hkv, long long D, long long max_len, long long slots, long long window,
@@ -1313,7 +1826,7 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
   int ctas = 0;
   rc = R <= 8    ? attn_launch_fwd<16, 8, 2, 6, 4>(p, max_tiles, &ctas, s)
        : R <= 16 ? attn_launch_fwd<16, 16, 2, 6, 4>(p, max_tiles, &ctas, s)
-                 : attn_launch_fwd<64, 64, 4, 4, 2>(p, max_tiles, &ctas, s);
+                 : attn_launch_rows<3, 2>(p, max_tiles, &ctas, s);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned int>(B * Hkv * R), 1, 1);
