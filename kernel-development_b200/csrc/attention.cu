@@ -503,10 +503,11 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
 // Q rows of (b, g) as two e4m3 terms with one power-of-two scale s for the segment, chosen so the largest |q| of its
 // rows lands in [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; returns
 // score_scale / s (the same in every thread).  Run by all softmax threads (one named barrier); each fences its
-// writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.  BAR: the named barrier used.
+// writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.  BAR: the named barrier used; tid: the
+// thread's index among the SOFT_THREADS taking part.
 template <int SOFT_THREADS, int ROWS, int BAR = 1>
-__device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* rowmax) {
-  const int tid = threadIdx.x;
+__device__ float attn_prepare_q_t(const AttnParams& p, int tid, int b, int g, uint8_t* qhi, uint8_t* qlo,
+                                  float* rowmax) {
   const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
   auto load = [&](int item, float (&x)[8]) {
     const int r = item >> 4, piece = item & 15;
@@ -559,6 +560,10 @@ __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi,
   }
   fence_proxy_async_smem();
   return p.score_scale / sc;
+}
+template <int SOFT_THREADS, int ROWS>
+__device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi, uint8_t* qlo, float* rowmax) {
+  return attn_prepare_q_t<SOFT_THREADS, ROWS, 1>(p, static_cast<int>(threadIdx.x), b, g, qhi, qlo, rowmax);
 }
 
 template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
@@ -1092,25 +1097,32 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
 // chunks.  O^T += V^T P^T as in the decode kernel (TMEM lanes = dims); four correction warps own those lanes:
 // they rescale O^T when a row's running maximum rises and write the partial output at a segment's end.
 // ---------------------------------------------------------------------------------------------
+// Warps: 0, 1 and 4, 5 softmax (rows 0..63 = TMEM lanes 0..63; keys 0..63 / 64..127 of each tile); 2, 3, 8, 9
+// correction (TMEM lanes 64..127 / 0..63 of O^T); 6, 7 producers; 10 MMA.
 template <int STAGES, int NPROD>
 struct AttnRowsLayout {
+  static_assert(NPROD == 2, "warp map");
   static constexpr int kRows = 64;                    // query rows handled (R <= 64)
-  static constexpr int kSoftWarps = 2;                // rows 0..63 = TMEM lanes 0..63
-  static constexpr int kCorrWarps = 4;                // TMEM lanes 0..127 of O^T
-  static constexpr int kSoftThreads = 32 * kSoftWarps;
-  static constexpr int kThreads = 32 * (kSoftWarps + kCorrWarps + NPROD + 1);
+  static constexpr int kSoftThreads = 128;            // two threads per row, 64 keys each
+  static constexpr int kCorrThreads = 128;
+  static constexpr int kThreads = 32 * 11;
   static constexpr int kPf = STAGES - 2;
   static constexpr int kKvBytes = kAttnTile * kAttnD;
   static constexpr int kStageBytes = 2 * kKvBytes;
-  static constexpr int kQBytes = 128 * kAttnD;        // one e4m3 term of Q: 128 rows (64 used) x 128 B
+  // Q: [hi][lo][zeros], 64 rows x 128 B each.  The QK MMA reads 128 rows from hi (its rows 64..127 are lo) and
+  // from lo (rows 64..127 zero): only S rows 0..63 (TMEM lanes 0..63) are read, so the upper rows need no zeros
+  // of their own.  One buffer: a segment's Q is written after the last QK of the previous segment completed.
+  static constexpr int kQBytes = kRows * kAttnD;      // one e4m3 term of Q: 64 rows x 128 B
   static constexpr int kPBytes = kRows * kAttnTile;   // one e4m3 term of P^T: 64 rows x 128 keys
-  static constexpr int kQOffset = STAGES * kStageBytes;          // Q[buffer][hi, lo]
-  static constexpr int kPOffset = kQOffset + 4 * kQBytes;        // P^T[buffer][hi, lo]
+  static constexpr int kQOffset = STAGES * kStageBytes;          // Q hi, lo, zeros
+  static constexpr int kPOffset = kQOffset + 3 * kQBytes;        // P^T[buffer][hi, lo]
   static constexpr int kFOffset = kPOffset + 4 * kPBytes;        // rescale factors [2][64] + flags [2]
-  static constexpr int kRowmaxOffset = kFOffset + 2 * kRows * 4 + 16;   // |q| maxima [2][64]
+  static constexpr int kXOffset = kFOffset + 2 * kRows * 4 + 16;        // half-tile maxima [2][64], row sums [64]
+  static constexpr int kRowmaxOffset = kXOffset + 3 * kRows * 4;        // |q| maxima [2][64]
   static constexpr int kBtOffset = kRowmaxOffset + 2 * kRows * 4;        // block-table rings [NPROD][kPf][128]
   static constexpr int kBarOffset = kBtOffset + NPROD * kPf * kAttnTile * 4;
-  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2], f_ready[2], o_free, drain
+  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2] (one used), f_ready[2], o_free,
+  // drain
   static constexpr int kNumBars = 2 * STAGES + 14;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOffset + 48 * 4 + 1024;
@@ -1141,6 +1153,8 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   float* fbuf = reinterpret_cast<float*>(smem + L::kFOffset);                       // [2][64]
   int* fflag = reinterpret_cast<int*>(smem + L::kFOffset + 2 * L::kRows * 4);       // [2]
   float* rowmax = reinterpret_cast<float*>(smem + L::kRowmaxOffset);
+  float* xmax = reinterpret_cast<float*>(smem + L::kXOffset);   // [2][64]: half 1's tile maxima by tile parity
+  float* lhalf = xmax + 2 * L::kRows;                            // [64]: half 1's row sums at a segment end
   int* bt_ring = reinterpret_cast<int*>(smem + L::kBtOffset);
   uint8_t* qtile = smem + L::kQOffset;
   uint8_t* ptile = smem + L::kPOffset;
@@ -1148,16 +1162,15 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
   const int tid = threadIdx.x;
-  constexpr int kCorrWarp0 = L::kSoftWarps;
-  constexpr int kProducerWarp = L::kSoftWarps + L::kCorrWarps;
-  constexpr int kMmaWarp = kProducerWarp + NPROD;
+  constexpr int kProducerWarp = 6;
+  constexpr int kMmaWarp = 10;
 
   int b0 = 0, g0 = 0, t0 = 0;
   const int count = attn_locate(p, scratch, &b0, &g0, &t0);
   if (count == 0) return;
 
-  for (int i = tid; i < (4 * L::kQBytes + 4 * L::kPBytes) / 16; i += L::kThreads)
-    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);   // Q rows 64..127 stay zero
+  for (int i = tid; i < (3 * L::kQBytes + 4 * L::kPBytes) / 16; i += L::kThreads)
+    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);   // Q rows R..63 and the zero rows stay zero
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], NPROD);
@@ -1166,12 +1179,12 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
     for (int u = 0; u < 2; ++u) {
       mbar_init(&s_full[u], 1);
       mbar_init(&s_free[u], L::kSoftThreads);
-      mbar_init(&p_full[u], L::kSoftThreads + 32 * L::kCorrWarps);
+      mbar_init(&p_full[u], L::kSoftThreads + L::kCorrThreads);
       mbar_init(&pv_done[u], 1);
       mbar_init(&q_full[u], L::kSoftThreads);
-      mbar_init(&f_ready[u], L::kSoftThreads);
+      mbar_init(&f_ready[u], L::kRows);
     }
-    mbar_init(o_free, 32 * L::kCorrWarps);
+    mbar_init(o_free, L::kCorrThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -1186,7 +1199,7 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp >= kProducerWarp && warp < kMmaWarp) {
+  if (warp >= kProducerWarp && warp < kProducerWarp + NPROD) {
     // ------------------------------------------------------------------ producers (as in attn_fwd_kernel)
     constexpr int kPf = L::kPf;
     const int wp = warp - kProducerWarp;
@@ -1291,11 +1304,11 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
       for (int i = 0; ok && cur.remaining > 0; ++i, cur.next(p)) {
         const int s = i % STAGES, u = i & 1;
         if (!attn_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
-        if (cur.seg_start && !attn_wait(&q_full[cur.seg & 1], (cur.seg >> 1) & 1, abort_flag, kSiteAttnMmaQ)) break;
+        if (cur.seg_start && !attn_wait(&q_full[0], cur.seg & 1, abort_flag, kSiteAttnMmaQ)) break;
         if (!attn_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + s * L::kStageBytes);
-        const uint32_t qh_addr = smem_u32(qtile + (2 * (cur.seg & 1)) * L::kQBytes);
+        const uint32_t qh_addr = smem_u32(qtile);
         const uint32_t ql_addr = qh_addr + L::kQBytes;
         const uint32_t s_tmem = tmem_base + u * 128;
 #pragma unroll
@@ -1323,53 +1336,33 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
     }
   } else {
     // ------------------------------------------------------------------ softmax (rows) and correction (dims)
-    const bool soft = warp < kCorrWarp0;
+    const bool soft = warp == 0 || warp == 1 || warp == 4 || warp == 5;
+    const int half = warp >> 2;                          // softmax: keys [64 half, 64 half + 64) of each tile
     const int quad = warp & 3;
-    const int r = warp * 32 + static_cast<int>(lane);   // softmax: this thread's query row (0..63)
+    const int r = quad * 32 + static_cast<int>(lane);    // softmax: this thread's query row (0..63)
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     constexpr float kTau = 4.f;
     constexpr float kPShift = 4.f;
 
-    // the queries are prepared by the two softmax warps alone (named barrier 2): the correction warps share no
+    // the queries are prepared by the softmax warps alone (named barrier 2): the correction warps share no
     // barrier with them and may leave on their own after a timed-out wait
-    AttnCursor qcur;
-    qcur.init(p, b0, g0, t0, count);
-    float qsc0 = 0.f, qsc1 = 0.f;   // score scales of the segments in Q buffers 0 and 1
-    bool q_more = false;
-    if (soft) {
-      qsc0 = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(p, qcur.b, qcur.g, qtile, qtile + L::kQBytes, rowmax);
-      mbar_arrive(&q_full[0]);
-      q_more = qcur.next_segment(p);
-      if (q_more) {
-        qsc1 = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(p, qcur.b, qcur.g, qtile + 2 * L::kQBytes,
-                                                          qtile + 3 * L::kQBytes, rowmax + L::kRows);
-        mbar_arrive(&q_full[1]);
-      }
-    }
+    float qcs = 0.f;   // the segment's score scale
+    const int stid = (warp >> 2) * 64 + quad * 32 + static_cast<int>(lane);   // 0..127 over the softmax warps
 
     AttnCursor cur;
     cur.init(p, b0, g0, t0, count);
-    float m_run = -INFINITY, l_run = 0.f;   // softmax: this row's running maximum (log2) and sum
+    float m_run = -INFINITY, l_run = 0.f;   // softmax: the row's running maximum (log2) and this half's sum
     const int trow = r / p.group;            // token of the row
     bool ok = true;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int u = i & 1;
       const int bg = cur.b * p.Hkv + cur.g;
       if (cur.seg_start) {
-        if (soft && cur.seg >= 1 && q_more) {
-          q_more = qcur.next_segment(p);
-          if (q_more) {
-            const int qb = (cur.seg + 1) & 1;
-            const float sc = attn_prepare_q<L::kSoftThreads, L::kRows, 2>(
-                p, qcur.b, qcur.g, qtile + 2 * qb * L::kQBytes, qtile + (2 * qb + 1) * L::kQBytes,
-                rowmax + qb * L::kRows);
-            if (qb == 0) {
-              qsc0 = sc;
-            } else {
-              qsc1 = sc;
-            }
-            mbar_arrive(&q_full[qb]);
-          }
+        if (soft) {
+          // the previous segment's last S was read by this thread, so its QK MMAs no longer read Q
+          qcs = attn_prepare_q_t<L::kSoftThreads, L::kRows, 2>(p, stid, cur.b, cur.g, qtile, qtile + L::kQBytes,
+                                                              rowmax);
+          mbar_arrive(&q_full[0]);
         }
         m_run = -INFINITY;
         l_run = 0.f;
@@ -1377,63 +1370,66 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
       }
       const long long slot = static_cast<long long>(blockIdx.x) + bg;
       if (soft) {
-        // ---- this row's 128 scores: maximum (pass 1), then probabilities into P^T (pass 2)
+        // ---- this thread's 64 scores of its row, read once
         const bool got = __all_sync(0xffffffffu, attn_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
         ok = ok && got;
-        const float qcs = (cur.seg & 1) ? qsc1 : qsc0;
-        const int k0 = cur.lo + cur.tile * kAttnTile;
+        const int k0 = cur.lo + cur.tile * kAttnTile + 64 * half;   // position of this thread's first key
         const int qpos = cur.L - p.T + trow;
         const bool live = r < p.R;
-        // keys [k0 + klo, k0 + khi) of this tile are this row's (causal and window limits)
+        // keys [klo, khi) of this thread's 64 are the row's (causal and window limits)
         int khi = qpos - k0 + 1;
-        khi = khi < 0 ? 0 : (khi > kAttnTile ? kAttnTile : khi);
+        khi = khi < 0 ? 0 : (khi > 64 ? 64 : khi);
         int klo = p.window > 0 ? qpos - p.window + 1 - k0 : 0;
-        klo = klo < 0 ? 0 : (klo > kAttnTile ? kAttnTile : klo);
-        if (!live) khi = 0;
-        if (got) tc_fence_after();
-        float tmax = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < kAttnTile / 32; ++c) {
-          uint32_t acc[32];
-          if (got) {
-            tmem_ld_32x32b_x32(lane_addr + u * 128 + 32 * c, acc);
-            tmem_ld_wait();
-          }
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int k = 32 * c + e;
-            if (got && k >= klo && k < khi) tmax = fmaxf(tmax, __uint_as_float(acc[e]));
-          }
+        klo = klo < 0 ? 0 : (klo > 64 ? 64 : klo);
+        if (!live || !got) khi = 0;
+        uint32_t acc[64];
+        if (got) {
+          tc_fence_after();
+          tmem_ld_32x32b_x32(lane_addr + u * 128 + 64 * half, *reinterpret_cast<uint32_t(*)[32]>(&acc[0]));
+          tmem_ld_32x32b_x32(lane_addr + u * 128 + 64 * half + 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[32]));
+          tmem_ld_wait();
         }
-        tmax = tmax == -INFINITY ? tmax : tmax * qcs;
+        tc_fence_before();
+        mbar_arrive(&s_free[u]);
+        float hmax = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 64; ++e)
+          if (e >= klo && e < khi) hmax = fmaxf(hmax, __uint_as_float(acc[e]));
+        hmax = hmax == -INFINITY ? hmax : hmax * qcs;
+        // the two halves of a row meet through shared memory: half 1's maximum before the first barrier, the row's
+        // running maximum (owned by half 0) before the second
+        if (half == 1) xmax[u * L::kRows + r] = hmax;
+        if (named_bar_or(2, L::kSoftThreads, !ok)) break;
         float f = 1.f;
         bool resc = false;
-        if (m_run == -INFINITY) {
-          m_run = tmax;
-        } else if (tmax > m_run + kTau) {
-          f = fast_exp2(m_run - tmax);
-          m_run = tmax;
-          l_run *= f;
-          resc = true;
+        if (half == 0) {
+          const float tmax = fmaxf(hmax, xmax[u * L::kRows + r]);
+          if (m_run == -INFINITY) {
+            m_run = tmax;
+          } else if (tmax > m_run + kTau) {
+            f = fast_exp2(m_run - tmax);
+            m_run = tmax;
+            resc = true;
+          }
+          fbuf[u * L::kRows + r] = f;
+          xmax[u * L::kRows + r] = m_run;
         }
-        // tell the correction warps whether (and by how much) to rescale O^T before this tile's PV; the two
-        // softmax warps agree on leaving after a timed-out wait here (named barrier 2)
-        if (!named_bar_and(2, L::kSoftThreads, ok)) break;
         const bool any = named_bar_or(2, L::kSoftThreads, resc);
-        fbuf[u * L::kRows + r] = f;
-        if (r == 0) fflag[u] = any ? 1 : 0;
-        mbar_arrive(&f_ready[u]);
+        if (half == 0) {
+          if (r == 0) fflag[u] = any ? 1 : 0;
+          mbar_arrive(&f_ready[u]);
+          l_run *= f;
+        } else {
+          const float mnew = xmax[u * L::kRows + r];
+          if (l_run > 0.f && mnew != m_run) l_run *= fast_exp2(m_run - mnew);
+          m_run = mnew;
+        }
         if (i >= 2) ok = attn_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
         uint8_t* ph = ptile + (2 * u) * L::kPBytes;
         uint8_t* pl = ph + L::kPBytes;
         const float shift = kPShift - m_run;
-#pragma unroll 1
-        for (int c = 0; c < kAttnTile / 32; ++c) {
-          uint32_t acc[32];
-          if (got) {
-            tmem_ld_32x32b_x32(lane_addr + u * 128 + 32 * c, acc);
-            tmem_ld_wait();
-          }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           uint32_t hw[8], lw[8];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
@@ -1441,8 +1437,8 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
               const int k = 32 * c + e + t;
-              a[t] = (got && k >= klo && k < khi && m_run != -INFINITY)
-                         ? fmaf(__uint_as_float(acc[e + t]), qcs, shift) : -INFINITY;
+              a[t] = (k >= klo && k < khi && m_run != -INFINITY) ? fmaf(__uint_as_float(acc[k]), qcs, shift)
+                                                                 : -INFINITY;
             }
             const __half2 ha = __floats2half2_rn(a[0], a[1]);
             uint32_t hv;
@@ -1462,21 +1458,25 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
               lw[e >> 2] |= static_cast<uint32_t>(lo) << 16;
             }
           }
-          // keys 32c .. 32c+31 of row r: 16-byte chunks 2c and 2c+1 of the swizzled [64][128 B] tile
+          // keys 64 half + 32c .. +31 of row r: two 16-byte chunks of the swizzled [64][128 B] tile
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int off = sw128_offset(r, 32 * c + 16 * h);
+            const int off = sw128_offset(r, 64 * half + 32 * c + 16 * h);
             *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[4 * h], hw[4 * h + 1], hw[4 * h + 2], hw[4 * h + 3]);
             *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[4 * h], lw[4 * h + 1], lw[4 * h + 2], lw[4 * h + 3]);
           }
         }
-        tc_fence_before();
-        mbar_arrive(&s_free[u]);
         fence_proxy_async_smem();
+        tc_fence_before();
         mbar_arrive(&p_full[u]);
-        if (cur.seg_end && live) {
-          p.part_m[slot * p.R + r] = m_run;
-          p.part_l[slot * p.R + r] = l_run;
+        if (cur.seg_end) {
+          if (half == 1) lhalf[r] = l_run;
+          named_bar_sync(2, L::kSoftThreads);
+          if (half == 0 && live) {
+            p.part_m[slot * p.R + r] = m_run;
+            p.part_l[slot * p.R + r] = l_run + lhalf[r];
+          }
+          named_bar_sync(2, L::kSoftThreads);   // lhalf read before a later segment end rewrites it
         }
       } else {
         // ---- correction warps (thread = dim): rescale O^T when asked, then write the partial at a segment end
@@ -1521,9 +1521,9 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
           tc_fence_before();
           mbar_arrive(o_free);
         }
+        if (!__all_sync(0xffffffffu, ok)) break;
       }
       if (tid == 0 && cur.seg_end && cur.tile == cur.ntiles - 1) p.meta[bg * 2 + 1] = blockIdx.x;
-      if (!soft && !__all_sync(0xffffffffu, ok)) break;
     }
   }
 
@@ -1826,7 +1826,7 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
   int ctas = 0;
   rc = R <= 8    ? attn_launch_fwd<16, 8, 2, 6, 4>(p, max_tiles, &ctas, s)
        : R <= 16 ? attn_launch_fwd<16, 16, 2, 6, 4>(p, max_tiles, &ctas, s)
-                 : attn_launch_rows<3, 2>(p, max_tiles, &ctas, s);
+                 : attn_launch_rows<5, 2>(p, max_tiles, &ctas, s);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned int>(B * Hkv * R), 1, 1);
