@@ -504,10 +504,10 @@ __device__ int attn_locate(const AttnParams& p, int* scratch, int* b0, int* g0, 
 // rows lands in [128, 256): Qhi = e4m3(q s), Qlo = e4m3(q s - Qhi), into the swizzled [NQ][128 B] tiles; returns
 // score_scale / s (the same in every thread).  Run by all softmax threads (one named barrier); each fences its
 // writes for the tensor cores.  rowmax: this Q buffer's [ROWS] scratch.  BAR: the named barrier used; tid: the
-// thread's index among the SOFT_THREADS taking part.
+// thread's index among the SOFT_THREADS taking part; dup > 0: both terms are written a second time dup bytes on.
 template <int SOFT_THREADS, int ROWS, int BAR = 1>
 __device__ float attn_prepare_q_t(const AttnParams& p, int tid, int b, int g, uint8_t* qhi, uint8_t* qlo,
-                                  float* rowmax) {
+                                  float* rowmax, int dup = 0) {
   const int items = p.R * 16;   // R rows x 16 pieces of 8 dims; a row's 16 pieces sit in one half-warp
   auto load = [&](int item, float (&x)[8]) {
     const int r = item >> 4, piece = item & 15;
@@ -557,6 +557,10 @@ __device__ float attn_prepare_q_t(const AttnParams& p, int tid, int b, int g, ui
     const int off = sw128_offset(item >> 4, (item & 15) * 8);
     *reinterpret_cast<uint2*>(qhi + off) = *reinterpret_cast<const uint2*>(hb);
     *reinterpret_cast<uint2*>(qlo + off) = *reinterpret_cast<const uint2*>(lb);
+    if (dup) {   // the same rows again, dup bytes further on
+      *reinterpret_cast<uint2*>(qhi + dup + off) = *reinterpret_cast<const uint2*>(hb);
+      *reinterpret_cast<uint2*>(qlo + dup + off) = *reinterpret_cast<const uint2*>(lb);
+    }
   }
   fence_proxy_async_smem();
   return p.score_scale / sc;
@@ -1091,48 +1095,89 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
 }
 
 // ---------------------------------------------------------------------------------------------
-// Many query rows (verify: T x group up to 64): one thread per query row.  S = Q K^T with the query rows in the
-// TMEM lanes (M = 128, rows 64..127 zero), so a row's 128 scores sit in one thread: its maximum, sum and
-// probabilities need no exchange between threads, and its P^T row (128 keys, K-major) is written as 16-byte
-// chunks.  O^T += V^T P^T as in the decode kernel (TMEM lanes = dims); four correction warps own those lanes:
-// they rescale O^T when a row's running maximum rises and write the partial output at a segment's end.
+// Many query rows (verify: T x group up to 64).  S = Q K^T with the query rows in the TMEM lanes: the A operand
+// holds the 64 rows twice (M = 128), so row r's scores sit in lanes r and r + 64, where warps of all four lane
+// quadrants can read them.  Four softmax threads share a row, 32 keys each; they meet once per tile through
+// shared memory for the row maximum, after which each computes the same running maximum, so nothing is sent
+// back.  P^T (K-major, one buffer) is written as 16-byte chunks.  O^T += V^T P^T as in the decode kernel (TMEM
+// lanes = dims); four correction warps own those lanes: they rescale O^T when a row's running maximum rises and
+// write the partial output at a segment's end.
 // ---------------------------------------------------------------------------------------------
-// Warps: 0, 1 and 4, 5 softmax (rows 0..63 = TMEM lanes 0..63; keys 0..63 / 64..127 of each tile); 2, 3, 8, 9
-// correction (TMEM lanes 64..127 / 0..63 of O^T); 6, 7 producers; 10 MMA.
+// Warps 0..7 softmax (warp w: lane quadrant w & 3, rows 32 (w & 1) + lane, keys 32 q .. 32 q + 31 of each tile
+// with q = (w >> 1 & 1) + 2 (w >> 2)); 8..11 correction (O^T lanes 32 (w & 3) + lane); 12, 13 producers; 14 MMA.
 template <int STAGES, int NPROD>
 struct AttnRowsLayout {
   static_assert(NPROD == 2, "warp map");
   static constexpr int kRows = 64;                    // query rows handled (R <= 64)
-  static constexpr int kSoftThreads = 128;            // two threads per row, 64 keys each
+  static constexpr int kSoftThreads = 256;            // four threads per row, 32 keys each
   static constexpr int kCorrThreads = 128;
-  static constexpr int kThreads = 32 * 11;
+  static constexpr int kCorrWarp0 = 8;
+  static constexpr int kProducerWarp = 12;
+  static constexpr int kMmaWarp = 14;
+  static constexpr int kThreads = 32 * 15;
+  // the bound given to the compiler: four of the 15 warps share a sub-partition of the SM, whose 16K registers
+  // allow 128 per thread (65536 / 512)
+  static constexpr int kLaunchBound = 512;
   static constexpr int kPf = STAGES - 2;
   static constexpr int kKvBytes = kAttnTile * kAttnD;
   static constexpr int kStageBytes = 2 * kKvBytes;
-  // Q: [hi][lo][zeros], 64 rows x 128 B each.  The QK MMA reads 128 rows from hi (its rows 64..127 are lo) and
-  // from lo (rows 64..127 zero): only S rows 0..63 (TMEM lanes 0..63) are read, so the upper rows need no zeros
-  // of their own.  One buffer: a segment's Q is written after the last QK of the previous segment completed.
-  static constexpr int kQBytes = kRows * kAttnD;      // one e4m3 term of Q: 64 rows x 128 B
+  static constexpr int kQBytes = kRows * kAttnD;      // one copy of one e4m3 term of Q: 64 rows x 128 B
   static constexpr int kPBytes = kRows * kAttnTile;   // one e4m3 term of P^T: 64 rows x 128 keys
-  static constexpr int kQOffset = STAGES * kStageBytes;          // Q hi, lo, zeros
-  static constexpr int kPOffset = kQOffset + 3 * kQBytes;        // P^T[buffer][hi, lo]
-  static constexpr int kFOffset = kPOffset + 4 * kPBytes;        // rescale factors [2][64] + flags [2]
-  static constexpr int kXOffset = kFOffset + 2 * kRows * 4 + 16;        // half-tile maxima [2][64], row sums [64]
-  static constexpr int kRowmaxOffset = kXOffset + 3 * kRows * 4;        // |q| maxima [2][64]
-  static constexpr int kBtOffset = kRowmaxOffset + 2 * kRows * 4;        // block-table rings [NPROD][kPf][128]
+  static constexpr int kQOffset = STAGES * kStageBytes;          // Q hi, hi again, lo, lo again
+  static constexpr int kPOffset = kQOffset + 4 * kQBytes;        // P^T hi, lo
+  static constexpr int kFOffset = kPOffset + 2 * kPBytes;        // rescale factors [2][64] + flags [2]
+  static constexpr int kXOffset = kFOffset + 2 * kRows * 4 + 16;         // quarter-tile maxima [2][4][64]
+  static constexpr int kLOffset = kXOffset + 2 * 4 * kRows * 4;          // quarter row sums [4][64]
+  static constexpr int kRowmaxOffset = kLOffset + 4 * kRows * 4;         // |q| maxima [64]
+  static constexpr int kBtOffset = kRowmaxOffset + kRows * 4;             // block-table rings [NPROD][kPf][128]
   static constexpr int kBarOffset = kBtOffset + NPROD * kPf * kAttnTile * 4;
-  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full[2] (one used), f_ready[2], o_free,
-  // drain
-  static constexpr int kNumBars = 2 * STAGES + 14;
+  // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], pv_done[2], q_full, f_ready[2], o_free, drain
+  static constexpr int kNumBars = 2 * STAGES + 13;
   static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
   static constexpr int kSmemBytes = kMiscOffset + 48 * 4 + 1024;
-  static constexpr uint32_t kTmemCols = 512;          // S^T... S[2] at [0, 256), O^T at [256, 320)
+  static constexpr uint32_t kTmemCols = 512;          // S[2] at [0, 256), O^T at [256, 320)
   static constexpr int kOCol = 256;
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
+// 32 probabilities p = 2^(s qcs + shift) of one row (keys outside [klo, khi) give 0 when MASK) as two e4m3 terms,
+// hi = e4m3(p) and lo = e4m3(p - hi), four keys per 32-bit word; returns the sum of the p.  The exponent is taken
+// in f16 pairs (shift keeps p <= 2^8); the residual is formed in f16 from hi widened by a shift of its bits.
+template <bool MASK>
+__device__ __forceinline__ float attn_row_p32(const uint32_t (&acc)[32], float qcs, float shift, int klo, int khi,
+                                              uint32_t (&hw)[8], uint32_t (&lw)[8]) {
+  float sum = 0.f;
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float a[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float x = fmaf(__uint_as_float(acc[e + t]), qcs, shift);
+      a[t] = (!MASK || (e + t >= klo && e + t < khi)) ? x : -INFINITY;
+    }
+    const __half2 ha = __floats2half2_rn(a[0], a[1]);
+    uint32_t hv;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(hv) : "r"(*reinterpret_cast<const uint32_t*>(&ha)));
+    const __half2 h2 = *reinterpret_cast<const __half2*>(&hv);
+    const float2 pf2 = __half22float2(h2);
+    sum += pf2.x + pf2.y;
+    const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hb_bits = __byte_perm(static_cast<uint32_t>(hi), 0u, 0x4140) << 7;
+    const __half2 res = __hfma2(*reinterpret_cast<const __half2*>(&hb_bits), __float2half2_rn(-256.f), h2);
+    const __nv_fp8x2_storage_t lo = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(res), __NV_SATFINITE, __NV_E4M3);
+    if ((e & 2) == 0) {
+      hw[e >> 2] = static_cast<uint32_t>(hi);
+      lw[e >> 2] = static_cast<uint32_t>(lo);
+    } else {
+      hw[e >> 2] |= static_cast<uint32_t>(hi) << 16;
+      lw[e >> 2] |= static_cast<uint32_t>(lo) << 16;
+    }
+  }
+  return sum;
+}
+
 template <int STAGES, int NPROD>
-__global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) attn_rows_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kLaunchBound, 1) attn_rows_kernel(const AttnParams p) {
   using L = AttnRowsLayout<STAGES, NPROD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1143,7 +1188,7 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_full = pv_done + 2;
-  uint64_t* f_ready = q_full + 2;
+  uint64_t* f_ready = q_full + 1;
   uint64_t* o_free = f_ready + 2;
   uint64_t* drain = o_free + 1;
   int* misc = reinterpret_cast<int*>(smem + L::kMiscOffset);
@@ -1152,9 +1197,9 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   int* scratch = misc + 8;
   float* fbuf = reinterpret_cast<float*>(smem + L::kFOffset);                       // [2][64]
   int* fflag = reinterpret_cast<int*>(smem + L::kFOffset + 2 * L::kRows * 4);       // [2]
+  float* xq = reinterpret_cast<float*>(smem + L::kXOffset);                         // [2][4][64]
+  float* lq = reinterpret_cast<float*>(smem + L::kLOffset);                         // [4][64]
   float* rowmax = reinterpret_cast<float*>(smem + L::kRowmaxOffset);
-  float* xmax = reinterpret_cast<float*>(smem + L::kXOffset);   // [2][64]: half 1's tile maxima by tile parity
-  float* lhalf = xmax + 2 * L::kRows;                            // [64]: half 1's row sums at a segment end
   int* bt_ring = reinterpret_cast<int*>(smem + L::kBtOffset);
   uint8_t* qtile = smem + L::kQOffset;
   uint8_t* ptile = smem + L::kPOffset;
@@ -1162,15 +1207,15 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
   const int tid = threadIdx.x;
-  constexpr int kProducerWarp = 6;
-  constexpr int kMmaWarp = 10;
+  constexpr int kProducerWarp = L::kProducerWarp;
+  constexpr int kMmaWarp = L::kMmaWarp;
 
   int b0 = 0, g0 = 0, t0 = 0;
   const int count = attn_locate(p, scratch, &b0, &g0, &t0);
   if (count == 0) return;
 
-  for (int i = tid; i < (3 * L::kQBytes + 4 * L::kPBytes) / 16; i += L::kThreads)
-    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);   // Q rows R..63 and the zero rows stay zero
+  for (int i = tid; i < (4 * L::kQBytes + 2 * L::kPBytes) / 16; i += L::kThreads)
+    reinterpret_cast<uint4*>(qtile)[i] = make_uint4(0u, 0u, 0u, 0u);   // Q rows R..63 stay zero
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], NPROD);
@@ -1181,9 +1226,9 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
       mbar_init(&s_free[u], L::kSoftThreads);
       mbar_init(&p_full[u], L::kSoftThreads + L::kCorrThreads);
       mbar_init(&pv_done[u], 1);
-      mbar_init(&q_full[u], L::kSoftThreads);
       mbar_init(&f_ready[u], L::kRows);
     }
+    mbar_init(q_full, L::kSoftThreads);
     mbar_init(o_free, L::kCorrThreads);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -1273,9 +1318,13 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, 128, false, false);   // S[rows x keys]
+      constexpr uint32_t kIdQK = idesc_e4m3_f32(128, 128, false, false);   // S[rows (twice) x keys]
       constexpr uint32_t kIdPV = idesc_e4m3_f32(128, 64, true, false);     // O^T[dims x rows]
       const uint32_t o_tmem = tmem_base + L::kOCol;
+      const uint32_t qh_addr = smem_u32(qtile);
+      const uint32_t ql_addr = qh_addr + 2 * L::kQBytes;
+      const uint32_t ph_addr = smem_u32(ptile);
+      const uint32_t pl_addr = ph_addr + L::kPBytes;
       AttnCursor cur;
       cur.init(p, b0, g0, t0, count);
       bool ok = true, issued = false;
@@ -1287,8 +1336,6 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
         if (start && seg > 0 && !attn_wait(o_free, (seg - 1) & 1, abort_flag, kSiteAttnMmaOFree)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + sj * L::kStageBytes + L::kKvBytes);
-        const uint32_t ph_addr = smem_u32(ptile + (2 * uj) * L::kPBytes);
-        const uint32_t pl_addr = ph_addr + L::kPBytes;
 #pragma unroll
         for (int ks = 0; ks < kAttnTile / 32; ++ks)
           mma_e4m3(o_tmem, sdesc_sw128_mnmajor(v_addr + ks * 4096), sdesc_sw128_kmajor(ph_addr + ks * 32), kIdPV,
@@ -1304,12 +1351,10 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
       for (int i = 0; ok && cur.remaining > 0; ++i, cur.next(p)) {
         const int s = i % STAGES, u = i & 1;
         if (!attn_wait(&kv_full[s], (i / STAGES) & 1, abort_flag, kSiteAttnMmaFull)) break;
-        if (cur.seg_start && !attn_wait(&q_full[0], cur.seg & 1, abort_flag, kSiteAttnMmaQ)) break;
+        if (cur.seg_start && !attn_wait(q_full, cur.seg & 1, abort_flag, kSiteAttnMmaQ)) break;
         if (!attn_wait(&s_free[u], ((i >> 1) & 1) ^ 1u, abort_flag, kSiteAttnMmaSFree)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + s * L::kStageBytes);
-        const uint32_t qh_addr = smem_u32(qtile);
-        const uint32_t ql_addr = qh_addr + L::kQBytes;
         const uint32_t s_tmem = tmem_base + u * 128;
 #pragma unroll
         for (int ks = 0; ks < kAttnD / 32; ++ks)
@@ -1334,196 +1379,168 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kThreads, 1) at
         mbar_wait_drain(drain, 0, kSiteAttnDrainMma);
       }
     }
-  } else {
-    // ------------------------------------------------------------------ softmax (rows) and correction (dims)
-    const bool soft = warp == 0 || warp == 1 || warp == 4 || warp == 5;
-    const int half = warp >> 2;                          // softmax: keys [64 half, 64 half + 64) of each tile
+  } else if (warp < L::kCorrWarp0) {
+    // ------------------------------------------------------------------ softmax: thread = (row, quarter tile)
     const int quad = warp & 3;
-    const int r = quad * 32 + static_cast<int>(lane);    // softmax: this thread's query row (0..63)
-    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const int r = (quad & 1) * 32 + static_cast<int>(lane);      // query row
+    const int qt = (quad >> 1) + 2 * (warp >> 2);               // keys 32 qt .. 32 qt + 31 of each tile
+    const uint32_t s_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + 32 * qt;
+    const int trow = r / p.group;   // token of the row
+    const bool live = r < p.R;
     constexpr float kTau = 4.f;
     constexpr float kPShift = 4.f;
-
-    // the queries are prepared by the softmax warps alone (named barrier 2): the correction warps share no
-    // barrier with them and may leave on their own after a timed-out wait
-    float qcs = 0.f;   // the segment's score scale
-    const int stid = (warp >> 2) * 64 + quad * 32 + static_cast<int>(lane);   // 0..127 over the softmax warps
-
+    float qcs = 0.f;                        // the segment's score scale
+    float m_run = -INFINITY, l_run = 0.f;   // the row's running maximum (log2) and this quarter's sum
+    bool ok = true;
     AttnCursor cur;
     cur.init(p, b0, g0, t0, count);
-    float m_run = -INFINITY, l_run = 0.f;   // softmax: the row's running maximum (log2) and this half's sum
-    const int trow = r / p.group;            // token of the row
-    bool ok = true;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int u = i & 1;
       const int bg = cur.b * p.Hkv + cur.g;
       if (cur.seg_start) {
-        if (soft) {
-          // the previous segment's last S was read by this thread, so its QK MMAs no longer read Q
-          qcs = attn_prepare_q_t<L::kSoftThreads, L::kRows, 2>(p, stid, cur.b, cur.g, qtile, qtile + L::kQBytes,
-                                                              rowmax);
-          mbar_arrive(&q_full[0]);
-        }
+        // the previous segment's last S was read by these threads, so its QK MMAs no longer read Q
+        qcs = attn_prepare_q_t<L::kSoftThreads, L::kRows, 2>(p, tid, cur.b, cur.g, qtile, qtile + 2 * L::kQBytes,
+                                                            rowmax, L::kQBytes);
+        mbar_arrive(q_full);
         m_run = -INFINITY;
         l_run = 0.f;
         if (tid == 0 && cur.tile == 0) p.meta[bg * 2] = blockIdx.x;
       }
-      const long long slot = static_cast<long long>(blockIdx.x) + bg;
-      if (soft) {
-        // ---- this thread's 64 scores of its row, read once
-        const bool got = __all_sync(0xffffffffu, attn_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
-        ok = ok && got;
-        const int k0 = cur.lo + cur.tile * kAttnTile + 64 * half;   // position of this thread's first key
-        const int qpos = cur.L - p.T + trow;
-        const bool live = r < p.R;
-        // keys [klo, khi) of this thread's 64 are the row's (causal and window limits)
-        int khi = qpos - k0 + 1;
-        khi = khi < 0 ? 0 : (khi > 64 ? 64 : khi);
-        int klo = p.window > 0 ? qpos - p.window + 1 - k0 : 0;
-        klo = klo < 0 ? 0 : (klo > 64 ? 64 : klo);
-        if (!live || !got) khi = 0;
-        uint32_t acc[64];
-        if (got) {
-          tc_fence_after();
-          tmem_ld_32x32b_x32(lane_addr + u * 128 + 64 * half, *reinterpret_cast<uint32_t(*)[32]>(&acc[0]));
-          tmem_ld_32x32b_x32(lane_addr + u * 128 + 64 * half + 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[32]));
-          tmem_ld_wait();
-        }
-        tc_fence_before();
-        mbar_arrive(&s_free[u]);
-        float hmax = -INFINITY;
-#pragma unroll
-        for (int e = 0; e < 64; ++e)
-          if (e >= klo && e < khi) hmax = fmaxf(hmax, __uint_as_float(acc[e]));
-        hmax = hmax == -INFINITY ? hmax : hmax * qcs;
-        // the two halves of a row meet through shared memory: half 1's maximum before the first barrier, the row's
-        // running maximum (owned by half 0) before the second
-        if (half == 1) xmax[u * L::kRows + r] = hmax;
-        if (named_bar_or(2, L::kSoftThreads, !ok)) break;
-        float f = 1.f;
-        bool resc = false;
-        if (half == 0) {
-          const float tmax = fmaxf(hmax, xmax[u * L::kRows + r]);
-          if (m_run == -INFINITY) {
-            m_run = tmax;
-          } else if (tmax > m_run + kTau) {
-            f = fast_exp2(m_run - tmax);
-            m_run = tmax;
-            resc = true;
-          }
-          fbuf[u * L::kRows + r] = f;
-          xmax[u * L::kRows + r] = m_run;
-        }
-        const bool any = named_bar_or(2, L::kSoftThreads, resc);
-        if (half == 0) {
-          if (r == 0) fflag[u] = any ? 1 : 0;
-          mbar_arrive(&f_ready[u]);
-          l_run *= f;
-        } else {
-          const float mnew = xmax[u * L::kRows + r];
-          if (l_run > 0.f && mnew != m_run) l_run *= fast_exp2(m_run - mnew);
-          m_run = mnew;
-        }
-        if (i >= 2) ok = attn_wait(&pv_done[u], ((i - 2) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
-        uint8_t* ph = ptile + (2 * u) * L::kPBytes;
-        uint8_t* pl = ph + L::kPBytes;
-        const float shift = kPShift - m_run;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t hw[8], lw[8];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float a[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int k = 32 * c + e + t;
-              a[t] = (k >= klo && k < khi && m_run != -INFINITY) ? fmaf(__uint_as_float(acc[k]), qcs, shift)
-                                                                 : -INFINITY;
-            }
-            const __half2 ha = __floats2half2_rn(a[0], a[1]);
-            uint32_t hv;
-            asm("ex2.approx.f16x2 %0, %1;" : "=r"(hv) : "r"(*reinterpret_cast<const uint32_t*>(&ha)));
-            const __half2 h2 = *reinterpret_cast<const __half2*>(&hv);
-            const float2 pf2 = __half22float2(h2);
-            l_run += pf2.x + pf2.y;
-            const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
-            const uint32_t hb_bits = __byte_perm(static_cast<uint32_t>(hi), 0u, 0x4140) << 7;
-            const __half2 res = __hfma2(*reinterpret_cast<const __half2*>(&hb_bits), __float2half2_rn(-256.f), h2);
-            const __nv_fp8x2_storage_t lo = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(res), __NV_SATFINITE, __NV_E4M3);
-            if ((e & 2) == 0) {
-              hw[e >> 2] = static_cast<uint32_t>(hi);
-              lw[e >> 2] = static_cast<uint32_t>(lo);
-            } else {
-              hw[e >> 2] |= static_cast<uint32_t>(hi) << 16;
-              lw[e >> 2] |= static_cast<uint32_t>(lo) << 16;
-            }
-          }
-          // keys 64 half + 32c .. +31 of row r: two 16-byte chunks of the swizzled [64][128 B] tile
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int off = sw128_offset(r, 64 * half + 32 * c + 16 * h);
-            *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[4 * h], hw[4 * h + 1], hw[4 * h + 2], hw[4 * h + 3]);
-            *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[4 * h], lw[4 * h + 1], lw[4 * h + 2], lw[4 * h + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(&p_full[u]);
-        if (cur.seg_end) {
-          if (half == 1) lhalf[r] = l_run;
-          named_bar_sync(2, L::kSoftThreads);
-          if (half == 0 && live) {
-            p.part_m[slot * p.R + r] = m_run;
-            p.part_l[slot * p.R + r] = l_run + lhalf[r];
-          }
-          named_bar_sync(2, L::kSoftThreads);   // lhalf read before a later segment end rewrites it
-        }
-      } else {
-        // ---- correction warps (thread = dim): rescale O^T when asked, then write the partial at a segment end
-        const int dim = quad * 32 + static_cast<int>(lane);
-        ok = __all_sync(0xffffffffu, attn_wait(&f_ready[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv)) && ok;
-        if (ok && fflag[u]) {
-          const int j1 = i - 1;
-          const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
-                                                            kSiteAttnSoftPv));
-          ok = ok && pv;
-          if (pv) {
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-              uint32_t o[32];
-              tmem_ld_32x32b_x32(lane_addr + L::kOCol + 32 * c, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fbuf[u * L::kRows + 32 * c + e]);
-              tmem_st_cols<32>(lane_addr + L::kOCol + 32 * c, o);
-            }
-            tmem_st_wait();
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&p_full[u]);
-        if (cur.seg_end) {
-          const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
-          ok = ok && pv;
-          if (pv) {
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-              uint32_t o[32];
-              tmem_ld_32x32b_x32(lane_addr + L::kOCol + 32 * c, o);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (32 * c + e < p.R) p.part_o[(slot * p.R + 32 * c + e) * kAttnD + dim] = __uint_as_float(o[e]);
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(o_free);
-        }
-        if (!__all_sync(0xffffffffu, ok)) break;
+      const bool got = __all_sync(0xffffffffu, attn_wait(&s_full[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftS));
+      ok = ok && got;
+      const int k0 = cur.lo + cur.tile * kAttnTile + 32 * qt;   // position of this thread's first key
+      const int qpos = cur.L - p.T + trow;
+      // keys [klo, khi) of this thread's 32 are the row's (causal and window limits)
+      int khi = qpos - k0 + 1;
+      khi = khi < 0 ? 0 : (khi > 32 ? 32 : khi);
+      int klo = p.window > 0 ? qpos - p.window + 1 - k0 : 0;
+      klo = klo < 0 ? 0 : (klo > 32 ? 32 : klo);
+      if (!live || !got) khi = 0;
+      const bool full = klo == 0 && khi == 32;
+      uint32_t acc[32];
+      if (got) {
+        tc_fence_after();
+        tmem_ld_32x32b_x32(s_addr + u * 128, acc);
+        tmem_ld_wait();
       }
-      if (tid == 0 && cur.seg_end && cur.tile == cur.ntiles - 1) p.meta[bg * 2 + 1] = blockIdx.x;
+      tc_fence_before();
+      mbar_arrive(&s_free[u]);
+      float qmax = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) qmax = fmaxf(qmax, __uint_as_float(acc[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (e >= klo && e < khi) qmax = fmaxf(qmax, __uint_as_float(acc[e]));
+      }
+      qmax = qmax == -INFINITY ? qmax : qmax * qcs;
+      xq[(u * 4 + qt) * L::kRows + r] = qmax;
+      if (named_bar_or(2, L::kSoftThreads, !ok)) break;
+      // the four quarters' maxima: every thread of the row takes the same decision
+      const float* xr = xq + u * 4 * L::kRows + r;
+      const float tmax = fmaxf(fmaxf(xr[0], xr[L::kRows]), fmaxf(xr[2 * L::kRows], xr[3 * L::kRows]));
+      float f = 1.f;
+      bool resc = false;
+      if (m_run == -INFINITY) {
+        m_run = tmax;
+      } else if (tmax > m_run + kTau) {
+        f = fast_exp2(m_run - tmax);
+        m_run = tmax;
+        resc = true;
+      }
+      l_run *= f;
+      if (qt == 0) {   // warps 0 and 1
+        fbuf[u * L::kRows + r] = f;
+        const bool any = named_bar_or(3, 64, resc);
+        if (r == 0) fflag[u] = any ? 1 : 0;
+        mbar_arrive(&f_ready[u]);
+      }
+      // the tensor cores have read the previous tile's P^T before this one overwrites the buffer
+      if (i >= 1) ok = attn_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1, abort_flag, kSiteAttnSoftPv) && ok;
+      uint32_t hw[8], lw[8];
+      const float shift = kPShift - m_run;
+      if (full) {
+        l_run += attn_row_p32<false>(acc, qcs, shift, 0, 32, hw, lw);
+      } else {
+        l_run += attn_row_p32<true>(acc, qcs, shift, klo, m_run == -INFINITY ? 0 : khi, hw, lw);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int off = sw128_offset(r, 32 * qt + 16 * h);
+        *reinterpret_cast<uint4*>(ptile + off) = make_uint4(hw[4 * h], hw[4 * h + 1], hw[4 * h + 2], hw[4 * h + 3]);
+        *reinterpret_cast<uint4*>(ptile + L::kPBytes + off) =
+            make_uint4(lw[4 * h], lw[4 * h + 1], lw[4 * h + 2], lw[4 * h + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[u]);
+      if (cur.seg_end) {
+        lq[qt * L::kRows + r] = l_run;
+        named_bar_sync(2, L::kSoftThreads);
+        if (qt == 0 && live) {
+          const long long slot = static_cast<long long>(blockIdx.x) + bg;
+          p.part_m[slot * p.R + r] = m_run;
+          p.part_l[slot * p.R + r] = (lq[r] + lq[L::kRows + r]) + (lq[2 * L::kRows + r] + lq[3 * L::kRows + r]);
+        }
+        named_bar_sync(2, L::kSoftThreads);   // lq read before a later segment end rewrites it
+        if (tid == 0 && cur.tile == cur.ntiles - 1) p.meta[bg * 2 + 1] = blockIdx.x;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ correction warps (thread = dim)
+    const int quad = warp & 3;
+    const int dim = quad * 32 + static_cast<int>(lane);
+    const uint32_t o_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + L::kOCol;
+    bool ok = true;
+    AttnCursor cur;
+    cur.init(p, b0, g0, t0, count);
+    for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
+      const int u = i & 1;
+      const int bg = cur.b * p.Hkv + cur.g;
+      ok = __all_sync(0xffffffffu, attn_wait(&f_ready[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv)) && ok;
+      if (ok && fflag[u] && i >= 1) {
+        // O^T holds the tiles before this one once PV(i - 1) completed; rescale its columns (rows)
+        const int j1 = i - 1;
+        const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[j1 & 1], (j1 >> 1) & 1, abort_flag,
+                                                          kSiteAttnSoftPv));
+        ok = ok && pv;
+        if (pv) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_addr + 32 * c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fbuf[u * L::kRows + 32 * c + e]);
+            tmem_st_cols<32>(o_addr + 32 * c, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&p_full[u]);
+      if (cur.seg_end) {
+        const bool pv = __all_sync(0xffffffffu, attn_wait(&pv_done[u], (i >> 1) & 1, abort_flag, kSiteAttnSoftPv));
+        ok = ok && pv;
+        if (pv) {
+          const long long slot = static_cast<long long>(blockIdx.x) + bg;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_addr + 32 * c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (32 * c + e < p.R) p.part_o[(slot * p.R + 32 * c + e) * kAttnD + dim] = __uint_as_float(o[e]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(o_free);
+      }
+      if (!__all_sync(0xffffffffu, ok)) break;
     }
   }
 
