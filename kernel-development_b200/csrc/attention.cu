@@ -675,7 +675,9 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
     cp_async_commit();
     cp_async_wait<0>();
     __syncwarp();
-    pdl_wait();   // the new tokens' rows are written by the append kernel launched just before
+    // the new tokens' rows are written by the append kernel launched just before: wait for it (once) before the
+    // first tile that holds one of the last T positions, so that it runs under the earlier tiles' copies
+    bool appended = false;
     int issued = 0;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int s = i % STAGES;
@@ -687,6 +689,10 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
       }
       const bool ok = attn_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
       if (!__all_sync(0xffffffffu, ok)) break;
+      if (!appended && cur.lo + cur.tile * kAttnTile + kAttnTile > cur.L - p.T) {
+        pdl_wait();
+        appended = true;
+      }
       const int* rt = bt_ring + (i % kPf) * kAttnTile;
       const int nvalid = cur.L - (cur.lo + cur.tile * kAttnTile);   // keys of this tile inside the sequence
       const uint8_t* kbase = p.k_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
@@ -713,6 +719,7 @@ __global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kT
       cp_async_commit();
       issued = i + 1;
     }
+    if (!appended) pdl_wait();   // this grid ends after the append grid in every case
     cp_async_wait<0>();
     fence_proxy_async_smem();
     __syncwarp();
@@ -1272,7 +1279,9 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kLaunchBound, 1
     cp_async_commit();
     cp_async_wait<0>();
     __syncwarp();
-    pdl_wait();   // the new tokens' rows are written by the append kernel launched just before
+    // the new tokens' rows are written by the append kernel launched just before: wait for it (once) before the
+    // first tile that holds one of the last T positions, so that it runs under the earlier tiles' copies
+    bool appended = false;
     int issued = 0;
     for (int i = 0; cur.remaining > 0; ++i, cur.next(p)) {
       const int s = i % STAGES;
@@ -1284,6 +1293,10 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kLaunchBound, 1
       }
       const bool ok = attn_wait(&kv_empty[s], ((i / STAGES) & 1) ^ 1u, abort_flag, kSiteAttnProdEmpty);
       if (!__all_sync(0xffffffffu, ok)) break;
+      if (!appended && cur.lo + cur.tile * kAttnTile + kAttnTile > cur.L - p.T) {
+        pdl_wait();
+        appended = true;
+      }
       const int* rt = bt_ring + (i % kPf) * kAttnTile;
       const int nvalid = cur.L - (cur.lo + cur.tile * kAttnTile);
       const uint8_t* kbase = p.k_cache + static_cast<long long>(cur.g) * kAttnD + chunk * 16;
@@ -1310,6 +1323,7 @@ __global__ void __launch_bounds__(AttnRowsLayout<STAGES, NPROD>::kLaunchBound, 1
       cp_async_commit();
       issued = i + 1;
     }
+    if (!appended) pdl_wait();   // this grid ends after the append grid in every case
     cp_async_wait<0>();
     fence_proxy_async_smem();
     __syncwarp();
@@ -1599,12 +1613,12 @@ __global__ void __launch_bounds__(128) attn_append_kernel(const AttnAppendParams
 }
 
 // ---------------------------------------------------------------------------------------------
-// merge: one CTA (16 warps) per (sequence, KV head, query row).  Pass 1: the largest partial maximum M; pass 2:
-// warp w sums the partials of CTAs c0 + w, + 16, ... weighted by 2^(m - M) (independent loads, no running
-// rescale), then the 16 warps' sums are added through shared memory.
+// merge: one CTA (W warps) per (sequence, KV head, query row).  Pass 1: the largest partial maximum M; pass 2:
+// warp w sums the partials of CTAs c0 + w, + W, ... weighted by 2^(m - M) (independent loads, no running
+// rescale), then the W warps' sums are added through shared memory.  W = 16 when a row has many partials (long
+// sequences over many CTAs); W = 4 when it has few, so that every row's CTA is resident in one wave.
 // ---------------------------------------------------------------------------------------------
-constexpr int kMergeWarps = 16;
-
+template <int kMergeWarps>
 __global__ void __launch_bounds__(kMergeWarps * 32)
     attn_merge_kernel(const AttnParams p, int ctas, float kv_scale, __nv_bfloat16* __restrict__ out) {
   __shared__ float red[kMergeWarps], sm_l[kMergeWarps];
@@ -1845,16 +1859,19 @@ int attn_decode_fp8(const void* q, const void* k_new, const void* v_new, void* k
        : R <= 16 ? attn_launch_fwd<16, 16, 2, 6, 4>(p, max_tiles, &ctas, s)
                  : attn_launch_rows<5, 2>(p, max_tiles, &ctas, s);
   if (rc) return rc;
+  // partials per (sequence, KV head) on average: ctas / (B Hkv) + 1 (a CTA's range may start inside a segment)
+  const bool few = ctas <= 7 * B * Hkv;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned int>(B * Hkv * R), 1, 1);
-  cfg.blockDim = dim3(kMergeWarps * 32, 1, 1);
+  cfg.blockDim = dim3(few ? 4 * 32 : 16 * 32, 1, 1);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  rc = cuda_status(cudaLaunchKernelEx(&cfg, attn_merge_kernel, static_cast<const AttnParams>(p), ctas, kv_scale,
+  rc = cuda_status(cudaLaunchKernelEx(&cfg, few ? attn_merge_kernel<4> : attn_merge_kernel<16>,
+                                      static_cast<const AttnParams>(p), ctas, kv_scale,
                                       static_cast<__nv_bfloat16*>(out)));
   if (rc) return rc;
   return cuda_status(cudaGetLastError());
