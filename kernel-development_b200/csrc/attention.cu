@@ -144,6 +144,9 @@ template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
 struct AttnLayout {
   static constexpr int kSoftThreads = 128 * SPLIT;
   static constexpr int kThreads = kSoftThreads + 32 * (NPROD + 1);   // + producer warps + MMA warp
+  // the bound given to the compiler: the threads rounded up to whole groups of four warps, so that the registers of
+  // the warps on one SM sub-partition (at most one warp in four) fit its 16K (65536 / kLaunchBound per thread)
+  static constexpr int kLaunchBound = (kThreads + 127) / 128 * 128;
   static constexpr int kRpt = ROWS / SPLIT;            // query rows per softmax thread
   static constexpr int kPf = STAGES - 2;               // tiles of copies in flight
   static constexpr int kKvBytes = kAttnTile * kAttnD;  // 16 KB: 128 rows of 128 B
@@ -172,7 +175,8 @@ struct AttnLayout {
   static_assert(kCols <= 256, "tensor memory columns");
   static_assert(ROWS % SPLIT == 0 && ROWS <= NQ && (kRpt == 2 || kRpt == 4 || kRpt == 8 || kRpt == 16 || kRpt == 32),
                 "rows per thread");
-  static_assert(kThreads <= 1024 && kPf >= 1 && 32 % NPROD == 0, "launch shape");
+  static_assert(kThreads <= 1024 && kPf >= 1 && NPROD >= 1 && NPROD <= 8, "launch shape");
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 // kind::f8f6f4, e4m3 x e4m3 -> f32, M = m, N = n; A K-major (scores) or MN-major (values: V^T), B K-major.
@@ -571,7 +575,7 @@ __device__ float attn_prepare_q(const AttnParams& p, int b, int g, uint8_t* qhi,
 }
 
 template <int NQ, int ROWS, int SPLIT, int STAGES, int NPROD>
-__global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kThreads, 1)
+__global__ void __launch_bounds__(AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>::kLaunchBound, 1)
     attn_fwd_kernel(const AttnParams p) {
   using L = AttnLayout<NQ, ROWS, SPLIT, STAGES, NPROD>;
   constexpr int RPT = L::kRpt;
