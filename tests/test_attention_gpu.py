@@ -96,6 +96,19 @@ def test_attention_edge_lengths(case, window):
     _check_cache(data, g)
 
 
+@pytest.mark.parametrize("q_len", [2, 3, 5, 7])
+@pytest.mark.parametrize("layer, heads, window", [("full", "tp8", None), ("sliding", "dp", 300)])
+def test_attention_other_query_lengths(q_len, layer, heads, window):
+    """Row counts between the problem's decode (8) and verify (64) shapes: 16 rows take the decode kernel with
+    16 query columns, 24 / 40 / 56 rows the rows kernel with part of its 64-row block empty."""
+    case = dict(batch=5, ctx=1500, heads=heads, layer=layer, q_len=q_len, spread="mixed")
+    data, g, out = _run(case, seed=20 + q_len, window=window)
+    ok, msg = OA.check(data, out.cpu(), window=window)
+    assert ok, f"q_len {q_len}: {msg}"
+    _check_cache(data, g)
+    assert _status()[0] == 0
+
+
 def test_attention_large_scores_rescale_path():
     """Keys late in each sequence score far above the earlier ones, so the running maximum rises by more
     than the lazy-rescale threshold mid-sequence and O is rescaled in tensor memory."""
