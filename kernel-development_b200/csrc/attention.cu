@@ -1153,11 +1153,13 @@ struct AttnRowsLayout {
 
 // 32 probabilities p = 2^(s qcs + shift) of one row (keys outside [klo, khi) give 0 when MASK) as two e4m3 terms,
 // hi = e4m3(p) and lo = e4m3(p - hi), four keys per 32-bit word; returns the sum of the p.  The exponent is taken
-// in f16 pairs (shift keeps p <= 2^8); the residual is formed in f16 from hi widened by a shift of its bits.
+// in f16 pairs (shift keeps p <= 2^8); the residual is formed in f16 from hi widened by a shift of its bits.  The
+// sum adds f16 pairs within groups of 8 keys (three f16 roundings at most) and the groups in f32.
 template <bool MASK>
 __device__ __forceinline__ float attn_row_p32(const uint32_t (&acc)[32], float qcs, float shift, int klo, int khi,
                                               uint32_t (&hw)[8], uint32_t (&lw)[8]) {
   float sum = 0.f;
+  __half2 grp = __float2half2_rn(0.f);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
     float a[2];
@@ -1170,8 +1172,12 @@ __device__ __forceinline__ float attn_row_p32(const uint32_t (&acc)[32], float q
     uint32_t hv;
     asm("ex2.approx.f16x2 %0, %1;" : "=r"(hv) : "r"(*reinterpret_cast<const uint32_t*>(&ha)));
     const __half2 h2 = *reinterpret_cast<const __half2*>(&hv);
-    const float2 pf2 = __half22float2(h2);
-    sum += pf2.x + pf2.y;
+    grp = __hadd2(grp, h2);
+    if ((e & 6) == 6) {   // every 8 keys: the group's f16 pair sums (at most 4 x 2^8 each) into the f32 total
+      const float2 g2 = __half22float2(grp);
+      sum += g2.x + g2.y;
+      grp = __float2half2_rn(0.f);
+    }
     const __nv_fp8x2_storage_t hi = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(h2), __NV_SATFINITE, __NV_E4M3);
     const uint32_t hb_bits = __byte_perm(static_cast<uint32_t>(hi), 0u, 0x4140) << 7;
     const __half2 res = __hfma2(*reinterpret_cast<const __half2*>(&hb_bits), __float2half2_rn(-256.f), h2);
